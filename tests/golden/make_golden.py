@@ -1,0 +1,322 @@
+"""Regenerate the golden fixtures in tests/golden/ by running the reference itself.
+
+Run in a container where the reference checkout is mounted (default
+``/root/reference``; override with ``CARDGYM_REFERENCE``)::
+
+    python tests/golden/make_golden.py
+
+Every fixture stores the inputs, the seed of the synthetic weights
+(``card_playing_gym_b200.config.synthetic_plump_actor_state``, regenerated
+bit-for-bit on any machine from the seed) and the outputs the reference's own
+code computed from them. Nothing here is needed at run time on the GPU box: the
+.npz files are committed.
+
+Fixtures:
+  plump_streams.npz   real plump observer streams from the reference game engine
+  trunk_<name>.npz    full forward, prefill + ragged cached steps, heads (fp32),
+                      and the reference's own bf16-autocast/fp16-KV ragged outputs
+  sampling.npz        masked_probabilities / sample_rows
+  ppo.npz             ppo_terms terms and the autograd gradient of the head objective
+  gae.npz             gae_advantages per game, acting-seat advantages
+  value_loss.npz      PPOTrainer._value_loss and its autograd gradient
+"""
+
+from __future__ import annotations
+
+import os
+import random
+import sys
+from pathlib import Path
+from types import SimpleNamespace
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parents[1]
+REFERENCE = Path(os.environ.get("CARDGYM_REFERENCE", "/root/reference"))
+sys.path.insert(0, str(REPO))
+sys.path.insert(0, str(REFERENCE))
+
+from card_playing_gym_b200.config import PlumpModelConfig, synthetic_plump_actor_state  # noqa: E402
+
+TRUNK_CONFIGS = {
+    # tests/conftest.py:16-19 of the reference with all-layer value embeddings (d % ple == 0 branch)
+    "tiny_div": dict(d_model=32, n_layers=2, n_heads=4, n_kv_heads=2, d_ff=64, per_layer_dim=8, value_embeddings="all"),
+    # d % ple != 0: the truncated-repeat PLE branch rl-v6 takes, GQA group 5, one KV head
+    "tiny_cat": dict(d_model=40, n_layers=3, n_heads=5, n_kv_heads=1, d_ff=48, per_layer_dim=16, value_embeddings="alternating"),
+    # the rl-v6 architecture with synthetic weights
+    "rlv6": dict(d_model=240, n_layers=16, n_heads=10, n_kv_heads=2, d_ff=720, per_layer_dim=64, value_embeddings="alternating"),
+}
+
+
+def plump_streams(count: int, seed: int) -> list[np.ndarray]:
+    """Observer streams of random complete plump rounds (the reference's tests/nn/test_trunk.py:18-35 recipe)."""
+
+    from cardgym.games.plump.env import PlumpEnv
+    from cardgym.games.plump.rounds import RoundSpec, round_game_config
+    from cardgym.games.plump.tokens import Schema, seat_tokens
+
+    rng = random.Random(seed)
+    result = []
+    for index in range(count):
+        players, hand = rng.choice([3, 4, 5]), rng.choice(range(3, 11))
+        start = rng.randrange(players)
+        env = PlumpEnv(round_game_config(RoundSpec(players, hand), bidding_start_player=start), seed=seed * 1000 + index)
+        env.reset(seed=seed * 1000 + index)
+        while not env.is_done():
+            env.step(rng.choice(env.legal_actions()))
+        observer = rng.randrange(players)
+        result.append(
+            seat_tokens(Schema(), env.state.event_log, observer, players, hand,
+                        env.state.current_round.initial_hands[observer], start)
+        )
+    return result
+
+
+def pad(streams: list[np.ndarray]) -> tuple[np.ndarray, np.ndarray]:
+    lengths = np.array([s.shape[0] for s in streams], dtype=np.int64)
+    out = np.zeros((len(streams), lengths.max(), streams[0].shape[1]), dtype=np.int64)
+    for row, s in enumerate(streams):
+        out[row, : s.shape[0]] = s
+    return out, lengths
+
+
+def reference_actor(config: dict, seed: int):
+    from cardgym.games.plump.model import PlumpActor
+    from cardgym.games.plump.model import PlumpModelConfig as RefConfig
+
+    actor = PlumpActor(RefConfig(**config))
+    state = synthetic_plump_actor_state(PlumpModelConfig(**config), seed=seed)
+    missing, unexpected = actor.load_state_dict({k: torch.from_numpy(v) for k, v in state.items()}, strict=False)
+    # Auxiliary heads stay at their init: they are off the rollout path.
+    assert not unexpected and all(
+        name.startswith(("suit_head", "rank_boundary_head", "trick_head", "next_winner_head", "bid_hit_head"))
+        for name in missing
+    ), (missing, unexpected)
+    return actor.eval()
+
+
+def ragged_schedule(lengths: np.ndarray, prefix: int, seed: int) -> list[np.ndarray]:
+    """Per wave, the tokens each row appends (0..3), as the reference's test_trunk.py:51-56 draws them."""
+
+    rng = random.Random(seed)
+    cursor = [prefix] * len(lengths)
+    waves = []
+    while any(c < n for c, n in zip(cursor, lengths)):
+        counts = [min(rng.randint(0, 3), int(n) - c) for c, n in zip(cursor, lengths)]
+        if not any(counts):
+            continue
+        waves.append(np.array(counts, dtype=np.int64))
+        cursor = [c + n for c, n in zip(cursor, counts)]
+    return waves
+
+
+def run_ragged(actor, padded, lengths, prefix, waves, kv_dtype, autocast: bool):
+    """Prefill then the ragged waves; returns per-wave (tokens, positions, offsets, hidden, bid, card, values)."""
+
+    from contextlib import nullcontext
+
+    ctx = torch.autocast("cpu", dtype=torch.bfloat16) if autocast else nullcontext()
+    records = []
+    with torch.no_grad():
+        cache = actor.new_cache(len(lengths), int(lengths.max()) + 1, kv_dtype)
+        with ctx:
+            hidden = actor.forward_prefill(torch.from_numpy(padded[:, :prefix]), cache, None)
+        prefill_hidden = hidden.float().numpy()
+        cursor = np.full(len(lengths), prefix, dtype=np.int64)
+        for counts in waves:
+            run = int(counts.max())
+            tokens = np.zeros((len(lengths), run, padded.shape[2]), dtype=np.int64)
+            offsets = np.zeros(len(lengths), dtype=np.int64)
+            for row, (start, count) in enumerate(zip(cursor, counts)):
+                if not count:
+                    continue
+                block = padded[row, start : start + count]
+                tokens[row, :count] = block
+                tokens[row, count:] = block[-1]
+                offsets[row] = count - 1
+            with ctx:
+                h = actor.forward_ragged(torch.from_numpy(tokens), torch.from_numpy(cursor.copy()), cache, torch.from_numpy(offsets))
+                bid = actor.policy_logits(h, "bid").float()
+                card = actor.policy_logits(h, "play").float()
+                values = actor.player_values(h).float()
+            records.append((tokens, cursor.copy(), offsets, h.float().numpy(), bid.numpy(), card.numpy(), values.numpy()))
+            cursor = cursor + counts
+    return prefill_hidden, records
+
+
+def make_trunk(name: str, config: dict, streams: list[np.ndarray], seed: int) -> None:
+    actor = reference_actor(config, seed)
+    padded, lengths = pad(streams)
+    prefix = 4
+    waves = ragged_schedule(lengths, prefix, seed + 1)
+    out: dict[str, np.ndarray] = {
+        "seed": np.int64(seed),
+        "config_keys": np.array(list(config.keys())),
+        "config_values": np.array([str(v) for v in config.values()]),
+        "tokens": padded.astype(np.int16),
+        "lengths": lengths,
+        "prefix": np.int64(prefix),
+        "n_waves": np.int64(len(waves)),
+    }
+    with torch.no_grad():
+        full = actor.forward_hidden(torch.from_numpy(padded))
+        out["full_hidden"] = full.numpy()
+        out["full_bid"] = actor.policy_logits(full, "bid").numpy()
+        out["full_card"] = actor.policy_logits(full, "play").numpy()
+        out["full_values"] = actor.player_values(full).numpy()
+    prefill, records = run_ragged(actor, padded, lengths, prefix, waves, torch.float32, autocast=False)
+    out["prefill_hidden"] = prefill
+    for i, (tokens, positions, offsets, hidden, bid, card, values) in enumerate(records):
+        out[f"wave{i}_counts"] = waves[i]
+        out[f"wave{i}_tokens"] = tokens.astype(np.int16)
+        out[f"wave{i}_positions"] = positions
+        out[f"wave{i}_offsets"] = offsets
+        out[f"wave{i}_hidden"] = hidden
+        out[f"wave{i}_bid"] = bid
+        out[f"wave{i}_card"] = card
+        out[f"wave{i}_values"] = values
+    # The reference's own reduced-precision rollout (bf16 autocast, fp16 KV): its deviation
+    # from fp32 is the accuracy bar a bf16 kernel has to stay within.
+    _, low = run_ragged(actor, padded, lengths, prefix, waves, torch.float16, autocast=True)
+    for i, (_, _, _, hidden, bid, card, values) in enumerate(low):
+        out[f"wave{i}_bf16_hidden"] = hidden
+        out[f"wave{i}_bf16_card"] = card
+        out[f"wave{i}_bf16_bid"] = bid
+        out[f"wave{i}_bf16_values"] = values
+    np.savez_compressed(HERE / f"trunk_{name}.npz", **out)
+
+
+def make_sampling() -> None:
+    from cardgym.rl.ppo import masked_probabilities, sample_rows
+
+    rng = np.random.default_rng(11)
+    cases = {}
+    for width in (11, 52, 64):
+        rows = 1024
+        mask = rng.random((rows, width)) < 0.3
+        mask[np.arange(rows), rng.integers(0, width, rows)] = True
+        logits = (rng.standard_normal((rows, width)) * 2.0).astype(np.float32)
+        uniforms = rng.random(rows)
+        uniforms[:8] = [0.0, 1.0, 1.0 - 1e-12, 1e-12, 0.5, 0.25, 0.75, 0.999]
+        probs = masked_probabilities(logits, mask)
+        cases[f"w{width}_logits"] = logits
+        cases[f"w{width}_mask"] = mask
+        cases[f"w{width}_uniforms"] = uniforms
+        cases[f"w{width}_probs"] = probs.astype(np.float32)
+        cases[f"w{width}_actions"] = sample_rows(probs, mask, uniforms).astype(np.int64)
+    np.savez_compressed(HERE / "sampling.npz", **cases)
+
+
+def make_ppo() -> None:
+    from cardgym.rl.ppo import ppo_terms
+
+    rng = np.random.default_rng(12)
+    rows, width = 1024, 52
+    legal = rng.random((rows, width)) < 0.3
+    legal[np.arange(rows), rng.integers(0, width, rows)] = True
+    legal[:16] = False
+    legal[:16, 3] = True  # forced moves: one legal action, entropy ineligible
+    old_logits = rng.standard_normal((rows, width)).astype(np.float32)
+    old = torch.softmax(torch.from_numpy(old_logits).masked_fill(~torch.from_numpy(legal), float("-inf")), -1).numpy()
+    old = np.where(legal, old, 0.0).astype(np.float32)
+    actions = np.array([rng.choice(np.flatnonzero(old[r] > 0), p=old[r][old[r] > 0] / old[r][old[r] > 0].sum()) for r in range(rows)])
+    new_logits = (old_logits + rng.normal(0.0, 0.05, (rows, width))).astype(np.float32)
+    new_logits[16:64] += rng.normal(0.0, 2.0, (48, width)).astype(np.float32)  # far outside the clip range
+    new_logits[64:72] = old_logits[64:72]  # ratio exactly 1
+    advantages = rng.standard_normal(rows).astype(np.float32)
+    advantages[72:80] = 0.0
+    weights = (rng.random(rows) / rows).astype(np.float32)
+    clip, alpha = 0.2, 0.05
+    logits_t = torch.from_numpy(new_logits).requires_grad_()
+    terms = ppo_terms(logits_t, torch.from_numpy(old), torch.from_numpy(actions), torch.from_numpy(advantages), clip_ratio=clip)
+    w = torch.from_numpy(weights)
+    loss = (w * terms.losses).sum()
+    eligible = w * terms.entropy_eligible.float()
+    objective = loss - alpha * (eligible * terms.normalized_entropy).sum()
+    objective.backward()
+    np.savez_compressed(
+        HERE / "ppo.npz",
+        logits=new_logits, old_probs=old, actions=actions.astype(np.int64), advantages=advantages, weights=weights,
+        clip=np.float32(clip), alpha=np.float32(alpha),
+        losses=terms.losses.detach().numpy(), divergences=terms.divergences.detach().numpy(),
+        entropy=terms.entropy.detach().numpy(), normalized_entropy=terms.normalized_entropy.detach().numpy(),
+        entropy_eligible=terms.entropy_eligible.numpy(), ratios=terms.ratios.detach().numpy(),
+        clipped=terms.clipped.numpy(), log_probs=terms.log_probs.detach().numpy(),
+        objective=np.float64(objective.item()), grad=logits_t.grad.numpy(),
+    )
+
+
+def make_gae() -> None:
+    from cardgym.rl.ppo import gae_advantages
+
+    rng = np.random.default_rng(13)
+    games, players = 160, 4
+    lengths = rng.integers(13, 53, games)
+    lengths[:3] = [1, 2, 3]
+    starts = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int64)
+    values = rng.standard_normal((starts[-1], players))
+    seats = rng.integers(0, players, starts[-1])
+    returns = rng.standard_normal((games, players))
+    returns -= returns.mean(axis=1, keepdims=True)
+    out = {}
+    for lam in (0.0, 0.95, 1.0):
+        adv = np.zeros(starts[-1])
+        for g in range(games):
+            lo, hi = starts[g], starts[g + 1]
+            a = gae_advantages(values[lo:hi], returns[g], lam)
+            adv[lo:hi] = a[np.arange(hi - lo), seats[lo:hi]]
+        out[f"adv_{lam}"] = adv
+    np.savez_compressed(HERE / "gae.npz", values=values, seats=seats, starts=starts, returns=returns, **out)
+
+
+def make_value_loss() -> None:
+    from cardgym.rl.trainer import PPOTrainer
+
+    rng = np.random.default_rng(14)
+    rows, players_max = 1024, 5
+    players = rng.integers(3, 6, rows)
+    returns = rng.standard_normal((rows, players_max)) * (np.arange(players_max)[None, :] < players[:, None])
+    prediction = torch.from_numpy(rng.standard_normal((rows, players_max)).astype(np.float32)).requires_grad_()
+    weight = (rng.random(rows) / rows).astype(np.float32)
+    scale = 5.0
+    fake = SimpleNamespace(
+        config=SimpleNamespace(value_reward_scale=scale), device=torch.device("cpu"),
+        upload=lambda array: torch.from_numpy(np.asarray(array)),
+    )
+    dense = SimpleNamespace(
+        flat=torch.arange(rows), seq=np.arange(rows), start=0, weight=torch.from_numpy(weight)
+    )
+    group = SimpleNamespace(player_counts=players, returns=returns.astype(np.float32))
+    totals: dict = {"actor_value_loss": [], "actor_value_squared_error": [], "actor_value_target_squared": [], "actor_value_weight": []}
+    from collections import defaultdict
+
+    totals = defaultdict(list)
+    loss = PPOTrainer._value_loss(fake, None, None, dense, group, totals, "actor_value", values=prediction)
+    loss.backward()
+    np.savez_compressed(
+        HERE / "value_loss.npz", prediction=prediction.detach().numpy(), players=players, returns=returns.astype(np.float32),
+        weight=weight, scale=np.float32(scale), loss=np.float64(loss.item()),
+        squared_error=np.float64(totals["actor_value_squared_error"][0].item()), grad=prediction.grad.numpy(),
+    )
+
+
+def main() -> None:
+    torch.manual_seed(0)
+    streams = plump_streams(48, seed=0)
+    padded, lengths = pad(streams)
+    np.savez_compressed(HERE / "plump_streams.npz", tokens=padded.astype(np.int16), lengths=lengths)
+    make_trunk("tiny_div", TRUNK_CONFIGS["tiny_div"], streams[:6], seed=3)
+    make_trunk("tiny_cat", TRUNK_CONFIGS["tiny_cat"], streams[6:12], seed=4)
+    make_trunk("rlv6", TRUNK_CONFIGS["rlv6"], streams[12:16], seed=5)
+    make_sampling()
+    make_ppo()
+    make_gae()
+    make_value_loss()
+    for path in sorted(HERE.glob("*.npz")):
+        print(f"{path.name}: {path.stat().st_size / 1024:.0f} KiB")
+
+
+if __name__ == "__main__":
+    main()
