@@ -1,0 +1,405 @@
+#!/usr/bin/env python
+"""Self-play decode benchmark: decisions/s of one rl-v6 rollout wave, per GPU and whole box.
+
+One step = one merged rollout wave of the reference's batch collector
+(cardgym/rl/selfplay.py:406-454 + 486-567) at the BASELINE.json rl-v6 configuration:
+4096 concurrent 4-player games = 16,384 KV-cache rows, each appending one token at
+its own length (per-game length U[16, 256], shared by the game's four observers;
+fp16 KV pool of 257 positions), the fused plump field lookup, the 16-layer trunk,
+the final norm, and for each game's acting observer the heads, the legal mask and
+an inverse-CDF draw from a host-supplied uniform. Weights are synthetic N(0, 0.02)
+in the rl-v6 architecture (no checkpoint is read); tokens, masks and uniforms are
+seeded synthetic data.
+
+``value``: decisions/s with every input resident in HBM (4096 decisions per step per
+GPU, summed over GPUs; the KV stream alone is ~6.9 GB per wave, far beyond L2, so no
+flush is needed). ``e2e``: the same metric through the public API with the step's
+inputs copied from pinned host memory and the actions + probabilities copied back,
+every step. ``roofline``: the decode-attention kernel, timed live with CUDA events
+around each of its launches inside the timed region, against the measured HBM copy
+bandwidth. ``cpu_baseline``: the numpy CPU port of the reference path (oracle/) on a
+bounded sample, on this host's cores.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+METRIC = "self-play decisions/sec (whole box, 1/2/4/8 B200); PPO-iteration wall time"
+UNIT = "decisions/s"
+FALLBACK_HBM_GBS = 6650.0
+# DRAM bytes per decode-attention launch from an ncu capture of this workload
+# (profiles/decode_attention_rlv6.md); None until captured.
+ATTENTION_DRAM_BYTES_PER_LAUNCH: float | None = None
+
+
+def parse_args(argv=None):
+    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=30)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    parser.add_argument("--games", type=int, default=4096, help="concurrent 4-player games per GPU")
+    parser.add_argument("--min-len", type=int, default=16)
+    parser.add_argument("--max-len", type=int, default=256)
+    parser.add_argument("--kv", choices=("fp16", "bf16", "fp32"), default="fp16")
+    parser.add_argument("--precision", choices=("bf16", "fp32"), default="bf16")
+    parser.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
+    parser.add_argument("--cpu-games", type=int, default=32, help="games per CPU-baseline wave")
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    return parser.parse_args(argv)
+
+
+def world() -> tuple[int, int, int]:
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def workload_name(args) -> str:
+    return (f"rl-v6 rollout decode wave: {args.games} concurrent 4-player games ({4 * args.games} KV rows), "
+            f"1 token/row, per-game length U[{args.min_len},{args.max_len}], {args.kv} KV, {args.precision} GEMMs")
+
+
+# ---------------------------------------------------------------------------------------------
+# synthetic wave inputs (numpy, seeded)
+# ---------------------------------------------------------------------------------------------
+def synthetic_wave(games: int, min_len: int, max_len: int, seed: int) -> dict[str, np.ndarray]:
+    from card_playing_gym_b200.plump_schema import PlumpSchema, TOKEN_WIDTH, TOKEN_TRICK_WIN
+
+    rng = np.random.default_rng(seed)
+    schema = PlumpSchema()
+    rows = 4 * games
+    lengths = rng.integers(min_len, max_len + 1, games)  # keys each row attends after the append
+    positions = np.repeat(lengths - 1, 4).astype(np.int64)
+    tokens = np.zeros((rows, 1, TOKEN_WIDTH), dtype=np.int16)
+    sizes = schema.base_vocab_sizes
+    tokens[:, 0, 0] = rng.integers(1, 7, rows)
+    for slot in range(1, 16):
+        tokens[:, 0, slot] = rng.integers(0, sizes[slot], rows)
+    tokens[:, 0, 16:25] = rng.integers(0, 53, (rows, 9))
+    tokens[:, 0, 25] = rng.integers(0, 12, rows)
+    tokens[rng.random(rows) < 0.2, 0, 0] = TOKEN_TRICK_WIN
+    seat = rng.integers(0, 4, games)
+    readout_rows = (4 * np.arange(games) + seat).astype(np.int64)
+    heads = rng.integers(0, 2, games).astype(np.int32)
+    legal = rng.random((games, 52)) < 0.3
+    legal[np.arange(games), rng.integers(0, 11, games)] = True
+    legal[heads == 0, 11:] = False
+    uniforms = rng.random(games)
+    return dict(tokens=tokens, positions=positions, offsets=np.zeros(rows, np.int64), readout_rows=readout_rows,
+                heads=heads, legal=legal.astype(np.uint8), uniforms=uniforms, lengths=lengths)
+
+
+# ---------------------------------------------------------------------------------------------
+# CPU port of the reference path (oracle/): the baseline leg and the reference arm
+# ---------------------------------------------------------------------------------------------
+class CpuWave:
+    """One rollout wave of the numpy port on a bounded sample of games (float32, all host cores)."""
+
+    def __init__(self, games: int, min_len: int, max_len: int, seed: int):
+        from card_playing_gym_b200.config import RL_V6, synthetic_plump_actor_state
+        from oracle import plump as oplump
+        from oracle.trunk import Precision
+
+        config = {k: getattr(RL_V6, k) for k in ("d_model", "n_layers", "n_heads", "n_kv_heads", "d_ff",
+                                                  "per_layer_dim", "value_embeddings", "max_players", "max_hand_size")}
+        state = synthetic_plump_actor_state(RL_V6, seed=0)
+        self.actor = oplump.PlumpActor(state, config, Precision(kv="fp32", dtype=np.float32))
+        self.wave = synthetic_wave(games, min_len, max_len, seed)
+        self.games = games
+        rng = np.random.default_rng(seed + 1)
+        self.cache = self.actor.new_cache(4 * games, max_len + 1)
+        self.cache.k[...] = rng.standard_normal(self.cache.k.shape, dtype=np.float32)
+        self.cache.v[...] = rng.standard_normal(self.cache.v.shape, dtype=np.float32)
+        self.span = max_len + 1
+
+    def step(self) -> np.ndarray:
+        from oracle import ppo as oppo
+
+        w = self.wave
+        hidden = self.actor.forward_ragged(w["tokens"].astype(np.int64), w["positions"], self.cache, w["offsets"],
+                                           span=self.span)
+        readout = hidden[w["readout_rows"]]
+        actions = np.zeros(self.games, dtype=np.int64)
+        for head, (name, width) in enumerate((("bid", 11), ("play", 52))):
+            rows = w["heads"] == head
+            logits = self.actor.heads.policy_logits(readout[rows], name).astype(np.float32)
+            mask = w["legal"][rows, :width].astype(bool)
+            probs = oppo.masked_probabilities(logits, mask)
+            actions[rows] = oppo.sample_rows(probs, mask, w["uniforms"][rows])
+        self.actor.heads.player_values(readout)
+        return actions
+
+
+def cpu_baseline(args, seconds: float) -> dict:
+    wave = CpuWave(args.cpu_games, args.min_len, args.max_len, seed=99)
+    wave.step()  # warm-up
+    count, start = 0, time.perf_counter()
+    while True:
+        wave.step()
+        count += 1
+        elapsed = time.perf_counter() - start
+        if elapsed >= seconds or count >= 1000:
+            break
+    return {
+        "value": count * args.cpu_games / elapsed,
+        "unit": UNIT,
+        "cores": os.cpu_count(),
+        "kind": "port",
+        "sample": (f"{count} waves of {args.cpu_games} games ({4 * args.cpu_games} rows) of the same workload, "
+                   f"numpy float32 port (oracle/), {elapsed:.1f} s"),
+    }
+
+
+def run_reference(args) -> int:
+    rank, world_size, _ = world()
+    if rank != 0:
+        return 0
+    wave = CpuWave(args.cpu_games, args.min_len, args.max_len, seed=99)
+    for _ in range(max(args.warmup, 1)):
+        wave.step()
+    start = time.perf_counter()
+    for _ in range(args.steps):
+        wave.step()
+    elapsed = time.perf_counter() - start
+    value = args.steps * args.cpu_games / elapsed
+    sample = f"{args.cpu_games} games ({4 * args.cpu_games} rows) per step, numpy float32 port of the reference path"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world_size,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * elapsed / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": workload_name(args), "cpu_sample_games": args.cpu_games},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": os.cpu_count(), "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------------------------
+CLOCK_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+
+class ClockSampler:
+    def __init__(self, gpus: list[int]):
+        self.gpus = gpus
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={CLOCK_FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.file, stderr=subprocess.DEVNULL,
+            )
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.seek(0)
+        clocks, maxima, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.file.read().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9 or not parts[0].isdigit() or int(parts[0]) not in self.gpus:
+                continue
+            try:
+                clocks.append(float(parts[1]))
+                maxima.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        os.unlink(self.file.name)
+        return {
+            "sm_mhz": statistics.median(clocks) if clocks else None,
+            "sm_max_mhz": max(maxima) if maxima else None,
+            "reasons": sorted(reasons),
+            "samples": len(clocks),
+        }
+
+
+def measured_peak() -> tuple[float, str]:
+    path = REPO / "MEASURED_PEAKS.json"
+    try:
+        peaks = json.loads(path.read_text())
+        return float(peaks["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+# ---------------------------------------------------------------------------------------------
+# the B200 arm
+# ---------------------------------------------------------------------------------------------
+def run_b200(args) -> int:
+    import torch
+    import torch.distributed as dist
+
+    from card_playing_gym_b200 import _native as nat
+    from card_playing_gym_b200.config import RL_V6, synthetic_plump_actor_state
+    from card_playing_gym_b200.plump import PlumpActor
+
+    rank, world_size, local = world()
+    if world_size > 1:
+        import datetime
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    kv_dtype = {"fp16": torch.float16, "bf16": torch.bfloat16, "fp32": torch.float32}[args.kv]
+
+    state = synthetic_plump_actor_state(RL_V6, seed=0)
+    actor = PlumpActor(RL_V6, state, device=device, precision=args.precision)
+    wave = synthetic_wave(args.games, args.min_len, args.max_len, seed=1000 + 7919 * rank)
+    rows = 4 * args.games
+    max_len = args.max_len + 1
+    cache = actor.new_cache(rows + 1, max_len, kv_dtype)  # + the collector's spare scratch row
+    generator = torch.Generator(device=device).manual_seed(17 + rank)
+    for pool in (cache.k_pool, cache.v_pool):
+        for layer in range(pool.shape[0]):
+            pool[layer].normal_(generator=generator)
+    dev = {k: torch.from_numpy(v).to(device) for k, v in wave.items()}
+    span = max_len
+    games = args.games
+
+    def step():
+        hidden = actor.forward_ragged(dev["tokens"], dev["positions"], cache, dev["offsets"], span=span)
+        return actor.decide(hidden, dev["heads"], dev["legal"], dev["uniforms"], dev["readout_rows"], logits=False,
+                            values=True)
+
+    def barrier():
+        if world_size > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    def max_over_ranks(value: float) -> float:
+        if world_size == 1:
+            return value
+        t = torch.tensor([value], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    stream = torch.cuda.current_stream(device)
+    clocks = ClockSampler(list(range(world_size)) if rank == 0 else []) if rank == 0 else None
+    nat.attention_profiling(True, capacity=args.steps * RL_V6.n_layers + 16)
+    launches0 = nat.launch_count()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    start.record(stream)
+    for _ in range(args.steps):
+        step()
+    end.record(stream)
+    barrier()
+    launches = nat.launch_count() - launches0
+    device_ms = start.elapsed_time(end)
+    attention_ms = nat.attention_timings()
+    nat.attention_profiling(False)
+    clock_info = clocks.stop() if clocks else None
+    device_ms = max_over_ranks(device_ms)
+    ms_per_step = device_ms / args.steps
+    value = world_size * games * args.steps / (device_ms / 1000.0)
+
+    # e2e: public API, pinned host inputs in, actions + probabilities out, every step.
+    host = {k: torch.from_numpy(v).pin_memory() for k, v in wave.items() if k != "lengths"}
+    out_actions = torch.empty(games, dtype=torch.int64).pin_memory()
+    out_probs = torch.empty((games, 52), dtype=torch.float32).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = out_actions.numel() * 8 + out_probs.numel() * 4
+
+    def e2e_step():
+        inputs = {k: v.to(device, non_blocking=True) for k, v in host.items()}
+        hidden = actor.forward_ragged(inputs["tokens"], inputs["positions"], cache, inputs["offsets"], span=span)
+        _, probs, actions, _ = actor.decide(hidden, inputs["heads"], inputs["legal"], inputs["uniforms"],
+                                            inputs["readout_rows"], logits=False, values=False)
+        out_actions.copy_(actions, non_blocking=True)
+        out_probs.copy_(probs, non_blocking=True)
+        stream.synchronize()  # the host needs the actions before it can step its games
+
+    for _ in range(max(2, args.warmup // 2)):
+        e2e_step()
+    barrier()
+    start.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    end.record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(start.elapsed_time(end))
+    e2e_value = world_size * games * args.steps / (e2e_ms / 1000.0)
+
+    if rank == 0:
+        head_dim = RL_V6.head_dim
+        esize = torch.tensor([], dtype=kv_dtype).element_size()
+        keys = np.minimum(wave["positions"] + 1, span).sum()  # T = 1: key_length = position + 1
+        kv_bytes = float(keys) * RL_V6.n_kv_heads * head_dim * esize * 2
+        qo_bytes = rows * RL_V6.n_heads * head_dim * (esize + 4)  # q in the cache dtype, fp32 output
+        algorithmic = kv_bytes + qo_bytes
+        mean_ms = statistics.fmean(attention_ms) if attention_ms else float("nan")
+        achieved = algorithmic / (mean_ms / 1000.0) / 1e9
+        peak, peak_kind = measured_peak()
+        traffic = ATTENTION_DRAM_BYTES_PER_LAUNCH
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world_size, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": args.precision, "data": "synthetic (seeded tokens, masks, uniforms; N(0,0.02) weights)",
+            "config": {
+                "workload": workload_name(args), "games_per_gpu": games, "rows_per_gpu": rows, "tokens_per_row": 1,
+                "max_context": args.max_len, "kv_dtype": args.kv, "precision": args.precision,
+                "decisions_per_step_per_gpu": games, "l2": "inputs larger than L2 (KV read ~6.9 GB per wave per GPU)",
+                "parallelism": f"independent self-play games on each of {world_size} GPU(s), no collective",
+            },
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "roofline": {
+                "kernel": "decode attention (attn_tc_kernel)", "bound": "hbm", "achieved": achieved, "peak": peak,
+                "unit": "GB/s", "frac": achieved / peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                "traffic": traffic, "algorithmic_bytes_per_launch": algorithmic, "mean_launch_ms": mean_ms,
+                "launches_timed": len(attention_ms),
+            },
+            "gpu_launches": int(launches),
+            "clocks": clock_info,
+        }
+        if world_size == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(args, args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+    if world_size > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main(argv=None) -> int:
+    args = parse_args(argv)
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_b200(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,108 @@
+// KV pool maintenance: per-row writes and row copies (cardgym/nn/kv_cache.py:84-105, 122-138).
+#include "common.cuh"
+
+namespace cg {
+
+// k_new/v_new [B, KVH, T, D] -> pool[rows[b], kvh, positions[b, t], :]
+__global__ void kv_write_step_kernel(void* k_layer, void* v_layer, int kv_dtype, int kv_heads, int max_len, int head_dim,
+                                     const int64_t* rows, const int64_t* positions, int64_t batch, int steps,
+                                     const void* k_new, const void* v_new, int src_dtype) {
+  const int64_t total = batch * kv_heads * steps * head_dim;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int d = static_cast<int>(i % head_dim);
+    const int t = static_cast<int>((i / head_dim) % steps);
+    const int kvh = static_cast<int>((i / (static_cast<int64_t>(head_dim) * steps)) % kv_heads);
+    const int64_t b = i / (static_cast<int64_t>(head_dim) * steps * kv_heads);
+    const int64_t row = rows ? rows[b] : b;
+    const int64_t pos = positions[b * steps + t];
+    const int64_t dst = ((row * kv_heads + kvh) * max_len + pos) * head_dim + d;
+    store_from_float(k_layer, dst, kv_dtype, load_as_float(k_new, i, src_dtype));
+    store_from_float(v_layer, dst, kv_dtype, load_as_float(v_new, i, src_dtype));
+  }
+}
+
+// Gather (to_stage=1) or scatter (to_stage=0) `count` rows of every layer, first `length` positions.
+// The stage holds [count, n_layers, 2, KVH, length, D] in 16-byte words when the row width allows.
+__global__ void kv_stage_kernel(unsigned char* k_pool, unsigned char* v_pool, unsigned char* stage, int n_layers,
+                                int64_t capacity, int kv_heads, int max_len, int64_t row_bytes_pos, const int64_t* rows,
+                                int64_t count, int length, int to_stage) {
+  // One "segment" = one (row, layer, k|v, head): `length * row_bytes_pos` contiguous bytes.
+  const int64_t seg_bytes = static_cast<int64_t>(length) * row_bytes_pos;
+  const int64_t segs = count * n_layers * 2 * kv_heads;
+  const bool vec = (seg_bytes % 16 == 0) && (row_bytes_pos * max_len % 16 == 0);
+  const int64_t unit = vec ? 16 : 1;
+  const int64_t per_seg = seg_bytes / unit;
+  const int64_t total = segs * per_seg;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t seg = i / per_seg, w = i % per_seg;
+    const int kvh = static_cast<int>(seg % kv_heads);
+    const int which = static_cast<int>((seg / kv_heads) % 2);
+    const int layer = static_cast<int>((seg / (2 * kv_heads)) % n_layers);
+    const int64_t r = seg / (2 * kv_heads * static_cast<int64_t>(n_layers));
+    const int64_t row = rows[r];
+    unsigned char* pool = which ? v_pool : k_pool;
+    const int64_t pool_off = (((static_cast<int64_t>(layer) * capacity + row) * kv_heads + kvh) * max_len) * row_bytes_pos;
+    unsigned char* a = pool + pool_off + w * unit;
+    unsigned char* s = stage + seg * seg_bytes + w * unit;
+    if (vec) {
+      if (to_stage) *reinterpret_cast<uint4*>(s) = *reinterpret_cast<const uint4*>(a);
+      else *reinterpret_cast<uint4*>(a) = *reinterpret_cast<const uint4*>(s);
+    } else {
+      if (to_stage) *s = *a;
+      else *a = *s;
+    }
+  }
+}
+
+}  // namespace cg
+
+extern "C" int cg_kv_write_step(void* k_layer, void* v_layer, int kv_dtype, int64_t capacity, int kv_heads, int max_len,
+                                int head_dim, const int64_t* rows, const int64_t* positions, int64_t batch, int steps,
+                                const void* k_new, const void* v_new, int src_dtype, void* stream) {
+  using namespace cg;
+  CG_REQUIRE(valid_dtype(kv_dtype) && valid_dtype(src_dtype), "cg_kv_write_step: bad dtype");
+  CG_REQUIRE(batch >= 0 && steps > 0 && kv_heads > 0 && head_dim > 0 && max_len > 0, "cg_kv_write_step: bad shape");
+  if (batch == 0) return CG_OK;
+  CG_REQUIRE(k_layer && v_layer && positions && k_new && v_new, "cg_kv_write_step: NULL pointer");
+  (void)capacity;
+  const int64_t total = batch * kv_heads * steps * head_dim;
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 65535) blocks = 65535;
+  kv_write_step_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      k_layer, v_layer, kv_dtype, kv_heads, max_len, head_dim, rows, positions, batch, steps, k_new, v_new, src_dtype);
+  return check_launch("kv_write_step_kernel");
+}
+
+extern "C" int64_t cg_kv_copy_rows_workspace_bytes(int n_layers, int kv_heads, int max_len, int head_dim, int kv_dtype,
+                                                   int64_t count) {
+  return count * n_layers * 2LL * kv_heads * max_len * head_dim * cg::dtype_size(kv_dtype);
+}
+
+extern "C" int cg_kv_copy_rows(void* k_pool, void* v_pool, int kv_dtype, int n_layers, int64_t capacity, int kv_heads,
+                               int max_len, int head_dim, const int64_t* sources, const int64_t* targets, int64_t count,
+                               int length, void* workspace, int64_t workspace_bytes, void* stream) {
+  using namespace cg;
+  CG_REQUIRE(valid_dtype(kv_dtype), "cg_kv_copy_rows: bad dtype");
+  CG_REQUIRE(count >= 0 && length >= 0 && length <= max_len, "cg_kv_copy_rows: bad count/length");
+  if (count == 0 || length == 0) return CG_OK;
+  CG_REQUIRE(k_pool && v_pool && sources && targets && workspace, "cg_kv_copy_rows: NULL pointer");
+  const int64_t row_bytes_pos = static_cast<int64_t>(head_dim) * dtype_size(kv_dtype);
+  const int64_t need = count * n_layers * 2LL * kv_heads * length * row_bytes_pos;
+  if (workspace_bytes < need)
+    return set_error(CG_ERR_WORKSPACE, "cg_kv_copy_rows: workspace %lld < %lld bytes", (long long)workspace_bytes,
+                     (long long)need);
+  CG_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 15) == 0, "cg_kv_copy_rows: workspace must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int blocks = sm_count() * 8;
+  kv_stage_kernel<<<blocks, 256, 0, s>>>(static_cast<unsigned char*>(k_pool), static_cast<unsigned char*>(v_pool),
+                                         static_cast<unsigned char*>(workspace), n_layers, capacity, kv_heads, max_len,
+                                         row_bytes_pos, sources, count, length, 1);
+  int rc = check_launch("kv_stage_kernel(gather)");
+  if (rc) return rc;
+  kv_stage_kernel<<<blocks, 256, 0, s>>>(static_cast<unsigned char*>(k_pool), static_cast<unsigned char*>(v_pool),
+                                         static_cast<unsigned char*>(workspace), n_layers, capacity, kv_heads, max_len,
+                                         row_bytes_pos, targets, count, length, 0);
+  return check_launch("kv_stage_kernel(scatter)");
+}

@@ -1,0 +1,202 @@
+// Plump field lookup and the token-level ragged forward.
+//
+// Reference: cardgym/games/plump/model.py:94-167 (PlumpEmbedding: three embedding_bag
+// sums + the NA-pattern row + the remaining-hand rank/suit rows on TRICK_WIN tokens)
+// and cardgym/nn/model.py:76-89 (SequenceModel.forward_ragged = embed -> condition ->
+// Trunk.forward_ragged). One fused lookup reads a packed [field rows + pattern rows,
+// d | ple | value] table, so all three sums come from one pass over each token, with
+// no boolean-mask nonzero (the reference's host sync, model.py:143).
+#include "trunk.h"
+
+namespace cg {
+
+int forward_ragged_impl(const cg_trunk_dims* dims_p, const void* blob, const float* x_in, const float* ple,
+                        const float* values, int64_t batch, int steps, const int64_t* positions,
+                        const int64_t* readout_offsets, const int64_t* rows, int span, void* k_pool, void* v_pool,
+                        int kv_dtype, int64_t capacity, int max_len, int precision, void* workspace,
+                        int64_t workspace_bytes, float* hidden_out, cudaStream_t s, bool x_in_workspace);
+
+namespace {
+constexpr int64_t kAlign = 256;
+inline int64_t align_up(int64_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
+
+__device__ __forceinline__ int64_t token_at(const void* tokens, int dtype, int64_t index) {
+  if (dtype == CG_I16) return static_cast<const int16_t*>(tokens)[index];
+  if (dtype == CG_I32) return static_cast<const int32_t*>(tokens)[index];
+  return static_cast<const int64_t*>(tokens)[index];
+}
+}  // namespace
+
+// One warp per token; lanes own 4 consecutive columns per 128-column block.
+__global__ void __launch_bounds__(256) plump_embed_kernel(cg_plump_schema sc, const float* __restrict__ table, int width,
+                                                          const void* __restrict__ tokens, int token_dtype, int64_t n,
+                                                          float* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t tok = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (tok >= n) return;
+  const int64_t base = tok * sc.token_width;
+  const int total_rows = sc.field_rows + sc.pattern_rows;
+  // Resolve the row ids once per token (lane f holds field f; lanes 0..2*hand_slots-1 the hand rows).
+  int field_row = -1;
+  if (lane < sc.field_count) {
+    const int64_t id = token_at(tokens, token_dtype, base + sc.field_slots[lane]);
+    const bool present = sc.field_na[lane] < 0 || id != sc.field_na[lane];
+    const int64_t row = id + sc.field_offsets[lane];
+    if (present) {
+      if (id < 0 || row >= sc.field_rows) {
+        raise_fault(0x200);
+      } else {
+        field_row = static_cast<int>(row);
+      }
+    }
+  }
+  int64_t pattern = token_at(tokens, token_dtype, base + sc.slot_pattern);
+  if (pattern < 0 || pattern >= sc.pattern_rows) {
+    raise_fault(0x201);
+    pattern = 0;
+  }
+  const bool trick_win = token_at(tokens, token_dtype, base + sc.slot_type) == sc.trick_win_type;
+  int hand_row = -1;  // lane 2c: rank row of card c, lane 2c+1: its suit row
+  if (trick_win && lane < 2 * sc.hand_slots) {
+    const int64_t card = token_at(tokens, token_dtype, base + sc.slot_hand + lane / 2);
+    if (card >= 0 && card < sc.num_cards) {
+      hand_row = (lane & 1) ? static_cast<int>(card / sc.num_ranks) + sc.suit_offset
+                            : static_cast<int>(card % sc.num_ranks) + sc.rank_offset;
+    }
+  }
+  const bool vec = (width & 3) == 0;
+  for (int c0 = 0; c0 < width; c0 += 128) {
+    const int c = c0 + lane * 4;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    float hand[4] = {0.f, 0.f, 0.f, 0.f};
+    auto add_row = [&](float (&dst)[4], int row) {
+      const float* src = table + static_cast<int64_t>(row) * width + c;
+      if (vec && c + 3 < width) {
+        const float4 v = *reinterpret_cast<const float4*>(src);
+        dst[0] += v.x;
+        dst[1] += v.y;
+        dst[2] += v.z;
+        dst[3] += v.w;
+      } else {
+        for (int j = 0; j < 4; ++j)
+          if (c + j < width) dst[j] += src[j];
+      }
+    };
+    for (int f = 0; f < sc.field_count; ++f) {
+      const int row = __shfl_sync(0xffffffffu, field_row, f);
+      if (row >= 0 && c < width) add_row(acc, row);
+    }
+    if (c < width) add_row(acc, sc.field_rows + static_cast<int>(pattern));
+    if (trick_win) {
+      for (int j = 0; j < 2 * sc.hand_slots; ++j) {
+        const int row = __shfl_sync(0xffffffffu, hand_row, j);
+        if (row >= 0 && c < width) add_row(hand, row);
+      }
+      for (int j = 0; j < 4; ++j) acc[j] += hand[j];
+    }
+    float* dst = out + tok * width + c;
+    if (vec && c + 3 < width) {
+      *reinterpret_cast<float4*>(dst) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    } else {
+      for (int j = 0; j < 4; ++j)
+        if (c + j < width) dst[j] = acc[j];
+    }
+  }
+  (void)total_rows;
+}
+
+int check_schema(const cg_plump_schema* sc) {
+  CG_REQUIRE(sc, "NULL plump schema");
+  CG_REQUIRE(sc->field_count > 0 && sc->field_count <= 16, "field_count must be 1..16");
+  CG_REQUIRE(sc->hand_slots >= 0 && sc->hand_slots <= 16, "hand_slots must be 0..16");
+  CG_REQUIRE(sc->token_width > 0 && sc->field_rows > 0 && sc->pattern_rows > 0, "bad schema sizes");
+  CG_REQUIRE(sc->num_ranks > 0 && sc->num_cards > 0, "bad card counts");
+  return CG_OK;
+}
+
+int embed(const cg_plump_schema& sc, const float* table, int width, const void* tokens, int token_dtype, int64_t n,
+          float* out, cudaStream_t s) {
+  if (n == 0) return CG_OK;
+  const int64_t blocks = (n + 7) / 8;
+  plump_embed_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(sc, table, width, tokens, token_dtype, n, out);
+  return check_launch("plump_embed_kernel");
+}
+
+struct PlumpWorkspace {
+  float* lookup;
+  float* ple;
+  float* values;
+  unsigned char* step;
+  int64_t step_bytes;
+  int64_t total;
+};
+
+PlumpWorkspace plan_plump(const cg_trunk_dims& dims, int64_t batch, int steps, int precision, unsigned char* base) {
+  PlumpWorkspace w{};
+  const int64_t nt = batch * steps;
+  const int64_t d = dims.d_model, ple_w = static_cast<int64_t>(dims.n_layers) * dims.per_layer_dim;
+  const int64_t val_w = static_cast<int64_t>(value_layer_count(dims)) * dims.n_kv_heads * head_dim(dims);
+  int64_t at = 0;
+  auto take = [&](int64_t bytes) {
+    unsigned char* here = base ? base + at : nullptr;
+    at = align_up(at + bytes);
+    return here;
+  };
+  w.lookup = reinterpret_cast<float*>(take(nt * (d + ple_w + val_w) * 4));
+  w.ple = reinterpret_cast<float*>(take(nt * ple_w * 4));
+  w.values = reinterpret_cast<float*>(take(nt * val_w * 4));
+  w.step_bytes = cg_trunk_step_workspace_bytes(&dims, batch, steps, precision);
+  w.step = take(w.step_bytes);
+  w.total = at;
+  return w;
+}
+
+}  // namespace cg
+
+extern "C" int cg_plump_embed(const cg_plump_schema* schema, const float* table, int width, const void* tokens,
+                              int token_dtype, int64_t n_tokens, float* out, void* stream) {
+  using namespace cg;
+  int rc;
+  if ((rc = check_schema(schema))) return rc;
+  CG_REQUIRE(token_dtype == CG_I16 || token_dtype == CG_I32 || token_dtype == CG_I64, "bad token dtype");
+  CG_REQUIRE(width > 0, "bad width");
+  if (n_tokens == 0) return CG_OK;
+  CG_REQUIRE(table && tokens && out, "cg_plump_embed: NULL pointer");
+  return embed(*schema, table, width, tokens, token_dtype, n_tokens, out, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int64_t cg_plump_step_workspace_bytes(const cg_trunk_dims* dims, int64_t batch, int steps, int precision) {
+  if (!dims) return -1;
+  return cg::plan_plump(*dims, batch, steps, precision, nullptr).total;
+}
+
+extern "C" int cg_plump_forward_ragged(const cg_trunk_dims* dims, const void* blob, const cg_plump_schema* schema,
+                                       const float* table, const void* tokens, int token_dtype, int64_t batch,
+                                       int steps, const int64_t* positions, const int64_t* readout_offsets,
+                                       const int64_t* rows, int span, void* k_pool, void* v_pool, int kv_dtype,
+                                       int64_t capacity, int max_len, int precision, void* workspace,
+                                       int64_t workspace_bytes, float* hidden_out, void* stream) {
+  using namespace cg;
+  int rc;
+  if ((rc = check_schema(schema))) return rc;
+  CG_REQUIRE(dims, "NULL trunk dims");
+  CG_REQUIRE(token_dtype == CG_I16 || token_dtype == CG_I32 || token_dtype == CG_I64, "bad token dtype");
+  if (batch == 0) return CG_OK;
+  CG_REQUIRE(table && tokens && workspace, "cg_plump_forward_ragged: NULL pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  PlumpWorkspace w = plan_plump(*dims, batch, steps, precision, static_cast<unsigned char*>(workspace));
+  if (workspace_bytes < w.total)
+    return set_error(CG_ERR_WORKSPACE, "plump step workspace %lld < %lld bytes", (long long)workspace_bytes,
+                     (long long)w.total);
+  const int64_t nt = batch * steps;
+  const int ple_w = dims->n_layers * dims->per_layer_dim;
+  const int val_w = value_layer_count(*dims) * dims->n_kv_heads * head_dim(*dims);
+  const int width = dims->d_model + ple_w + val_w;
+  if ((rc = embed(*schema, table, width, tokens, token_dtype, nt, w.lookup, s))) return rc;
+  // The residual stream x is the first buffer of the step workspace.
+  float* x = reinterpret_cast<float*>(w.step);
+  if ((rc = cg_trunk_condition(dims, blob, w.lookup, nt, x, w.ple, w.values, precision, s))) return rc;
+  return forward_ragged_impl(dims, blob, x, w.ple, w.values, batch, steps, positions, readout_offsets, rows, span,
+                             k_pool, v_pool, kv_dtype, capacity, max_len, precision, w.step, w.step_bytes, hidden_out, s,
+                             true);
+}

@@ -1,0 +1,234 @@
+/*
+ * card_playing_gym_b200 — C ABI of the B200-native self-play hot path.
+ *
+ * Plain pointers, sizes and a cudaStream_t passed as void*; no torch types. Every
+ * function returns 0 (CG_OK) or an error code and leaves a message for
+ * cg_last_error(). Device pointers must live on the current CUDA device; host
+ * pointers are rejected by the launch. Nothing here falls back to the CPU.
+ *
+ * Reference interfaces replaced (paths inside maxrlinder/card_playing_gym):
+ *   cardgym/nn/cuda_decode.py:135-151,172-202   decode_attention custom op
+ *   cardgym/nn/kv_cache.py:84-105,122-138        KVCache.write_step / copy_rows
+ *   cardgym/games/plump/model.py:94-167          PlumpEmbedding.forward (field lookup)
+ *   cardgym/nn/trunk.py:285-312,391-429          Trunk.condition / Trunk.forward_ragged
+ *   cardgym/nn/model.py:76-89                    SequenceModel.forward_ragged
+ *   cardgym/games/plump/model.py:204-217         PlumpActor.policy_logits / player_values
+ *   cardgym/rl/ppo.py:75-94                      masked_probabilities / sample_rows
+ *   cardgym/rl/selfplay.py:486-567               launch_policies / sample_decisions
+ *   cardgym/rl/ppo.py:121-144, rl/trainer.py:634-649   gae_advantages / PPOTrainer._gae
+ *   cardgym/rl/ppo.py:28-72, rl/trainer.py:733-802     ppo_terms + _policy_loss (+ autograd)
+ *   cardgym/rl/trainer.py:822-850                _value_loss (+ autograd)
+ *   cardgym/rl/ppo.py:147-153                    weighted_mean_std
+ */
+#ifndef CG_B200_H
+#define CG_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types */
+enum { CG_F32 = 0, CG_F16 = 1, CG_BF16 = 2 };
+/* integer index types (token arrays) */
+enum { CG_I16 = 16, CG_I32 = 32, CG_I64 = 64 };
+/* trunk arithmetic: fp32 everywhere (CUDA cores), or bf16 GEMM operands with fp32 accumulation (tensor cores) */
+enum { CG_PREC_FP32 = 0, CG_PREC_BF16 = 1 };
+/* status codes */
+enum { CG_OK = 0, CG_ERR_ARGUMENT = 1, CG_ERR_CUDA = 2, CG_ERR_WORKSPACE = 3, CG_ERR_FAULT = 4 };
+
+/* Message of the last failed call on this host thread. */
+const char* cg_last_error(void);
+/* ABI version (increments on any signature change). */
+int cg_version(void);
+/* Synchronizes the device, returns and clears the device fault word that kernels set
+ * when a bounded wait gives up (0 = no fault). */
+int cg_fault_status(int* code_out);
+/* Kernel launches this process has issued through the library so far. */
+int64_t cg_launch_count(void);
+/* Measurement hooks (no reference counterpart): while enabled, every decode-attention
+ * launch is bracketed by a pair of CUDA events on its stream (up to `capacity` launches;
+ * enabling clears earlier records). cg_attention_timings synchronizes and writes the
+ * recorded launch durations in milliseconds; it returns how many it wrote (or -1). */
+int cg_attention_profiling(int enable, int capacity);
+int cg_attention_timings(float* ms_out, int max_count);
+
+/* ---------------------------------------------------------------------------------
+ * Decode attention straight from the KV pool.
+ * Replaces torch.ops.cardgym.decode_attention (cardgym/nn/cuda_decode.py:135-151):
+ *   q [B, H, T, D] contiguous, k/v [R, KVH, L, D] (stride over D == 1), rows [B],
+ *   lengths [B] (key length including the row's first new token), span, scale;
+ *   query t of row b sees keys < min(lengths[b] + t, span).
+ * Beyond the reference: any D that is a multiple of 8 up to 128, H/KVH groups
+ * with G*T up to 64, spans up to L, and fp32 / fp16 / bf16 caches. q and out may
+ * use their own dtypes; out has q's [B, H, T, D] layout.
+ * ------------------------------------------------------------------------------- */
+int cg_decode_attention(const void* q, int q_dtype, const void* k_cache, const void* v_cache, int kv_dtype,
+                        int64_t kv_stride_row, int64_t kv_stride_head, int64_t kv_stride_pos,
+                        const int64_t* rows, const int64_t* lengths, int64_t batch, int heads, int kv_heads,
+                        int steps, int head_dim, int span, float scale, void* out, int out_dtype, void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * KV pool maintenance (cardgym/nn/kv_cache.py). A layer's pool is [R, KVH, L, D]
+ * contiguous; the stacked pool is [n_layers, R, KVH, L, D].
+ * ------------------------------------------------------------------------------- */
+/* KVCache.write_step (kv_cache.py:84-105): k_new/v_new [B, KVH, T, D] (src_dtype) land on
+ * rows[b], positions [B, T] (already clamped by the caller, as the reference does). */
+int cg_kv_write_step(void* k_layer, void* v_layer, int kv_dtype, int64_t capacity, int kv_heads, int max_len,
+                     int head_dim, const int64_t* rows, const int64_t* positions, int64_t batch, int steps,
+                     const void* k_new, const void* v_new, int src_dtype, void* stream);
+
+/* KVCache.copy_rows (kv_cache.py:122-138): the first `length` positions of every layer of
+ * sources[i] onto targets[i]; overlapping source/target sets are allowed (staged through
+ * the workspace, at most cg_kv_copy_rows_workspace_bytes). */
+int64_t cg_kv_copy_rows_workspace_bytes(int n_layers, int kv_heads, int max_len, int head_dim, int kv_dtype,
+                                        int64_t count);
+int cg_kv_copy_rows(void* k_pool, void* v_pool, int kv_dtype, int n_layers, int64_t capacity, int kv_heads,
+                    int max_len, int head_dim, const int64_t* sources, const int64_t* targets, int64_t count,
+                    int length, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * Trunk weights: one device blob. Its fp32 section holds the reference's parameters
+ * (cardgym/nn/trunk.py:124-139,259-270 names) at the offsets below; cg_trunk_prepare
+ * derives the bf16 tensor-core copies of the GEMM weights into the rest of the blob.
+ * ------------------------------------------------------------------------------- */
+typedef struct {
+  int32_t d_model, n_layers, n_heads, n_kv_heads, d_ff, per_layer_dim;
+  int32_t input_norm; /* 1: RMSNorm on the embedding sum (trunk.py:265) */
+  int32_t reserved;
+  uint64_t value_layers; /* bit l set: block l adds a value embedding to V (trunk.py:58-72) */
+} cg_trunk_dims;
+
+enum {
+  CG_PART_INPUT_NORM = 0, CG_PART_PLE_CONTEXT, CG_PART_FINAL_W, CG_PART_FINAL_B,
+  CG_PART_LN_ATTN_W, CG_PART_LN_ATTN_B, CG_PART_QKV, CG_PART_OUT, CG_PART_LN_MLP_W, CG_PART_LN_MLP_B,
+  CG_PART_UP, CG_PART_UP_B, CG_PART_DOWN, CG_PART_DOWN_B, CG_PART_COUNT
+};
+
+int64_t cg_trunk_blob_bytes(const cg_trunk_dims* dims);
+/* Byte offset of a fp32 tensor in the blob (layer ignored for trunk-wide parts); -1 if absent. */
+int64_t cg_trunk_part_offset(const cg_trunk_dims* dims, int part, int layer);
+/* Fill the blob's bf16 tensor-core section from its fp32 section. */
+int cg_trunk_prepare(const cg_trunk_dims* dims, void* blob, void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * Plump field lookup (cardgym/games/plump/model.py:94-167).
+ * table: fp32 [field_rows + pattern_rows, width] with the d, PLE and value tables side
+ * by side (width = d + ple_width + value_width); rows 0..field_rows-1 are the field
+ * rows, then the NA-pattern rows.
+ * ------------------------------------------------------------------------------- */
+typedef struct {
+  int32_t field_count;
+  int32_t field_slots[16];
+  int32_t field_offsets[16];
+  int32_t field_na[16]; /* -1: always present */
+  int32_t field_rows, pattern_rows, token_width;
+  int32_t slot_type, slot_pattern, slot_hand, hand_slots, trick_win_type;
+  int32_t rank_offset, suit_offset, num_cards, num_ranks;
+} cg_plump_schema;
+
+/* out [n, width] fp32: the raw lookup sums (x | ple lookup | value lookup). */
+int cg_plump_embed(const cg_plump_schema* schema, const float* table, int width, const void* tokens, int token_dtype,
+                   int64_t n_tokens, float* out, void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * Ragged cached decode of the whole trunk (cardgym/nn/trunk.py:391-429, 183-223):
+ * appends `steps` tokens to each of `batch` cache rows (rows[b], or b when rows is NULL)
+ * at positions[b], and returns the final-normed hidden state of token readout_offsets[b]
+ * of each row. k_pool/v_pool are the stacked [n_layers, capacity, KVH, max_len, D] pools.
+ * cg_trunk_forward_ragged takes conditioned inputs (Trunk.condition outputs):
+ *   x fp32 [B, T, d], ple fp32 [B, T, n_layers, per_layer_dim], values fp32 [B, T, n_value_layers, KVH*D].
+ * cg_plump_forward_ragged starts from tokens (SequenceModel.forward_ragged, model.py:76-89).
+ * ------------------------------------------------------------------------------- */
+int64_t cg_trunk_step_workspace_bytes(const cg_trunk_dims* dims, int64_t batch, int steps, int precision);
+int cg_trunk_forward_ragged(const cg_trunk_dims* dims, const void* blob, const float* x, const float* ple,
+                            const float* values, int64_t batch, int steps, const int64_t* positions,
+                            const int64_t* readout_offsets, const int64_t* rows, int span, void* k_pool,
+                            void* v_pool, int kv_dtype, int64_t capacity, int max_len, int precision,
+                            void* workspace, int64_t workspace_bytes, float* hidden_out, void* stream);
+
+int64_t cg_plump_step_workspace_bytes(const cg_trunk_dims* dims, int64_t batch, int steps, int precision);
+int cg_plump_forward_ragged(const cg_trunk_dims* dims, const void* blob, const cg_plump_schema* schema,
+                            const float* table, const void* tokens, int token_dtype, int64_t batch, int steps,
+                            const int64_t* positions, const int64_t* readout_offsets, const int64_t* rows, int span,
+                            void* k_pool, void* v_pool, int kv_dtype, int64_t capacity, int max_len, int precision,
+                            void* workspace, int64_t workspace_bytes, float* hidden_out, void* stream);
+
+/* Trunk.condition alone (trunk.py:285-312): raw lookup [n, d+ple+value] -> x, ple, values. */
+int cg_trunk_condition(const cg_trunk_dims* dims, const void* blob, const float* lookup, int64_t n_tokens,
+                       float* x_out, float* ple_out, float* values_out, int precision, void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * Heads, legal masking and sampling for one wave of decisions
+ * (cardgym/games/plump/model.py:204-217; cardgym/rl/selfplay.py:486-567; rl/ppo.py:75-94).
+ * heads_blob: fp32; policy head h is W [width[h], d] at weight_offset[h] and b [width[h]]
+ * at bias_offset[h]; the value MLP (d -> d GELU -> value_outputs) at value_* offsets.
+ * ------------------------------------------------------------------------------- */
+typedef struct {
+  int32_t d_model, n_policy, value_outputs, max_width;
+  int32_t width[8];
+  int64_t weight_offset[8], bias_offset[8];
+  int64_t value_w1, value_b1, value_w2, value_b2; /* -1 when value_outputs == 0 */
+} cg_heads_desc;
+
+/* Per decision i: logits of head head_of[i] on hidden[hidden_rows[i]] (hidden_rows NULL: i),
+ * masked softmax over legal[i, :width] (uint8 [D, max_width]), inverse-CDF draw with
+ * uniforms[i] (float64) clamped to the last legal action. Outputs (any may be NULL except
+ * actions): logits/probs fp32 [D, max_width] (zero past the head's width), actions int64 [D],
+ * values fp32 [D, value_outputs]. */
+int cg_plump_decide(const cg_heads_desc* desc, const float* heads_blob, const float* hidden,
+                    const int64_t* hidden_rows, int64_t decisions, const int32_t* head_of, const uint8_t* legal,
+                    const double* uniforms, float* logits_out, float* probs_out, int64_t* actions_out,
+                    float* values_out, void* stream);
+
+/* masked_probabilities + sample_rows on given logits [rows, width] fp32 (ppo.py:75-94). */
+int cg_masked_sample(const float* logits, const uint8_t* mask, const double* uniforms, int64_t rows, int width,
+                     float* probs_out, int64_t* actions_out, void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * PPO advantage and loss step.
+ * ------------------------------------------------------------------------------- */
+/* Undiscounted GAE per game segment, acting-seat column (ppo.py:121-144, trainer.py:634-649):
+ * values f64 [N, players] (game g owns rows starts[g]..starts[g+1]-1 in decision order),
+ * seats int32 [N], returns f64 [G, players] -> advantages f64 [N]. Bit-exact with the
+ * reference's float64 recurrence. */
+int cg_gae_segments(const double* values, int players, const int32_t* seats, const int64_t* starts, int64_t games,
+                    const double* returns, double gae_lambda, double* advantages_out, void* stream);
+
+/* Sums for the batch-global advantage normalisation (ppo.py:147-153): out[0] = sum w,
+ * out[1] = sum w (x - shift), out[2] = sum w (x - shift)^2, in float64, deterministic. */
+int64_t cg_weighted_sums_workspace_bytes(int64_t n);
+int cg_weighted_sums(const double* values, const double* weights, int64_t n, double shift, double* out3,
+                     void* workspace, int64_t workspace_bytes, void* stream);
+/* x <- (x - mean) / std in place. */
+int cg_normalize(double* values, int64_t n, double mean, double std, void* stream);
+
+/* The fused per-head PPO objective (ppo.py:28-72 terms; trainer.py:774-797 objective):
+ *   L = sum_i w_i * loss_i - alpha * sum_i w_i * eligible_i * normalized_entropy_i
+ * logits/old_probs fp32 [rows, width] (row stride `stride`), actions int64, advantages and
+ * weights fp32 [rows]. Outputs (each may be NULL): dlogits fp32 [rows, width] = dL/dlogits;
+ * row_terms fp32 [rows, 8] = (loss, divergence, entropy, normalized entropy, eligible, ratio,
+ * clipped, action log-prob); totals f64 [8] = (sum w loss, sum w, sum w entropy,
+ * sum w eligible normalized_entropy, sum w eligible, sum w clipped, sum w divergence, L),
+ * reduced deterministically through the workspace. */
+int64_t cg_ppo_objective_workspace_bytes(int64_t rows);
+int cg_ppo_objective(const float* logits, const float* old_probs, int64_t rows, int width, int64_t stride,
+                     const int64_t* actions, const float* advantages, const float* weights, float clip_ratio,
+                     float alpha, float* dlogits, float* row_terms, double* totals, void* workspace,
+                     int64_t workspace_bytes, void* stream);
+
+/* Dense per-seat zero-sum value regression and its gradient (trainer.py:822-850):
+ * prediction/targets fp32 [rows, players_max], players int32 [rows], weights fp32 [rows];
+ * grad fp32 [rows, players_max] = dloss/dprediction (may be NULL); totals f64 [4] =
+ * (loss, sum w/n sum raw^2, sum w/n sum target^2, sum w). */
+int64_t cg_value_loss_workspace_bytes(int64_t rows);
+int cg_value_loss(const float* prediction, const float* targets, const int32_t* players, const float* weights,
+                  int64_t rows, int players_max, float reward_scale, float* grad, double* totals, void* workspace,
+                  int64_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CG_B200_H */

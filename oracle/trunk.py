@@ -337,3 +337,38 @@ class Trunk:
             x = self.add_ple(x, ple, layer)
         readout = x[np.arange(batch), np.asarray(readout_offsets, dtype=np.int64)]
         return layer_norm(readout, self.w.final_w, self.w.final_b)
+
+
+def decode_attention(q, k_cache, v_cache, rows, key_lengths, span: int, scale: float, kv: str = "fp32",
+                     dtype=np.float64) -> np.ndarray:
+    """The reference op's contract (cardgym/nn/cuda_decode.py:188-202, trunk.py:225-256).
+
+    q [B, H, T, D]; k/v [R, KVH, L, D]; query t of row b sees keys < min(key_lengths[b] + t, span).
+    ``kv`` names the cache dtype: q is rounded to it (cuda_decode.py:202), and with a
+    16-bit cache the probabilities multiplying V are rounded to it as well.
+    """
+
+    prec = Precision(kv=kv, dtype=dtype)
+    q = prec.stored(np.asarray(q, np.float64))
+    batch, heads, steps, dim = q.shape
+    kv_heads = k_cache.shape[1]
+    group = heads // kv_heads
+    out = np.zeros((batch, heads, steps, dim), dtype=dtype)
+    for b in range(batch):
+        row = int(rows[b])
+        for h in range(heads):
+            kvh = h // group
+            keys = np.asarray(k_cache[row, kvh], np.float64)
+            values = np.asarray(v_cache[row, kvh], np.float64)
+            for t in range(steps):
+                limit = min(int(key_lengths[b]) + t, span)
+                if limit <= 0:
+                    continue
+                scores = keys[:limit] @ q[b, h, t] * scale
+                weights = np.exp(scores - scores.max())
+                total = weights.sum()
+                if kv != "fp32":
+                    out[b, h, t] = prec.stored(weights) @ values[:limit] / total
+                else:
+                    out[b, h, t] = (weights / total) @ values[:limit]
+    return out

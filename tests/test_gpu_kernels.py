@@ -1,0 +1,211 @@
+"""Op-level parity of the CUDA kernels against the CPU oracle, through the C ABI (B200 only)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import plump as oplump
+from oracle import ppo as oppo
+from oracle.trunk import Cache, Precision
+from oracle.trunk import decode_attention as oracle_attention
+from tests.conftest import load_golden
+
+pytestmark = pytest.mark.gpu
+
+TORCH_DTYPES = {"fp32": torch.float32, "fp16": torch.float16, "bf16": torch.bfloat16}
+# Tolerances on max |error| / max |expected|: fp32 arithmetic, then one storage rounding
+# of the probabilities (fp16: 2^-11, bf16: 2^-8) that the oracle places at the final
+# softmax max while the kernel's online softmax places it at the running max.
+ATTN_TOL = {"fp32": 2e-5, "fp16": 2e-3, "bf16": 1.5e-2}
+
+
+def scaled_error(actual: np.ndarray, expected: np.ndarray) -> float:
+    return float(np.abs(actual - expected).max() / max(np.abs(expected).max(), 1e-30))
+
+
+@pytest.mark.parametrize("kv", ["fp32", "fp16", "bf16"])
+@pytest.mark.parametrize("heads,kv_heads,dim", [(10, 2, 24), (8, 2, 32), (5, 1, 40), (8, 4, 64)])
+@pytest.mark.parametrize("steps", [1, 3])
+def test_decode_attention_matches_the_oracle(kv, heads, kv_heads, dim, steps):
+    rng = np.random.default_rng(heads * 100 + dim + steps)
+    batch, capacity, max_len = 37, 48, 300
+    k = rng.standard_normal((capacity, kv_heads, max_len, dim)).astype(np.float32)
+    v = rng.standard_normal((capacity, kv_heads, max_len, dim)).astype(np.float32)
+    q = rng.standard_normal((batch, heads, steps, dim)).astype(np.float32)
+    rows = rng.permutation(capacity)[:batch].astype(np.int64)
+    lengths = rng.integers(1, max_len - steps, batch).astype(np.int64)
+    lengths[:3] = [1, 64, 65]  # one key; chunk boundaries
+    span = int(lengths.max()) + steps - 1
+    span -= 7  # a cap below the longest row: rows near the top see only `span` keys
+    dt = TORCH_DTYPES[kv]
+    kd, vd = torch.from_numpy(k).cuda().to(dt), torch.from_numpy(v).cuda().to(dt)
+    k_stored, v_stored = kd.float().cpu().numpy(), vd.float().cpu().numpy()
+    from card_playing_gym_b200.cuda_decode import decode_attention
+
+    out = decode_attention(torch.from_numpy(q).cuda(), kd, vd, torch.from_numpy(rows).cuda(),
+                           torch.from_numpy(lengths).cuda(), span, dim ** -0.5)
+    assert out.dtype == dt and out.shape == q.shape
+    expected = oracle_attention(q, k_stored, v_stored, rows, lengths, span, dim ** -0.5, kv=kv)
+    assert scaled_error(out.float().cpu().numpy(), expected) < ATTN_TOL[kv]
+
+
+def test_decode_attention_at_the_reference_kernel_shapes():
+    """cardgym/nn/cuda_decode.py's own envelope: head_dim 32, spans <= 64, fp16, 384 rows x 3 tokens."""
+
+    rng = np.random.default_rng(7)
+    batch, heads, kv_heads, dim, steps, max_len = 384, 8, 2, 32, 3, 64
+    k = rng.standard_normal((batch, kv_heads, max_len, dim)).astype(np.float16)
+    v = rng.standard_normal((batch, kv_heads, max_len, dim)).astype(np.float16)
+    q = rng.standard_normal((batch, heads, steps, dim)).astype(np.float32)
+    lengths = rng.integers(1, max_len - steps + 1, batch).astype(np.int64)
+    rows = np.arange(batch, dtype=np.int64)
+    from card_playing_gym_b200.cuda_decode import decode_attention
+
+    out = decode_attention(torch.from_numpy(q).cuda(), torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda(),
+                           torch.from_numpy(rows).cuda(), torch.from_numpy(lengths).cuda(), max_len, dim ** -0.5)
+    expected = oracle_attention(q, k.astype(np.float32), v.astype(np.float32), rows, lengths, max_len, dim ** -0.5,
+                                kv="fp16")
+    assert scaled_error(out.float().cpu().numpy(), expected) < ATTN_TOL["fp16"]
+
+
+@pytest.mark.parametrize("kv", ["fp32", "fp16", "bf16"])
+def test_kv_write_step_and_overlapping_copy_rows(kv):
+    from card_playing_gym_b200.kv_cache import KVCache
+
+    rng = np.random.default_rng(3)
+    layers, kvh, dim, capacity, max_len = 3, 2, 24, 12, 20
+    cache = KVCache(n_layers=layers, kv_heads=kvh, head_dim=dim, capacity=capacity, max_len=max_len, device="cuda",
+                    dtype=TORCH_DTYPES[kv])
+    ref = Cache(layers, capacity, kvh, max_len, dim, Precision(kv=kv))
+    rows = np.array([5, 1, 7, 2], dtype=np.int64)
+    for layer in range(layers):
+        positions = rng.integers(0, max_len - 3, (4, 1)) + np.arange(3)[None, :]
+        k_new = rng.standard_normal((4, kvh, 3, dim)).astype(np.float32)
+        v_new = rng.standard_normal((4, kvh, 3, dim)).astype(np.float32)
+        cache.write_step(layer, torch.from_numpy(rows).cuda(), torch.from_numpy(positions).cuda(),
+                         torch.from_numpy(k_new).cuda(), torch.from_numpy(v_new).cuda())
+        ref.write_step(layer, rows, positions, k_new, v_new)
+        cache.write_range(layer, None, 2, torch.from_numpy(k_new[:2]).cuda(), torch.from_numpy(v_new[:2]).cuda())
+        ref.write_range(layer, None, 2, k_new[:2], v_new[:2])
+    # Survivors slide down: row 2 is both a source and a target.
+    sources, targets = np.array([2, 5, 7]), np.array([1, 2, 3])
+    cache.copy_rows(torch.from_numpy(sources).cuda(), torch.from_numpy(targets).cuda(), 11)
+    ref.copy_rows(sources, targets, 11)
+    assert np.array_equal(cache.k_pool.float().cpu().numpy(), ref.k)
+    assert np.array_equal(cache.v_pool.float().cpu().numpy(), ref.v)
+
+
+def test_plump_field_lookup_matches_the_oracle():
+    from card_playing_gym_b200.config import PlumpModelConfig, synthetic_plump_actor_state
+    from card_playing_gym_b200.plump import PlumpActor
+
+    config = PlumpModelConfig()
+    state = synthetic_plump_actor_state(config, seed=9)
+    actor = PlumpActor(config, state, precision="fp32")
+    streams = load_golden("plump_streams")["tokens"]
+    tokens = torch.from_numpy(streams.astype(np.int64)).cuda()
+    x, ple, values = actor.embed(tokens)
+    ox, ople, ovalues = oplump.Embedding.from_state(state).forward(streams.astype(np.int64))
+    np.testing.assert_allclose(x.cpu().numpy(), ox, atol=2e-6, rtol=0)
+    np.testing.assert_allclose(ple.cpu().numpy(), ople, atol=2e-6, rtol=0)
+    np.testing.assert_allclose(values.cpu().numpy(), ovalues, atol=2e-6, rtol=0)
+    # int16 tokens (the collector's storage) give the same sums
+    x16, _, _ = actor.embed(torch.from_numpy(streams).cuda())
+    assert torch.equal(x16, x)
+
+
+@pytest.mark.parametrize("width", (11, 52, 64))
+def test_masked_sampling_matches_the_reference(width):
+    from card_playing_gym_b200.sampling import masked_sample
+
+    data = load_golden("sampling")
+    logits, mask, uniforms = data[f"w{width}_logits"], data[f"w{width}_mask"], data[f"w{width}_uniforms"]
+    probs, actions = masked_sample(torch.from_numpy(logits).cuda(), torch.from_numpy(mask).cuda(),
+                                   torch.from_numpy(uniforms).cuda())
+    probs, actions = probs.cpu().numpy(), actions.cpu().numpy()
+    expected = data[f"w{width}_probs"]
+    # numpy's float32 exp is within ~2.4 ulp of exact; the kernel's is correctly rounded.
+    np.testing.assert_allclose(probs, expected, rtol=2e-6, atol=1e-12)
+    assert (probs[~mask] == 0).all()
+    assert mask[np.arange(len(actions)), actions].all()
+    differ = actions != data[f"w{width}_actions"]
+    near = oppo.boundary_distance(expected, uniforms) < 1e-6
+    assert not (differ & ~near).any(), "draws differ away from a CDF step"
+    assert differ.sum() <= max(1, len(actions) // 1000)
+
+
+def test_gae_segments_are_bit_exact():
+    from card_playing_gym_b200.ppo import gae_advantages, segmented_gae
+
+    data = load_golden("gae")
+    for lam in (0.0, 0.95, 1.0):
+        adv = segmented_gae(torch.from_numpy(data["values"]).cuda(), torch.from_numpy(data["seats"]).cuda(),
+                            torch.from_numpy(data["starts"]).cuda(), torch.from_numpy(data["returns"]).cuda(), lam)
+        assert np.array_equal(adv.cpu().numpy(), data[f"adv_{lam}"])
+    # the reference's known answers (tests/rl/test_rl.py:58-64)
+    values = torch.tensor([[1.0, -1.0], [3.0, -3.0], [2.0, -2.0]], dtype=torch.float64).cuda()
+    returns = torch.tensor([5.0, -5.0], dtype=torch.float64).cuda()
+    torch.testing.assert_close(gae_advantages(values, returns, 1.0), returns - values)
+    one = gae_advantages(values, returns, 0.0)
+    torch.testing.assert_close(one[0], values[1] - values[0])
+
+
+def test_weighted_mean_std_and_normalize():
+    from card_playing_gym_b200.ppo import normalize_, weighted_mean_std
+
+    rng = np.random.default_rng(5)
+    values = rng.standard_normal(100_003)
+    weights = rng.random(100_003)
+    mean, std = weighted_mean_std(torch.from_numpy(values).cuda(), torch.from_numpy(weights).cuda())
+    emean, estd = oppo.weighted_mean_std(values, weights)
+    assert mean == pytest.approx(emean, rel=1e-12, abs=1e-15) and std == pytest.approx(estd, rel=1e-12)
+    device = torch.from_numpy(values.copy()).cuda()
+    normalize_(device, emean, estd)
+    assert np.array_equal(device.cpu().numpy(), (values - emean) / estd)
+    assert weighted_mean_std(torch.zeros(4).cuda(), torch.zeros(4).cuda()) == (0.0, 1.0)
+
+
+def test_ppo_objective_matches_the_reference_autograd():
+    from card_playing_gym_b200.ppo import TOTAL_KEYS, policy_objective, ppo_terms
+
+    data = load_golden("ppo")
+    cuda = {k: torch.from_numpy(data[k]).cuda() for k in ("logits", "old_probs", "actions", "advantages", "weights")}
+    logits = cuda["logits"].clone().requires_grad_()
+    objective, totals = policy_objective(logits, cuda["old_probs"], cuda["actions"], cuda["advantages"],
+                                         cuda["weights"], clip_ratio=float(data["clip"]), alpha=float(data["alpha"]))
+    objective.backward()
+    assert objective.item() == pytest.approx(float(data["objective"]), rel=1e-5, abs=1e-7)
+    np.testing.assert_allclose(logits.grad.cpu().numpy(), data["grad"], rtol=1e-4, atol=1e-8)
+    totals = dict(zip(TOTAL_KEYS, totals.tolist()))
+    w = data["weights"].astype(np.float64)
+    assert totals["policy_loss"] == pytest.approx(float((w * data["losses"]).sum()), rel=1e-5)
+    assert totals["row_weight"] == pytest.approx(float(w.sum()), rel=1e-6)
+    assert totals["behavior_kl"] == pytest.approx(float((w * data["divergences"]).sum()), rel=1e-4, abs=1e-9)
+    terms = ppo_terms(cuda["logits"], cuda["old_probs"], cuda["actions"], cuda["advantages"],
+                      clip_ratio=float(data["clip"]))
+    for key in ("losses", "divergences", "entropy", "normalized_entropy", "ratios"):
+        np.testing.assert_allclose(getattr(terms, key).cpu().numpy(), data[key], rtol=1e-5, atol=1e-6, err_msg=key)
+    assert np.array_equal(terms.entropy_eligible.cpu().numpy(), data["entropy_eligible"])
+    assert np.array_equal(terms.clipped.cpu().numpy(), data["clipped"])
+
+
+def test_value_loss_matches_the_reference_autograd():
+    from card_playing_gym_b200.ppo import value_loss
+
+    data = load_golden("value_loss")
+    prediction = torch.from_numpy(data["prediction"]).cuda().requires_grad_()
+    loss, totals = value_loss(prediction, torch.from_numpy(data["players"]).cuda(),
+                              torch.from_numpy(data["returns"]).cuda(), torch.from_numpy(data["weight"]).cuda(),
+                              float(data["scale"]))
+    loss.backward()
+    assert loss.item() == pytest.approx(float(data["loss"]), rel=1e-5)
+    assert totals[1].item() == pytest.approx(float(data["squared_error"]), rel=1e-5)
+    np.testing.assert_allclose(prediction.grad.cpu().numpy(), data["grad"], rtol=1e-4, atol=1e-9)
+
+
+def test_no_kernel_fault_was_recorded():
+    from card_playing_gym_b200 import _native as nat
+
+    assert nat.fault_status() == 0

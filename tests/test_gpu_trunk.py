@@ -1,0 +1,167 @@
+"""Model-level parity: the B200 ragged decode against the oracle and the reference's own outputs (B200 only).
+
+The reference fixtures hold the reference's fp32 outputs for prefill + ragged waves
+(tests/golden/make_golden.py), and its own bf16-autocast / fp16-KV outputs on the same
+waves, whose deviation from fp32 is the accuracy bar for the B200 bf16 mode.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from card_playing_gym_b200.config import PlumpModelConfig, synthetic_plump_actor_state
+from oracle import plump as oplump
+from oracle import ppo as oppo
+from oracle.trunk import Precision
+from tests.conftest import trunk_fixture
+
+pytestmark = pytest.mark.gpu
+
+TRUNKS = ("tiny_div", "tiny_cat", "rlv6")
+# fp32 mode: hidden states are LayerNorm outputs (O(1)); fp32 summation-order noise over
+# 16 layers stays well below this.
+FP32_ATOL = 5e-5
+
+
+def make_actor(name: str, precision: str):
+    from card_playing_gym_b200.plump import PlumpActor
+
+    data, config = trunk_fixture(name)
+    model = PlumpModelConfig(**config)
+    state = synthetic_plump_actor_state(model, seed=int(data["seed"]))
+    return data, config, state, PlumpActor(model, state, precision=precision)
+
+
+def run_waves(actor, data, kv_dtype):
+    """Prefill then every ragged wave of the fixture; yields (wave, hidden, live rows)."""
+
+    tokens = torch.from_numpy(data["tokens"].astype(np.int64)).cuda()
+    lengths = data["lengths"]
+    prefix = int(data["prefix"])
+    cache = actor.new_cache(len(lengths), int(lengths.max()) + 1, kv_dtype)
+    hidden = actor.forward_prefill(tokens[:, :prefix], cache, None)
+    yield -1, hidden, np.ones(len(lengths), dtype=bool)
+    for wave in range(int(data["n_waves"])):
+        hidden = actor.forward_ragged(
+            torch.from_numpy(data[f"wave{wave}_tokens"]).cuda(),
+            torch.from_numpy(data[f"wave{wave}_positions"]).cuda(),
+            cache,
+            torch.from_numpy(data[f"wave{wave}_offsets"]).cuda(),
+        )
+        yield wave, hidden, data[f"wave{wave}_counts"] > 0
+
+
+@pytest.mark.parametrize("name", TRUNKS)
+def test_fp32_ragged_decode_matches_the_reference(name):
+    data, _, _, actor = make_actor(name, "fp32")
+    worst = 0.0
+    for wave, hidden, live in run_waves(actor, data, torch.float32):
+        got = hidden.cpu().numpy()
+        expected = data["prefill_hidden"] if wave < 0 else data[f"wave{wave}_hidden"]
+        worst = max(worst, float(np.abs(got[live] - expected[live]).max()))
+        if wave >= 0:
+            card = actor.policy_logits(hidden, "play").cpu().numpy()
+            np.testing.assert_allclose(card[live], data[f"wave{wave}_card"][live], atol=FP32_ATOL, rtol=1e-5)
+            values = actor.player_values(hidden).cpu().numpy()
+            np.testing.assert_allclose(values[live], data[f"wave{wave}_values"][live], atol=FP32_ATOL, rtol=1e-5)
+    assert worst < FP32_ATOL, worst
+
+
+@pytest.mark.parametrize("name", TRUNKS)
+def test_fp32_ragged_decode_with_gathered_rows(name):
+    """Explicit ``rows`` (the continuous collector's gathered cache rows) give the same outputs."""
+
+    data, _, _, actor = make_actor(name, "fp32")
+    lengths = data["lengths"]
+    batch = len(lengths)
+    rows = torch.arange(batch, device="cuda") * 3 + 1  # scattered rows of a larger pool
+    tokens = torch.from_numpy(data["tokens"].astype(np.int64)).cuda()
+    prefix = int(data["prefix"])
+    cache = actor.new_cache(3 * batch + 1, int(lengths.max()) + 1, torch.float32)
+    actor.forward_prefill(tokens[:, :prefix], cache, rows)
+    for wave in range(int(data["n_waves"])):
+        hidden = actor.forward_ragged(
+            torch.from_numpy(data[f"wave{wave}_tokens"]).cuda(), torch.from_numpy(data[f"wave{wave}_positions"]).cuda(),
+            cache, torch.from_numpy(data[f"wave{wave}_offsets"]).cuda(), rows=rows,
+        )
+        live = data[f"wave{wave}_counts"] > 0
+        np.testing.assert_allclose(hidden.cpu().numpy()[live], data[f"wave{wave}_hidden"][live], atol=FP32_ATOL, rtol=0)
+
+
+@pytest.mark.parametrize("name", TRUNKS)
+@pytest.mark.parametrize("kv", ["fp16", "bf16"])
+def test_bf16_ragged_decode_tracks_the_oracle_and_beats_reference_bf16_error(name, kv):
+    """bf16 GEMM operands, 16-bit KV.
+
+    (1) Against the oracle evaluated at the same rounding points (bf16 GEMM operands,
+    KV/Q/probabilities in the cache dtype): max |error| / max |value| below 1e-2 on
+    hidden states and play logits (the kernels differ from it only in fp32 summation
+    order, which can flip a bf16 rounding).
+    (2) Against the reference's fp32 outputs: no worse than twice the reference's own
+    bf16-autocast / fp16-KV rollout error on the same waves.
+    """
+
+    data, config, state, actor = make_actor(name, "bf16")
+    oracle = oplump.PlumpActor(state, config, Precision(gemm="bf16", kv=kv))
+    tokens = data["tokens"].astype(np.int64)
+    lengths = data["lengths"]
+    ocache = oracle.new_cache(len(lengths), int(lengths.max()) + 1)
+    prefix = int(data["prefix"])
+    # The B200 prefill is a ragged append of the whole prefix at length 0; so is the oracle's here.
+    oracle.forward_ragged(tokens[:, :prefix], np.zeros(len(lengths), np.int64), ocache,
+                          np.full(len(lengths), prefix - 1), span=prefix)
+    mine_err, ref_err = 0.0, 0.0
+    for wave, hidden, live in run_waves(actor, data, getattr(torch, {"fp16": "float16", "bf16": "bfloat16"}[kv])):
+        if wave < 0:
+            continue
+        expected = oracle.forward_ragged(data[f"wave{wave}_tokens"].astype(np.int64), data[f"wave{wave}_positions"],
+                                         ocache, data[f"wave{wave}_offsets"])
+        got = hidden.cpu().numpy()
+        scale = np.abs(expected[live]).max()
+        assert np.abs(got[live] - expected[live]).max() / scale < 1e-2
+        card = actor.policy_logits(hidden, "play").cpu().numpy()
+        ocard = oracle.heads.policy_logits(expected, "play")
+        assert np.abs(card[live] - ocard[live]).max() / np.abs(ocard[live]).max() < 1e-2
+        reference = data[f"wave{wave}_card"][live]
+        mine_err = max(mine_err, float(np.abs(card[live] - reference).max()))
+        ref_err = max(ref_err, float(np.abs(data[f"wave{wave}_bf16_card"][live] - reference).max()))
+    assert mine_err <= 2.0 * ref_err + 1e-4, (mine_err, ref_err)
+
+
+def test_decide_matches_the_oracle_heads_and_sampler():
+    from card_playing_gym_b200.plump import PlumpActor
+
+    config = PlumpModelConfig()
+    state = synthetic_plump_actor_state(config, seed=21)
+    actor = PlumpActor(config, state, precision="fp32")
+    heads = oplump.Heads.from_state(state)
+    rng = np.random.default_rng(4)
+    count = 4096
+    hidden = rng.standard_normal((count, config.d_model)).astype(np.float32)
+    which = rng.integers(0, 2, count).astype(np.int32)
+    legal = rng.random((count, 52)) < 0.3
+    legal[np.arange(count), rng.integers(0, 11, count)] = True
+    legal[which == 0, 11:] = False
+    uniforms = rng.random(count)
+    logits, probs, actions, values = actor.decide(
+        torch.from_numpy(hidden).cuda(), torch.from_numpy(which).cuda(), torch.from_numpy(legal).cuda(),
+        torch.from_numpy(uniforms).cuda(),
+    )
+    logits, probs, actions = logits.cpu().numpy(), probs.cpu().numpy(), actions.cpu().numpy()
+    h64 = hidden.astype(np.float64)
+    for head, width in ((0, 11), (1, 52)):
+        rows = which == head
+        expected = heads.policy_logits(h64[rows], ("bid", "play")[head])
+        np.testing.assert_allclose(logits[rows, :width], expected, atol=2e-5, rtol=1e-5)
+        # The reference samples on the host from these same logits (selfplay.py:539-548).
+        mask = legal[rows, :width]
+        host = oppo.masked_probabilities(logits[rows, :width], mask)
+        np.testing.assert_allclose(probs[rows, :width], host, rtol=2e-6, atol=1e-12)
+        drawn = oppo.sample_rows(host, mask, uniforms[rows])
+        differ = actions[rows] != drawn
+        near = oppo.boundary_distance(host, uniforms[rows]) < 1e-6
+        assert not (differ & ~near).any()
+        assert mask[np.arange(mask.shape[0]), actions[rows]].all()
+    np.testing.assert_allclose(values.cpu().numpy(), heads.player_values(h64), atol=2e-5, rtol=1e-5)
