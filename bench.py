@@ -355,7 +355,7 @@ def run_b200(args) -> int:
     e2e_value = world_size * games * args.steps / (e2e_ms / 1000.0)
 
     if rank == 0:
-        head_dim = RL_V6.head_dim
+        head_dim = RL_V6.trunk().head_dim
         esize = torch.tensor([], dtype=kv_dtype).element_size()
         keys = np.minimum(wave["positions"] + 1, span).sum()  # T = 1: key_length = position + 1
         kv_bytes = float(keys) * RL_V6.n_kv_heads * head_dim * esize * 2
