@@ -82,7 +82,11 @@ __global__ void __launch_bounds__(128) attn_simt_kernel(AttnParams p) {
 #pragma unroll
     for (int i = 0; i < kSimtMaxDim / 32; ++i) {
       const int d = lane + 32 * i;
-      if (d < D) store_from_float(p.out, ooff + d, p.out_dtype, acc[i] * inv);
+      if (d >= D) continue;
+      if (p.out_blocked)
+        store_from_float(p.out, blocked_offset(b * p.steps + t, h * D + d, p.blocked_width), p.out_dtype, acc[i] * inv);
+      else
+        store_from_float(p.out, ooff + d, p.out_dtype, acc[i] * inv);
     }
   }
 }
@@ -205,6 +209,18 @@ struct TcShape {
   static constexpr int kWarpBytes = kStages * 2 * kStageElems * static_cast<int>(sizeof(KV));
 };
 
+// Rows with no visible key get a zero output.
+__device__ void zero_unit(const AttnParams& p, int64_t b, int kvh, int M, int lane) {
+  const int D = p.head_dim;
+  for (int i = lane; i < M * D; i += 32) {
+    const int m = i / D, d = i % D;
+    const int h = kvh * p.group + m / p.steps, t = m % p.steps;
+    const int64_t off = p.out_blocked ? blocked_offset(b * p.steps + t, h * D + d, p.blocked_width)
+                                      : b * p.o_sb + h * p.o_sh + t * p.o_st + d;
+    store_from_float(p.out, off, p.out_dtype, 0.f);
+  }
+}
+
 template <typename KV, int D>
 __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
   using Shape = TcShape<KV, D>;
@@ -261,11 +277,7 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
     // No visible key: the output is defined as zero.
     const int64_t b = unit / p.kv_heads;
     const int kvh = static_cast<int>(unit % p.kv_heads);
-    for (int i = lane; i < M * D; i += 32) {
-      const int m = i / D, d = i % D;
-      const int h = kvh * p.group + m / p.steps, t = m % p.steps;
-      store_from_float(p.out, b * p.o_sb + h * p.o_sh + t * p.o_st + d, p.out_dtype, 0.f);
-    }
+    zero_unit(p, b, kvh, M, lane);
     unit += stride;
   }
   if (unit >= units) return;
@@ -289,11 +301,7 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
       while (next_unit < units && (next_keys = unit_keys(next_unit)) <= 0) {
         const int64_t b = next_unit / p.kv_heads;
         const int kvh = static_cast<int>(next_unit % p.kv_heads);
-        for (int i = lane; i < M * D; i += 32) {
-          const int m = i / D, d = i % D;
-          const int h = kvh * p.group + m / p.steps, t = m % p.steps;
-          store_from_float(p.out, b * p.o_sb + h * p.o_sh + t * p.o_st + d, p.out_dtype, 0.f);
-        }
+        zero_unit(p, b, kvh, M, lane);
         next_unit += stride;
       }
     }
@@ -454,8 +462,15 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
 #pragma unroll
           for (int j = 0; j < Shape::kDTiles; ++j) {
             const int d = j * 8 + 2 * tid4;
-            store_from_float(p.out, ooff + d, p.out_dtype, o[j][2 * r] * inv);
-            store_from_float(p.out, ooff + d + 1, p.out_dtype, o[j][2 * r + 1] * inv);
+            if (p.out_blocked) {
+              // even column pair inside one 8-column chunk: one 32-bit store of two bf16
+              const int64_t off = blocked_offset(b * p.steps + t, h * D + d, p.blocked_width);
+              *reinterpret_cast<__nv_bfloat162*>(static_cast<__nv_bfloat16*>(p.out) + off) =
+                  __floats2bfloat162_rn(o[j][2 * r] * inv, o[j][2 * r + 1] * inv);
+            } else {
+              store_from_float(p.out, ooff + d, p.out_dtype, o[j][2 * r] * inv);
+              store_from_float(p.out, ooff + d + 1, p.out_dtype, o[j][2 * r + 1] * inv);
+            }
           }
         }
       }
@@ -561,6 +576,8 @@ int run_attention_kernels(const AttnParams& p, cudaStream_t stream);
 
 int run_attention(const AttnParams& p, cudaStream_t stream) {
   if (p.batch == 0) return CG_OK;
+  if (p.out_blocked && (p.out_dtype != CG_BF16 || p.blocked_width != p.heads * p.head_dim || p.blocked_width % 8))
+    return set_error(CG_ERR_ARGUMENT, "blocked attention output must be bf16 with width heads*head_dim (multiple of 8)");
   const bool record = g_profile.enabled && g_profile.count < g_profile.capacity;
   if (record) cudaEventRecord(g_profile.start[g_profile.count], stream);
   const int rc = run_attention_kernels(p, stream);

@@ -14,7 +14,9 @@ int forward_ragged_impl(const cg_trunk_dims* dims_p, const void* blob, const flo
                         const float* values, int64_t batch, int steps, const int64_t* positions,
                         const int64_t* readout_offsets, const int64_t* rows, int span, void* k_pool, void* v_pool,
                         int kv_dtype, int64_t capacity, int max_len, int precision, void* workspace,
-                        int64_t workspace_bytes, float* hidden_out, cudaStream_t s, bool x_in_workspace);
+                        int64_t workspace_bytes, float* hidden_out, cudaStream_t s, bool x_in_workspace,
+                        const float* lookup, int lookup_width);
+bool tc_layers_available(const cg_trunk_dims& dims);
 
 namespace {
 constexpr int64_t kAlign = 256;
@@ -193,10 +195,16 @@ extern "C" int cg_plump_forward_ragged(const cg_trunk_dims* dims, const void* bl
   const int val_w = value_layer_count(*dims) * dims->n_kv_heads * head_dim(*dims);
   const int width = dims->d_model + ple_w + val_w;
   if ((rc = embed(*schema, table, width, tokens, token_dtype, nt, w.lookup, s))) return rc;
+  if (precision == CG_PREC_BF16 && tc_layers_available(*dims)) {
+    // The tensor-core path conditions the raw lookup inside its first kernel.
+    return forward_ragged_impl(dims, blob, nullptr, nullptr, nullptr, batch, steps, positions, readout_offsets, rows,
+                               span, k_pool, v_pool, kv_dtype, capacity, max_len, precision, w.step, w.step_bytes,
+                               hidden_out, s, false, w.lookup, width);
+  }
   // The residual stream x is the first buffer of the step workspace.
   float* x = reinterpret_cast<float*>(w.step);
   if ((rc = cg_trunk_condition(dims, blob, w.lookup, nt, x, w.ple, w.values, precision, s))) return rc;
   return forward_ragged_impl(dims, blob, x, w.ple, w.values, batch, steps, positions, readout_offsets, rows, span,
                              k_pool, v_pool, kv_dtype, capacity, max_len, precision, w.step, w.step_bytes, hidden_out, s,
-                             true);
+                             true, nullptr, 0);
 }

@@ -9,10 +9,11 @@
 
 namespace cg {
 
-int run_tc_layers(const cg_trunk_dims& dims, const void* blob, const BlobLayout& L, int64_t batch, int steps,
-                  const int64_t* positions, const int64_t* key_lengths, const int64_t* rows, int span, void* k_pool,
-                  void* v_pool, int kv_dtype, int64_t capacity, int max_len, float* x, const float* ple,
-                  const float* values, unsigned char* scratch, int64_t scratch_bytes, cudaStream_t stream);
+int run_tc_forward(const cg_trunk_dims& dims, const void* blob, const BlobLayout& L, int64_t batch, int steps,
+                   const int64_t* positions, const int64_t* key_lengths, const int64_t* rows, int span, void* k_pool,
+                   void* v_pool, int kv_dtype, int64_t capacity, int max_len, const float* lookup, int lookup_width,
+                   const float* x_in, const float* ple_in, const float* val_in, unsigned char* scratch,
+                   int64_t scratch_bytes, const int64_t* readout_offsets, float* hidden_out, cudaStream_t s);
 int64_t tc_layers_scratch_bytes(const cg_trunk_dims& dims, int64_t batch, int steps);
 bool tc_layers_available(const cg_trunk_dims& dims);
 int tc_pack(const cg_trunk_dims& dims, void* blob, const BlobLayout& L, cudaStream_t stream);
@@ -368,11 +369,15 @@ int run_fp32_layers(const cg_trunk_dims& dims, const void* blob, const BlobLayou
   return CG_OK;
 }
 
+// The layer loop from either conditioned inputs (x_in, ple, values) or, on the tensor-core
+// path, the raw field lookup (lookup != nullptr: conditioning runs inside the first kernel).
+// x_in_workspace: x_in already is the step workspace's residual buffer (fp32 path only).
 int forward_ragged_impl(const cg_trunk_dims* dims_p, const void* blob, const float* x_in, const float* ple,
                         const float* values, int64_t batch, int steps, const int64_t* positions,
                         const int64_t* readout_offsets, const int64_t* rows, int span, void* k_pool, void* v_pool,
                         int kv_dtype, int64_t capacity, int max_len, int precision, void* workspace,
-                        int64_t workspace_bytes, float* hidden_out, cudaStream_t s, bool x_in_workspace) {
+                        int64_t workspace_bytes, float* hidden_out, cudaStream_t s, bool x_in_workspace,
+                        const float* lookup, int lookup_width) {
   int rc;
   if ((rc = check_dims(dims_p))) return rc;
   const cg_trunk_dims& dims = *dims_p;
@@ -382,8 +387,8 @@ int forward_ragged_impl(const cg_trunk_dims* dims_p, const void* blob, const flo
   CG_REQUIRE(max_len > 0 && capacity > 0, "bad pool shape");
   if (batch == 0) return CG_OK;
   CG_REQUIRE(blob && positions && readout_offsets && k_pool && v_pool && hidden_out && workspace, "NULL pointer");
-  CG_REQUIRE(!dims.per_layer_dim || ple, "this trunk expects a per-layer embedding lookup");
-  CG_REQUIRE(!dims.value_layers || values, "this trunk expects a value-embedding lookup");
+  CG_REQUIRE(lookup || !dims.per_layer_dim || ple, "this trunk expects a per-layer embedding lookup");
+  CG_REQUIRE(lookup || !dims.value_layers || values, "this trunk expects a value-embedding lookup");
   if (span > max_len) span = max_len;
   StepWorkspace w = plan_step(dims, batch, steps, precision, static_cast<unsigned char*>(workspace));
   if (workspace_bytes < w.total)
@@ -391,19 +396,20 @@ int forward_ragged_impl(const cg_trunk_dims* dims_p, const void* blob, const flo
                      (long long)w.total);
   const BlobLayout L = blob_layout(dims);
   const int64_t nt = batch * steps;
+  key_lengths_kernel<<<static_cast<unsigned>((batch + 255) / 256), 256, 0, s>>>(positions, w.key_lengths, batch);
+  if ((rc = check_launch("key_lengths_kernel"))) return rc;
+  if (precision == CG_PREC_BF16 && tc_layers_available(dims)) {
+    return run_tc_forward(dims, blob, L, batch, steps, positions, w.key_lengths, rows, span, k_pool, v_pool, kv_dtype,
+                          capacity, max_len, lookup, lookup_width, x_in, ple, values, w.tc, w.tc_bytes,
+                          readout_offsets, hidden_out, s);
+  }
+  CG_REQUIRE(!lookup, "internal: the CUDA-core path takes conditioned inputs");
   if (!x_in_workspace) {
     cudaError_t err = cudaMemcpyAsync(w.x, x_in, nt * dims.d_model * sizeof(float), cudaMemcpyDeviceToDevice, s);
     if (err != cudaSuccess) return set_error(CG_ERR_CUDA, "copy x: %s", cudaGetErrorString(err));
   }
-  key_lengths_kernel<<<static_cast<unsigned>((batch + 255) / 256), 256, 0, s>>>(positions, w.key_lengths, batch);
-  if ((rc = check_launch("key_lengths_kernel"))) return rc;
-  if (precision == CG_PREC_FP32 || !tc_layers_available(dims)) {
-    rc = run_fp32_layers(dims, blob, L, batch, steps, positions, rows, span, k_pool, v_pool, kv_dtype, capacity,
-                         max_len, ple, values, w, precision == CG_PREC_BF16, s);
-  } else {
-    rc = run_tc_layers(dims, blob, L, batch, steps, positions, w.key_lengths, rows, span, k_pool, v_pool, kv_dtype,
-                       capacity, max_len, w.x, ple, values, w.tc, w.tc_bytes, s);
-  }
+  rc = run_fp32_layers(dims, blob, L, batch, steps, positions, rows, span, k_pool, v_pool, kv_dtype, capacity,
+                       max_len, ple, values, w, precision == CG_PREC_BF16, s);
   if (rc) return rc;
   // final LayerNorm at each row's readout token only (trunk.py:429)
   return norm(w.x, dims.d_model, part(blob, L, CG_PART_FINAL_W, 0), part(blob, L, CG_PART_FINAL_B, 0), hidden_out,
@@ -454,7 +460,7 @@ extern "C" int cg_trunk_forward_ragged(const cg_trunk_dims* dims, const void* bl
   if (batch > 0 && !x) return cg::set_error(CG_ERR_ARGUMENT, "cg_trunk_forward_ragged: NULL x");
   return cg::forward_ragged_impl(dims, blob, x, ple, values, batch, steps, positions, readout_offsets, rows, span,
                                  k_pool, v_pool, kv_dtype, capacity, max_len, precision, workspace, workspace_bytes,
-                                 hidden_out, static_cast<cudaStream_t>(stream), false);
+                                 hidden_out, static_cast<cudaStream_t>(stream), false, nullptr, 0);
 }
 
 extern "C" int cg_trunk_condition(const cg_trunk_dims* dims_p, const void* blob, const float* lookup, int64_t n,

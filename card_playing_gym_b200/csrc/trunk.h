@@ -21,7 +21,16 @@ struct AttnParams {
   void* out;
   int out_dtype;
   int64_t o_sb, o_sh, o_st;
+  // out_blocked: write the output as the next GEMM's operand, tile-blocked bf16: element
+  // (row-token r = b*T + t, column k = h*D + d) at ((r/128) * W/8 + k/8) * 1024 + (r%128) * 8 + k%8,
+  // W = blocked_width (= heads * head_dim).
+  int out_blocked;
+  int blocked_width;
 };
+
+__host__ __device__ inline int64_t blocked_offset(int64_t r, int k, int width) {
+  return ((r / 128) * (width / 8) + k / 8) * 1024 + (r % 128) * 8 + (k % 8);
+}
 
 int run_attention(const AttnParams& p, cudaStream_t stream);
 

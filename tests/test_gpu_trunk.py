@@ -165,3 +165,38 @@ def test_decide_matches_the_oracle_heads_and_sampler():
         assert not (differ & ~near).any()
         assert mask[np.arange(mask.shape[0]), actions[rows]].all()
     np.testing.assert_allclose(values.cpu().numpy(), heads.player_values(h64), atol=2e-5, rtol=1e-5)
+
+
+@pytest.mark.parametrize("precision,kv", [("fp32", "fp32"), ("bf16", "fp16")])
+def test_trunk_forward_ragged_from_conditioned_inputs(precision, kv):
+    """Trunk.forward_ragged's own signature (trunk.py:391-429): x, ple, values from Trunk.condition."""
+
+    from card_playing_gym_b200.trunk import B200Trunk
+
+    data, config, state, _ = make_actor("rlv6", "fp32")
+    model = PlumpModelConfig(**config)
+    trunk = B200Trunk(model.trunk(), state, precision=precision)
+    oracle = oplump.PlumpActor(state, config, Precision(gemm=precision, kv=kv))
+    rng = np.random.default_rng(8)
+    streams = data["tokens"].astype(np.int64)
+    batch = streams.shape[0]
+    prefix = int(data["prefix"])
+    lookup = oracle.embedding.forward(streams[:, : prefix + 2])
+    x, ple, values = oracle.trunk.condition(*lookup)
+    dtype = {"fp32": torch.float32, "fp16": torch.float16}[kv]
+    cache = trunk.new_cache(batch, 64, dtype)
+    ocache = oracle.new_cache(batch, 64)
+    cuda = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).cuda()  # noqa: E731
+    trunk.forward_ragged(cuda(x[:, :prefix]), cuda(ple[:, :prefix]), cuda(values[:, :prefix]), cache,
+                         torch.zeros(batch, dtype=torch.int64, device="cuda"),
+                         torch.full((batch,), prefix - 1, dtype=torch.int64, device="cuda"), span=prefix)
+    oracle.trunk.forward_ragged(x[:, :prefix], ple[:, :prefix], values[:, :prefix], ocache,
+                                np.zeros(batch, np.int64), np.full(batch, prefix - 1), span=prefix)
+    positions = np.full(batch, prefix, np.int64)
+    offsets = rng.integers(0, 2, batch)
+    hidden = trunk.forward_ragged(cuda(x[:, prefix:]), cuda(ple[:, prefix:]), cuda(values[:, prefix:]), cache,
+                                  torch.from_numpy(positions).cuda(), torch.from_numpy(offsets).cuda())
+    expected = oracle.trunk.forward_ragged(x[:, prefix:], ple[:, prefix:], values[:, prefix:], ocache, positions,
+                                           offsets)
+    error = np.abs(hidden.cpu().numpy() - expected).max() / np.abs(expected).max()
+    assert error < (FP32_ATOL if precision == "fp32" else 1e-2), error
