@@ -147,6 +147,22 @@ __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32
       : "memory");
 }
 
+// The KV stream is read once per layer: evict it from L2 first so that weights stay resident.
+__device__ __forceinline__ void bulk_copy_g2s_stream(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                                     uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ uint64_t evict_first_policy() {
+  uint64_t policy;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+  return policy;
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 template <typename T>
@@ -265,8 +281,9 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
       const int64_t off = row * p.kv_row + kvh * p.kv_head + static_cast<int64_t>(first) * p.kv_pos;
       KV* ks = stage_base + stage * 2 * Shape::kStageElems;
       mbar_expect_tx(&bars[wib][stage], 2 * bytes);
-      bulk_copy_g2s(ks, static_cast<const KV*>(p.k) + off, bytes, &bars[wib][stage]);
-      bulk_copy_g2s(ks + Shape::kStageElems, static_cast<const KV*>(p.v) + off, bytes, &bars[wib][stage]);
+      const uint64_t policy = evict_first_policy();
+      bulk_copy_g2s_stream(ks, static_cast<const KV*>(p.k) + off, bytes, &bars[wib][stage], policy);
+      bulk_copy_g2s_stream(ks + Shape::kStageElems, static_cast<const KV*>(p.v) + off, bytes, &bars[wib][stage], policy);
     }
   };
 

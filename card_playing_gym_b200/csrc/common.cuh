@@ -6,7 +6,7 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
-#include "../../include/cg_b200.h"
+#include "cg_b200.h"
 
 namespace cg {
 

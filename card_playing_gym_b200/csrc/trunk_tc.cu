@@ -9,11 +9,12 @@
 //   attention(l) output -> out_proj -> x += . -> LN -> up (d-wide chunks) -> GELU ->
 //   down (accumulated over the chunks) -> x += . + b -> x += PLE(l) -> LN -> QKV(l+1)
 //   -> q for attention(l+1), K/V appended to the pool.
-// Roles: warps 0-3 are epilogue warps (thread t owns row t = TMEM lane t); warp 4's
-// lane 0 streams weight K-slices into a ring of shared-memory stages with bulk async
-// copies; warp 5 allocates tensor memory and its lane 0 issues tcgen05.mma (M=128,
-// bf16 x bf16 -> fp32 in TMEM). The GEMM weights are pre-packed (tc_pack) so each
-// K=16 slice is one contiguous bulk copy already in the canonical operand layout.
+// Roles: warps 0-11 are epilogue warps (three threads per row, each holding a third of
+// the row's columns); warp 12's lane 0 streams weight K-slices into a ring of 32 KB
+// shared-memory stages with bulk async copies; warp 13 allocates tensor memory and its
+// lane 0 issues tcgen05.mma (M=128, bf16 x bf16 -> fp32 in TMEM). The GEMM weights are
+// pre-packed (tc_pack) so consecutive K=16 slices of a GEMM step are contiguous and
+// already in the canonical operand layout.
 //
 // Activations between kernels live in a tile-blocked layout so that thread-per-row
 // access is coalesced: element (row r, column k) of an fp32 [rows, width] array sits
@@ -28,10 +29,11 @@
 namespace cg {
 
 constexpr int kTile = 128;
-constexpr int kTcThreads = 192;
+constexpr int kTcThreads = 14 * 32;  // 12 epilogue warps + producer warp + MMA warp
 constexpr int kMaxOps = 16;
-constexpr int kMaxStages = 8;
-constexpr int kSmemBudget = 225 * 1024;
+constexpr int kMaxStages = 16;
+constexpr int kStageTarget = 32 * 1024;  // bytes per ring stage (one bulk copy)
+constexpr int kSmemBudget = 222 * 1024;  // dynamic shared memory; the static barriers and reductions need the rest of 227 KB
 
 enum TcMode { kLayer = 0, kFirstLookup = 1, kFirstConditioned = 2 };
 
@@ -39,6 +41,7 @@ struct GemmOp {
   const __nv_bfloat16* w;  // packed K-slices: ksteps x [n rows x 16 columns]
   int n;
   int ksteps;
+  int ks_per_stage;  // consecutive K-slices carried by one ring stage (one bulk copy)
   int tmem_col;
   int a_src;  // 0: A buffer, 1: H buffer
   int accumulate_first;
@@ -49,7 +52,7 @@ struct GemmOp {
 struct TcParams {
   int mode, layer, qkv_layer, has_next;
   GemmOp ops[kMaxOps];
-  int n_ops, stages, stage_bytes;
+  int n_ops, n_ple_ops, stages, stage_bytes;
   int d, f, H, KVH, D, L, P, nv, kvw, qw;
   int64_t nt, ntiles;
   int T;
@@ -117,37 +120,81 @@ __device__ __forceinline__ void store_operand16(unsigned char* buf, int col, int
   }
 }
 
-// LayerNorm (eps 1e-5, biased variance, two passes) of row t of the blocked x into the A buffer.
-__device__ void layer_norm_to_operand(const float* x, int64_t tile, int d, int t, const float* w, const float* b,
-                                      unsigned char* abuf) {
-  float v[16];
-  float sum = 0.f;
-  for (int col = 0; col < d; col += 16) {
-    load16(x, tile, d, col, t, v);
+// ---- epilogue geometry ---------------------------------------------------------------------------------
+// 12 epilogue warps; thread e belongs to warp w = e / 32. Warp w may only touch TMEM lanes
+// 32 * (w % 4) .. + 31, so row t = 32 * (w % 4) + lane, and the three warps with the same w % 4
+// split the row's columns in thirds (part qd = w / 4), in 16-column chunks. With the producer and
+// MMA warps the CTA has 14 warps, at most 4 per SM sub-partition, so a thread may use 128
+// registers: enough to hold its third of the residual row (<= 5 chunks, d <= 240) across a layer.
+constexpr int kParts = 3;
+constexpr int kEpiWarps = 4 * kParts;
+constexpr int kEpiThreads = kEpiWarps * 32;
+constexpr int kMaxRowChunks = 5;  // 16-column chunks of a d <= 240 row held per thread
+constexpr int kProducerWarp = kEpiWarps;
+constexpr int kMmaWarp = kEpiWarps + 1;
+
+struct EpiThread {
+  int t;   // row in the tile == TMEM lane
+  int qd;  // column part
+  uint32_t lane_tmem;
+};
+
+// This part's chunk range of a row of `width` columns.
+__device__ __forceinline__ void part_chunks(int width, int qd, int& lo, int& hi) {
+  const int chunks = width / 16;
+  const int per = (chunks + kParts - 1) / kParts;
+  lo = qd * per;
+  hi = min(chunks, lo + per);
+  if (lo > hi) lo = hi;
+}
+
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory"); }
+
+// Sum of `value` over the kParts threads that share row t.
+__device__ __forceinline__ float row_sum(float value, const EpiThread& e, float (*red)[kTile]) {
+  red[e.qd][e.t] = value;
+  epi_sync();
+  float total = 0.f;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) sum += v[i];
-  }
-  const float mean = sum / d;
-  float var = 0.f;
-  for (int col = 0; col < d; col += 16) {
-    load16(x, tile, d, col, t, v);
+  for (int q = 0; q < kParts; ++q) total += red[q][e.t];
+  return total;
+}
+
+// LayerNorm (eps 1e-5, biased variance, mean then centred variance) of the row held in
+// registers (this thread's chunks lo..hi-1 of d), written as bf16 into the operand buffer.
+__device__ void layer_norm_regs(const float (&x)[kMaxRowChunks][16], int lo, int hi, int d, const EpiThread& e,
+                                const float* w, const float* b, unsigned char* abuf, float (*red)[kTile]) {
+  float part = 0.f;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float c = v[i] - mean;
-      var += c * c;
-    }
-  }
-  const float rstd = rsqrtf(var / d + 1e-5f);
-  for (int col = 0; col < d; col += 16) {
-    load16(x, tile, d, col, t, v);
+  for (int c = 0; c < kMaxRowChunks; ++c)
+    if (lo + c < hi)
 #pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = (v[i] - mean) * rstd * w[col + i] + b[col + i];
-    store_operand16(abuf, col, t, v);
+      for (int i = 0; i < 16; ++i) part += x[c][i];
+  const float mean = row_sum(part, e, red) / d;
+  float sq = 0.f;
+#pragma unroll
+  for (int c = 0; c < kMaxRowChunks; ++c)
+    if (lo + c < hi)
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float z = x[c][i] - mean;
+        sq += z * z;
+      }
+  const float rstd = rsqrtf(row_sum(sq, e, red + kParts) / d + 1e-5f);
+#pragma unroll
+  for (int c = 0; c < kMaxRowChunks; ++c) {
+    if (lo + c >= hi) continue;
+    const int col = (lo + c) * 16;
+    float y[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) y[i] = (x[c][i] - mean) * rstd * w[col + i] + b[col + i];
+    store_operand16(abuf, col, e.t, y);
   }
 }
 
 // ---- the QKV epilogue: q out, K/V (+ value embedding) into the pool ------------------------------------
-__device__ void qkv_epilogue(const TcParams& p, uint32_t lane_tmem, int64_t tile, int t) {
+__device__ void qkv_epilogue(const TcParams& p, const EpiThread& e, int64_t tile) {
+  const int t = e.t;
   const int64_t row = tile * kTile + t;
   const bool valid = row < p.nt;
   const int64_t b = row / p.T;
@@ -159,10 +206,32 @@ __device__ void qkv_epilogue(const TcParams& p, uint32_t lane_tmem, int64_t tile
     cache_row = p.rows ? p.rows[b] : b;
   }
   const int hd = p.H * p.D;
-  float v[16];
-  for (int col0 = 0; col0 < p.qw; col0 += 16) {
-    tc::tmem_ld16(lane_tmem + col0, v);
+  int lo, hi;
+  part_chunks(p.qw, e.qd, lo, hi);
+  for (int c = lo; c < hi; ++c) {
+    float v[16];
+    tc::tmem_ld16(e.lane_tmem + c * 16, v);
     if (!valid) continue;
+    const int col0 = c * 16;
+    if (p.T == 1 && p.q_dtype != CG_F32 && col0 + 16 <= hd) {
+      // one row's q is contiguous when T == 1: two 16-byte stores
+      uint4 packed[2];
+      uint32_t* words = reinterpret_cast<uint32_t*>(packed);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (p.q_dtype == CG_F16) {
+          __half2 h2 = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+          words[i] = *reinterpret_cast<uint32_t*>(&h2);
+        } else {
+          __nv_bfloat162 h2 = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+          words[i] = *reinterpret_cast<uint32_t*>(&h2);
+        }
+      }
+      uint4* dst = reinterpret_cast<uint4*>(static_cast<unsigned char*>(p.q) + (b * hd + col0) * 2);
+      dst[0] = packed[0];
+      dst[1] = packed[1];
+      continue;
+    }
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       const int col = col0 + i;
@@ -175,9 +244,9 @@ __device__ void qkv_epilogue(const TcParams& p, uint32_t lane_tmem, int64_t tile
         const int kvh = rem / p.D, dd = rem % p.D;
         float value = v[i];
         if (which == 1 && p.value_index >= 0) {
-          const float4 e = *blk(p.val_blk, static_cast<int64_t>(p.value_index) * p.ntiles + tile, p.kvw, rem, t);
+          const float4 ev = *blk(p.val_blk, static_cast<int64_t>(p.value_index) * p.ntiles + tile, p.kvw, rem, t);
           const int lanei = rem & 3;
-          value += lanei == 0 ? e.x : lanei == 1 ? e.y : lanei == 2 ? e.z : e.w;
+          value += lanei == 0 ? ev.x : lanei == 1 ? ev.y : lanei == 2 ? ev.z : ev.w;
         }
         const int64_t dst = ((cache_row * p.KVH + kvh) * p.max_len + pos) * p.D + dd;
         store_from_float(which ? p.v_layer : p.k_layer, dst, p.kv_dtype, value);
@@ -186,164 +255,207 @@ __device__ void qkv_epilogue(const TcParams& p, uint32_t lane_tmem, int64_t tile
   }
 }
 
-// ---- epilogue warps (threads 0..127: thread t owns row t of the tile and TMEM lane t) ----------------
+// ---- epilogue warps ----------------------------------------------------------------------------------------
 __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned char* hbuf, uint32_t tmem,
-                               uint64_t* a_ready_bar, uint64_t* acc_ready_bar, uint64_t* attn_full_bar, int abytes) {
-  const int warp = threadIdx.x >> 5;
+                               uint64_t* a_ready_bar, uint64_t* acc_ready_bar, uint64_t* attn_full_bar, int abytes,
+                               float (*red)[kTile]) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t tile = blockIdx.x;
-  uint64_t& a_ready = *a_ready_bar;
-  uint64_t& acc_ready = *acc_ready_bar;
-  uint64_t& attn_full = *attn_full_bar;
-    const int t = threadIdx.x;  // row within the tile == TMEM lane
-    const uint32_t lane_tmem = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-    const int64_t row = tile * kTile + t;
-    const bool valid = row < p.nt;
-    uint32_t acc_phase = 0;
-    float v[16], x[16];
-    const int d = p.d;
-    auto publish = [&]() {  // operand written and TMEM reads done: hand over to the MMA warp
-      tc::fence_async_smem();
-      tc::fence_before_sync();
-      tc::bar_arrive(&a_ready);
-    };
-    auto wait_acc = [&]() -> bool {
-      if (!tc::bar_wait(&acc_ready, acc_phase, 0x403)) return false;
-      acc_phase ^= 1u;
-      tc::fence_after_sync();
-      return true;
-    };
+  EpiThread e;
+  e.t = (warp & 3) * 32 + lane;
+  e.qd = warp >> 2;  // 0 .. kParts-1
+  e.lane_tmem = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+  const int t = e.t;
+  const int64_t row = tile * kTile + t;
+  const bool valid = row < p.nt;
+  const int d = p.d;
+  int lo, hi;  // this thread's 16-column chunks of a d-wide row
+  part_chunks(d, e.qd, lo, hi);
+  uint32_t acc_phase = 0;
+  float x[kMaxRowChunks][16];
+  float v16[16];
+  // One thread waits on each mbarrier and arrives for the group; the others park on a
+  // hardware named barrier instead of polling shared memory.
+  auto publish = [&]() {  // operand written and TMEM reads done: hand over to the MMA warp
+    tc::fence_async_smem();
+    tc::fence_before_sync();
+    epi_sync();
+    if (threadIdx.x == 0) tc::bar_arrive(a_ready_bar);
+  };
+  auto group_wait = [&](uint64_t* bar, uint32_t parity, int code) -> bool {
+    if (threadIdx.x == 0) red[2 * kParts][0] = tc::bar_wait(bar, parity, code) ? 1.f : 0.f;
+    epi_sync();
+    return red[2 * kParts][0] != 0.f;
+  };
+  auto wait_acc = [&]() -> bool {
+    if (!group_wait(acc_ready_bar, acc_phase, 0x403)) return false;
+    acc_phase ^= 1u;
+    tc::fence_after_sync();
+    return true;
+  };
 
-    if (p.mode == kLayer) {
-      // E0: the attention output tile is already in operand layout: one bulk copy.
-      if (t == 0) {
-        tc::bar_expect_tx(&attn_full, abytes);
-        tc::bulk_g2s(abuf, reinterpret_cast<const unsigned char*>(p.attn_blk) + tile * abytes, abytes, &attn_full);
-      }
-      if (!tc::bar_wait(&attn_full, 0, 0x404)) return;
-      publish();
-      // E1: x += out_proj; LN_mlp(x) -> A.
+  if (p.mode == kLayer) {
+    // E0: the attention output tile is already in operand layout: one bulk copy.
+    if (threadIdx.x == 0) {
+      tc::bar_expect_tx(attn_full_bar, abytes);
+      tc::bulk_g2s(abuf, reinterpret_cast<const unsigned char*>(p.attn_blk) + tile * abytes, abytes, attn_full_bar);
+    }
+#pragma unroll
+    for (int c = 0; c < kMaxRowChunks; ++c)  // the residual row, in registers until E3
+      if (lo + c < hi) load16(p.x_blk, tile, d, (lo + c) * 16, t, x[c]);
+    if (!group_wait(attn_full_bar, 0, 0x404)) return;
+    publish();
+    // E1: x += out_proj; LN_mlp(x) -> A.
+    if (!wait_acc()) return;
+#pragma unroll
+    for (int c = 0; c < kMaxRowChunks; ++c) {
+      if (lo + c >= hi) continue;
+      tc::tmem_ld16(e.lane_tmem + p.ops[0].tmem_col + (lo + c) * 16, v16);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) x[c][i] += v16[i];
+    }
+    layer_norm_regs(x, lo, hi, d, e, p.ln_mlp_w, p.ln_mlp_b, abuf, red);
+    publish();
+    // E2: GELU of each up chunk into H.
+    const int chunks = p.f / d;
+    for (int uc = 0; uc < chunks; ++uc) {
       if (!wait_acc()) return;
-      for (int col = 0; col < d; col += 16) {
-        tc::tmem_ld16(lane_tmem + p.ops[0].tmem_col + col, v);
-        load16(p.x_blk, tile, d, col, t, x);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) x[i] += v[i];
-        store16(p.x_blk, tile, d, col, t, x);
+      for (int c = 0; c < kMaxRowChunks; ++c) {
+        if (lo + c >= hi) continue;
+        const int col = (lo + c) * 16;
+        tc::tmem_ld16(e.lane_tmem + 256 + col, v16);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v16[i] = gelu_erf(v16[i] + p.up_b[uc * d + col + i]);
+        store_operand16(hbuf, col, t, v16);
       }
-      layer_norm_to_operand(p.x_blk, tile, d, t, p.ln_mlp_w, p.ln_mlp_b, abuf);
       publish();
-      // E2: GELU of each up chunk into H.
-      const int chunks = p.f / d;
-      for (int c = 0; c < chunks; ++c) {
-        if (!wait_acc()) return;
-        for (int col = 0; col < d; col += 16) {
-          tc::tmem_ld16(lane_tmem + 256 + col, v);
+    }
+    // E3: x += down + b; x += PLE(l); store; then LN_attn(l+1) -> A.
+    // The PLE update and the bias do not depend on the GEMM: fold them into x first.
 #pragma unroll
-          for (int i = 0; i < 16; ++i) v[i] = gelu_erf(v[i] + p.up_b[c * d + col + i]);
-          store_operand16(hbuf, col, t, v);
-        }
-        publish();
-      }
-      // E3: x += down + b; x += PLE(l); then LN_attn(l+1) -> A.
-      if (!wait_acc()) return;
-      for (int col = 0; col < d; col += 16) {
-        tc::tmem_ld16(lane_tmem + col, v);
-        load16(p.x_blk, tile, d, col, t, x);
+    for (int c = 0; c < kMaxRowChunks; ++c) {
+      if (lo + c >= hi) continue;
+      const int col = (lo + c) * 16;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) x[i] += v[i] + p.down_b[col + i];
-        if (p.P) {
+      for (int i = 0; i < 16; ++i) x[c][i] += p.down_b[col + i];
+      if (p.P) {
 #pragma unroll
-          for (int i = 0; i < 16; i += 4) {
-            const int k = (col + i) % p.P;  // P % 4 == 0: four columns share a float4
-            const float4 e = *blk(p.ple_blk, static_cast<int64_t>(p.layer) * p.ntiles + tile, p.P, k, t);
-            x[i] += e.x * p.ple_scale;
-            x[i + 1] += e.y * p.ple_scale;
-            x[i + 2] += e.z * p.ple_scale;
-            x[i + 3] += e.w * p.ple_scale;
-          }
-        }
-        store16(p.x_blk, tile, d, col, t, x);
-      }
-      if (p.has_next) {
-        layer_norm_to_operand(p.x_blk, tile, d, t, p.ln_next_w, p.ln_next_b, abuf);
-        publish();
-        if (!wait_acc()) return;
-        qkv_epilogue(p, lane_tmem, tile, t);
-      }
-    } else {
-      // First kernel of a wave: conditioned x, PLE and value streams into blocked layout.
-      const int ple_w = p.L * p.P;
-      const int val_w = p.nv * p.kvw;
-      const float inv_sqrt2 = 0.70710678118654752f;
-      if (p.mode == kFirstLookup) {
-        const float* src = p.lookup + (valid ? row : 0) * p.lookup_width;
-        // x = RMSNorm(lookup[:, :d]) * gain (trunk.py:297-298, 104-115)
-        float ss = 0.f;
-        for (int col = 0; col < d; col += 4) {
-          const float4 e = *reinterpret_cast<const float4*>(src + col);
-          ss += e.x * e.x + e.y * e.y + e.z * e.z + e.w * e.w;
-        }
-        const float inv = rsqrtf(ss / d + 1e-5f);
-        for (int col = 0; col < d; col += 16) {
-#pragma unroll
-          for (int i = 0; i < 16; i += 4) {
-            const float4 e = *reinterpret_cast<const float4*>(src + col + i);
-            x[i] = e.x * inv * p.rms_w[col + i];
-            x[i + 1] = e.y * inv * p.rms_w[col + i + 1];
-            x[i + 2] = e.z * inv * p.rms_w[col + i + 2];
-            x[i + 3] = e.w * inv * p.rms_w[col + i + 3];
-          }
-          store16(p.x_blk, tile, d, col, t, x);
-          store_operand16(abuf, col, t, x);
-        }
-        for (int c4 = 0; c4 < val_w; c4 += 4) {
-          const float4 e = *reinterpret_cast<const float4*>(src + d + ple_w + c4);
-          *blk(p.val_blk, static_cast<int64_t>(c4 / p.kvw) * p.ntiles + tile, p.kvw, c4 % p.kvw, t) = e;
-        }
-        if (p.n_ops > 1) publish();
-        // ple = (lookup + W_c x) / sqrt(2), one TMEM chunk of up to 256 columns at a time.
-        int c0 = 0;
-        for (int o = 0; o + 1 < p.n_ops; ++o) {
-          const int n = p.ops[o].n;
-          if (!wait_acc()) return;
-          for (int col = 0; col < n; col += 16) {
-            tc::tmem_ld16(lane_tmem + col, v);
-#pragma unroll
-            for (int i = 0; i < 16; i += 4) {
-              const int k = c0 + col + i;
-              const float4 e = *reinterpret_cast<const float4*>(src + d + k);
-              const int layer = k / p.P, kk = k % p.P;
-              *blk(p.ple_blk, static_cast<int64_t>(layer) * p.ntiles + tile, p.P, kk, t) =
-                  make_float4((e.x + v[i]) * inv_sqrt2, (e.y + v[i + 1]) * inv_sqrt2, (e.z + v[i + 2]) * inv_sqrt2,
-                              (e.w + v[i + 3]) * inv_sqrt2);
-            }
-          }
-          c0 += n;
-          if (o + 2 < p.n_ops) publish();
-        }
-      } else {
-        const int64_t r = valid ? row : 0;
-        for (int col = 0; col < d; col += 16) {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) x[i] = p.x_in[r * d + col + i];
-          store16(p.x_blk, tile, d, col, t, x);
-        }
-        for (int k = 0; k < ple_w; k += 4) {
-          const float4 e = *reinterpret_cast<const float4*>(p.ple_in + r * ple_w + k);
-          *blk(p.ple_blk, static_cast<int64_t>(k / p.P) * p.ntiles + tile, p.P, k % p.P, t) = e;
-        }
-        for (int k = 0; k < val_w; k += 4) {
-          const float4 e = *reinterpret_cast<const float4*>(p.val_in + r * val_w + k);
-          *blk(p.val_blk, static_cast<int64_t>(k / p.kvw) * p.ntiles + tile, p.kvw, k % p.kvw, t) = e;
+        for (int i = 0; i < 16; i += 4) {
+          const int k = (col + i) % p.P;  // P % 4 == 0: four columns share a float4
+          const float4 ev = *blk(p.ple_blk, static_cast<int64_t>(p.layer) * p.ntiles + tile, p.P, k, t);
+          x[c][i] += ev.x * p.ple_scale;
+          x[c][i + 1] += ev.y * p.ple_scale;
+          x[c][i + 2] += ev.z * p.ple_scale;
+          x[c][i + 3] += ev.w * p.ple_scale;
         }
       }
-      (void)ple_w;
-      layer_norm_to_operand(p.x_blk, tile, d, t, p.ln_next_w, p.ln_next_b, abuf);
+    }
+    if (!wait_acc()) return;
+#pragma unroll
+    for (int c = 0; c < kMaxRowChunks; ++c) {
+      if (lo + c >= hi) continue;
+      const int col = (lo + c) * 16;
+      tc::tmem_ld16(e.lane_tmem + col, v16);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) x[c][i] += v16[i];
+      store16(p.x_blk, tile, d, col, t, x[c]);
+    }
+    if (p.has_next) {
+      layer_norm_regs(x, lo, hi, d, e, p.ln_next_w, p.ln_next_b, abuf, red);
       publish();
       if (!wait_acc()) return;
-      qkv_epilogue(p, lane_tmem, tile, t);
+      qkv_epilogue(p, e, tile);
+    }
+    return;
+  }
+
+  // First kernel of a wave: conditioned x, PLE and value streams into blocked layout.
+  const int ple_w = p.L * p.P;
+  const int val_w = p.nv * p.kvw;
+  const int64_t r = valid ? row : 0;
+  if (p.mode == kFirstLookup) {
+    const float* src = p.lookup + r * p.lookup_width;
+    // x = RMSNorm(lookup[:, :d]) * gain (trunk.py:297-298, 104-115)
+#pragma unroll
+    for (int c = 0; c < kMaxRowChunks; ++c) {
+      if (lo + c >= hi) continue;
+#pragma unroll
+      for (int i = 0; i < 16; i += 4) {
+        const float4 ev = *reinterpret_cast<const float4*>(src + (lo + c) * 16 + i);
+        x[c][i] = ev.x;
+        x[c][i + 1] = ev.y;
+        x[c][i + 2] = ev.z;
+        x[c][i + 3] = ev.w;
+      }
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < kMaxRowChunks; ++c)
+      if (lo + c < hi)
+#pragma unroll
+        for (int i = 0; i < 16; ++i) ss += x[c][i] * x[c][i];
+    const float inv = rsqrtf(row_sum(ss, e, red) / d + 1e-5f);
+#pragma unroll
+    for (int c = 0; c < kMaxRowChunks; ++c) {
+      if (lo + c >= hi) continue;
+      const int col = (lo + c) * 16;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) x[c][i] = x[c][i] * inv * p.rms_w[col + i];
+      store16(p.x_blk, tile, d, col, t, x[c]);
+      store_operand16(abuf, col, t, x[c]);
+    }
+    for (int k = e.qd * 4; k < val_w; k += 4 * kParts) {
+      const float4 ev = *reinterpret_cast<const float4*>(src + d + ple_w + k);
+      *blk(p.val_blk, static_cast<int64_t>(k / p.kvw) * p.ntiles + tile, p.kvw, k % p.kvw, t) = ev;
+    }
+    if (p.n_ple_ops > 0) publish();
+    // ple = (lookup + W_c x) / sqrt(2), one TMEM chunk of up to 256 columns at a time.
+    const float inv_sqrt2 = 0.70710678118654752f;
+    int c0 = 0;
+    for (int o = 0; o < p.n_ple_ops; ++o) {
+      const int n = p.ops[o].n;
+      int plo, phi;
+      part_chunks(n, e.qd, plo, phi);
+      if (!wait_acc()) return;
+      for (int c = plo; c < phi; ++c) {
+        tc::tmem_ld16(e.lane_tmem + c * 16, v16);
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) {
+          const int k = c0 + c * 16 + i;
+          const float4 ev = *reinterpret_cast<const float4*>(src + d + k);
+          const int layer = k / p.P, kk = k % p.P;
+          *blk(p.ple_blk, static_cast<int64_t>(layer) * p.ntiles + tile, p.P, kk, t) =
+              make_float4((ev.x + v16[i]) * inv_sqrt2, (ev.y + v16[i + 1]) * inv_sqrt2,
+                          (ev.z + v16[i + 2]) * inv_sqrt2, (ev.w + v16[i + 3]) * inv_sqrt2);
+        }
+      }
+      c0 += n;
+      if (o + 1 < p.n_ple_ops) publish();
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < kMaxRowChunks; ++c) {
+      if (lo + c >= hi) continue;
+      const int col = (lo + c) * 16;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) x[c][i] = p.x_in[r * d + col + i];
+      store16(p.x_blk, tile, d, col, t, x[c]);
+    }
+    for (int k = e.qd * 4; k < ple_w; k += 4 * kParts) {
+      const float4 ev = *reinterpret_cast<const float4*>(p.ple_in + r * ple_w + k);
+      *blk(p.ple_blk, static_cast<int64_t>(k / p.P) * p.ntiles + tile, p.P, k % p.P, t) = ev;
+    }
+    for (int k = e.qd * 4; k < val_w; k += 4 * kParts) {
+      const float4 ev = *reinterpret_cast<const float4*>(p.val_in + r * val_w + k);
+      *blk(p.val_blk, static_cast<int64_t>(k / p.kvw) * p.ntiles + tile, p.kvw, k % p.kvw, t) = ev;
     }
   }
+  layer_norm_regs(x, lo, hi, d, e, p.ln_next_w, p.ln_next_b, abuf, red);
+  publish();
+  if (!wait_acc()) return;
+  qkv_epilogue(p, e, tile);
+}
 
 // ---- the kernel ------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(kTcThreads, 1) tc_dense_kernel(const __grid_constant__ TcParams p) {
@@ -351,9 +463,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dense_kernel(const __grid_co
   __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages];
   __shared__ __align__(8) uint64_t a_ready, acc_ready, attn_full;
   __shared__ uint32_t tmem_base;
+  __shared__ float red[2 * kParts + 1][kTile];  // row reductions across a row's threads; last row: wait status
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t tile = blockIdx.x;
   const int abytes = kTile * p.d * 2;
   unsigned char* abuf = smem;
   unsigned char* hbuf = smem + abytes;
@@ -364,12 +476,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dense_kernel(const __grid_co
       tc::bar_init(&full[s], 1);
       tc::bar_init(&empty[s], 1);
     }
-    tc::bar_init(&a_ready, 4 * 32);
+    tc::bar_init(&a_ready, 1);
     tc::bar_init(&acc_ready, 1);
     tc::bar_init(&attn_full, 1);
     tc::bar_fence_init();
   }
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tc::tmem_alloc(&tmem_base, 512);
     tc::tmem_relinquish();
   }
@@ -378,62 +490,83 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dense_kernel(const __grid_co
   tc::fence_after_sync();
   const uint32_t tmem = tmem_base;
 
-  if (warp == 4) {
-    // ---- producer: weight K-slices into the ring -------------------------------------------------
+  if (warp == kProducerWarp) {
+    // ---- producer: weight K-slices into the ring, several slices per bulk copy ---------------------
+    // A bulk copy has a fixed cost of ~0.1 us, so each stage carries up to 32 KB of consecutive
+    // K-slices of one GEMM step (they are contiguous in the packed weights).
     if (lane == 0) {
-      int it = 0;
-      bool ok = true;
-      for (int o = 0; o < p.n_ops && ok; ++o) {
-        const GemmOp& op = p.ops[o];
-        const uint32_t bytes = static_cast<uint32_t>(op.n) * 32u;
-        for (int s = 0; s < op.ksteps; ++s, ++it) {
-          const int stage = it % p.stages;
-          const int fill = it / p.stages;
-          if (fill > 0 && !(ok = tc::bar_wait(&empty[stage], (fill - 1) & 1, 0x400))) break;
+      const uint64_t keep = tc::make_policy_evict_last();
+      const int stages = p.stages;
+      int stage = 0;
+      uint32_t lap = 0;  // completed passes over the ring
+      for (int o = 0; o < p.n_ops; ++o) {
+        const unsigned char* src = reinterpret_cast<const unsigned char*>(p.ops[o].w);
+        const uint32_t slice = static_cast<uint32_t>(p.ops[o].n) * 32u;
+        const int ksteps = p.ops[o].ksteps, per = p.ops[o].ks_per_stage;
+        for (int s = 0; s < ksteps; s += per) {
+          const uint32_t bytes = slice * static_cast<uint32_t>(min(per, ksteps - s));
+          // From the second pass on, the stage must have been released by its MMAs.
+          if (lap > 0 && !tc::bar_wait(&empty[stage], (lap - 1) & 1u, 0x400)) goto producer_done;
           tc::bar_expect_tx(&full[stage], bytes);
-          tc::bulk_g2s(ring + stage * p.stage_bytes, op.w + static_cast<int64_t>(s) * op.n * 16, bytes, &full[stage]);
+          tc::bulk_g2s_hint(ring + stage * p.stage_bytes, src, bytes, &full[stage], keep);
+          src += bytes;
+          if (++stage == stages) {
+            stage = 0;
+            ++lap;
+          }
         }
       }
+    producer_done:;
     }
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     // ---- MMA issuer ---------------------------------------------------------------------------------
     if (lane == 0) {
-      int it = 0;
+      const int stages = p.stages;
+      const uint32_t ring_addr = tc::smem_u32(ring);
+      int stage = 0;
+      uint32_t lap = 0;
       uint32_t a_phase = 0;
-      bool ok = true;
-      for (int o = 0; o < p.n_ops && ok; ++o) {
-        const GemmOp& op = p.ops[o];
+      for (int o = 0; o < p.n_ops; ++o) {
+        const GemmOp op = p.ops[o];
         if (op.wait_a) {
-          if (!(ok = tc::bar_wait(&a_ready, a_phase, 0x401))) break;
+          if (!tc::bar_wait(&a_ready, a_phase, 0x401)) break;
           a_phase ^= 1u;
           tc::fence_after_sync();
         }
-        const unsigned char* a_base = op.a_src ? hbuf : abuf;
-        for (int s = 0; s < op.ksteps; ++s, ++it) {
-          const int stage = it % p.stages;
-          if (!(ok = tc::bar_wait(&full[stage], (it / p.stages) & 1, 0x402))) break;
+        const uint32_t a_addr = tc::smem_u32(op.a_src ? hbuf : abuf);
+        const uint32_t slice = static_cast<uint32_t>(op.n) * 32u;
+        const uint32_t idesc = tc::idesc_bf16(128, op.n <= 256 ? op.n : 256);
+        const uint32_t idesc_rest = tc::idesc_bf16(128, op.n > 256 ? op.n - 256 : 16);
+        bool ok = true;
+        for (int s0 = 0; s0 < op.ksteps; s0 += op.ks_per_stage) {
+          if (!(ok = tc::bar_wait(&full[stage], lap & 1u, 0x402))) break;
           tc::fence_after_sync();
-          const uint64_t a_desc = tc::smem_desc(tc::smem_u32(a_base + 2 * s * (kTile * 16)), kTile * 16, 128);
-          const uint32_t b_addr = tc::smem_u32(ring + stage * p.stage_bytes);
-          const uint32_t acc = (s > 0 || op.accumulate_first) ? 1u : 0u;
-          if (op.n <= 256) {
-            tc::mma_bf16(tmem + op.tmem_col, a_desc, tc::smem_desc(b_addr, 128, 256), tc::idesc_bf16(128, op.n), acc);
-          } else {
-            tc::mma_bf16(tmem + op.tmem_col, a_desc, tc::smem_desc(b_addr, 128, 256), tc::idesc_bf16(128, 256), acc);
-            tc::mma_bf16(tmem + op.tmem_col + 256, a_desc, tc::smem_desc(b_addr + 32 * 256, 128, 256),
-                         tc::idesc_bf16(128, op.n - 256), acc);
+          const int end = min(op.ksteps, s0 + op.ks_per_stage);
+          for (int s = s0; s < end; ++s) {
+            const uint64_t a_desc = tc::smem_desc(a_addr + 2 * s * (kTile * 16), kTile * 16, 128);
+            const uint32_t b_addr = ring_addr + stage * p.stage_bytes + (s - s0) * slice;
+            const uint32_t acc = (s > 0 || op.accumulate_first) ? 1u : 0u;
+            tc::mma_bf16(tmem + op.tmem_col, a_desc, tc::smem_desc(b_addr, 128, 256), idesc, acc);
+            if (op.n > 256)
+              tc::mma_bf16(tmem + op.tmem_col + 256, a_desc, tc::smem_desc(b_addr + 32 * 256, 128, 256), idesc_rest,
+                           acc);
           }
           tc::mma_commit(&empty[stage]);
+          if (++stage == stages) {
+            stage = 0;
+            ++lap;
+          }
         }
-        if (ok && op.signal) tc::mma_commit(&acc_ready);
+        if (!ok) break;
+        if (op.signal) tc::mma_commit(&acc_ready);
       }
     }
   } else {
-    dense_epilogue(p, abuf, hbuf, tmem, &a_ready, &acc_ready, &attn_full, abytes);
+    dense_epilogue(p, abuf, hbuf, tmem, &a_ready, &acc_ready, &attn_full, abytes, red);
   }
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem, 512);
   }
@@ -480,7 +613,7 @@ LayerPack layer_pack(const cg_trunk_dims& dims, const void* blob, const BlobLayo
 
 bool tc_layers_available(const cg_trunk_dims& dims) {
   const int d = dims.d_model, D = head_dim(dims), q = qkv_width(dims);
-  if (d % 16 || d > 256 || dims.d_ff % d || q % 16 || q > 512 || D % 8) return false;
+  if (d % 16 || d / 16 > kParts * kMaxRowChunks || dims.d_ff % d || q % 16 || q > 512 || D % 8) return false;
   if (q > 256 && (q - 256) % 16) return false;
   if (dims.per_layer_dim % 4 || (static_cast<int64_t>(dims.n_layers) * dims.per_layer_dim) % 16) return false;
   if ((dims.n_kv_heads * D) % 4) return false;
@@ -508,7 +641,12 @@ int tc_pack(const cg_trunk_dims& dims, void* blob, const BlobLayout& L, cudaStre
   }
   for (int layer = 0; layer < dims.n_layers; ++layer) {
     LayerPack lp = layer_pack(dims, blob, L, layer);
-    if ((rc = pack(part(blob, L, CG_PART_QKV, layer), d, 0, q, 0, d, const_cast<__nv_bfloat16*>(lp.qkv)))) return rc;
+    // QKV as two GEMM steps of <= 256 output columns: rows [0, 256) then [256, q).
+    const int qa = q < 256 ? q : 256;
+    if ((rc = pack(part(blob, L, CG_PART_QKV, layer), d, 0, qa, 0, d, const_cast<__nv_bfloat16*>(lp.qkv)))) return rc;
+    if (q > 256 && (rc = pack(part(blob, L, CG_PART_QKV, layer), d, 256, q - 256, 0, d,
+                             const_cast<__nv_bfloat16*>(lp.qkv) + static_cast<int64_t>(256) * d)))
+      return rc;
     if ((rc = pack(part(blob, L, CG_PART_OUT, layer), d, 0, d, 0, d, const_cast<__nv_bfloat16*>(lp.out)))) return rc;
     for (int c = 0; c < f / d; ++c) {
       if ((rc = pack(part(blob, L, CG_PART_UP, layer), d, c * d, d, 0, d,
@@ -559,13 +697,22 @@ int64_t tc_layers_scratch_bytes(const cg_trunk_dims& dims, int64_t batch, int st
 }
 
 int launch_dense(TcParams& p, cudaStream_t s) {
-  int max_n = 0;
-  for (int i = 0; i < p.n_ops; ++i) max_n = p.ops[i].n > max_n ? p.ops[i].n : max_n;
-  p.stage_bytes = max_n * 32;
+  // Ring stages of up to 32 KB (several consecutive K-slices each); as many as fit.
   const int abytes = kTile * p.d * 2;
-  int stages = p.stage_bytes ? (kSmemBudget - 2 * abytes) / p.stage_bytes : 1;
+  int max_slice = 0;
+  for (int i = 0; i < p.n_ops; ++i) max_slice = p.ops[i].n * 32 > max_slice ? p.ops[i].n * 32 : max_slice;
+  p.stage_bytes = max_slice > kStageTarget ? max_slice : kStageTarget;
+  int stages = (kSmemBudget - 2 * abytes) / p.stage_bytes;
+  if (stages < 2) {
+    p.stage_bytes = max_slice;
+    stages = (kSmemBudget - 2 * abytes) / p.stage_bytes;
+  }
   p.stages = stages > kMaxStages ? kMaxStages : stages;
   if (p.stages < 2) return set_error(CG_ERR_ARGUMENT, "tensor-core dense layer does not fit in shared memory");
+  for (int i = 0; i < p.n_ops; ++i) {
+    const int per = p.stage_bytes / (p.ops[i].n * 32);
+    p.ops[i].ks_per_stage = per < p.ops[i].ksteps ? per : p.ops[i].ksteps;
+  }
   const int smem = 2 * abytes + p.stages * p.stage_bytes;
   static int configured_smem[64] = {0};
   int device = 0;
@@ -650,15 +797,25 @@ int run_tc_forward(const cg_trunk_dims& dims, const void* blob, const BlobLayout
     return static_cast<float>(1.0 / std::sqrt(static_cast<double>((d + p.P - 1) / p.P)));
   }();
 
-  auto qkv_op = [&](int layer) {
+  auto push_qkv = [&](int layer) {
+    const __nv_bfloat16* w = layer_pack(dims, blob, L, layer).qkv;
     GemmOp op{};
-    op.w = layer_pack(dims, blob, L, layer).qkv;
-    op.n = qw;
+    op.w = w;
+    op.n = qw < 256 ? qw : 256;
     op.ksteps = d / 16;
     op.tmem_col = 0;
     op.wait_a = 1;
-    op.signal = 1;
-    return op;
+    op.signal = qw <= 256;
+    p.ops[p.n_ops++] = op;
+    if (qw > 256) {
+      GemmOp rest{};
+      rest.w = w + static_cast<int64_t>(256) * d;
+      rest.n = qw - 256;
+      rest.ksteps = d / 16;
+      rest.tmem_col = 256;
+      rest.signal = 1;
+      p.ops[p.n_ops++] = rest;
+    }
   };
   auto set_qkv_target = [&](int layer) {
     p.qkv_layer = layer;
@@ -694,7 +851,8 @@ int run_tc_forward(const cg_trunk_dims& dims, const void* blob, const BlobLayout
     p.ple_in = ple_in;
     p.val_in = val_in;
   }
-  p.ops[p.n_ops++] = qkv_op(0);
+  p.n_ple_ops = p.n_ops;
+  push_qkv(0);
   set_qkv_target(0);
   p.layer = 0;
   p.has_next = 1;
@@ -738,6 +896,7 @@ int run_tc_forward(const cg_trunk_dims& dims, const void* blob, const BlobLayout
     p.up_b = part(blob, L, CG_PART_UP_B, layer);
     p.down_b = part(blob, L, CG_PART_DOWN_B, layer);
     p.n_ops = 0;
+    p.n_ple_ops = 0;
     GemmOp out{};
     out.w = lp.out;
     out.n = d;
@@ -768,7 +927,7 @@ int run_tc_forward(const cg_trunk_dims& dims, const void* blob, const BlobLayout
       p.ops[p.n_ops++] = down;
     }
     if (p.has_next) {
-      p.ops[p.n_ops++] = qkv_op(layer + 1);
+      push_qkv(layer + 1);
       set_qkv_target(layer + 1);
     }
     if (p.n_ops > kMaxOps) return set_error(CG_ERR_ARGUMENT, "too many GEMM steps in one dense layer");
