@@ -72,6 +72,8 @@ _SIGNATURES: dict[str, tuple[type, list]] = {
     "cg_kv_write_step": (_i32, [_p, _p, _i32, _i64, _i32, _i32, _i32, _p, _p, _i64, _i32, _p, _p, _i32, _p]),
     "cg_kv_copy_rows_workspace_bytes": (_i64, [_i32, _i32, _i32, _i32, _i32, _i64]),
     "cg_kv_copy_rows": (_i32, [_p, _p, _i32, _i32, _i64, _i32, _i32, _i32, _p, _p, _i64, _i32, _p, _i64, _p]),
+    "cg_kv_copy_rows_noalloc_max_bytes": (_i64, []),
+    "cg_kv_copy_rows_noalloc": (_i32, [_p, _p, _i32, _i32, _i64, _i32, _i32, _i32, _p, _p, _i64, _i32, _p]),
     "cg_trunk_blob_bytes": (_i64, [ctypes.POINTER(TrunkDims)]),
     "cg_trunk_part_offset": (_i64, [ctypes.POINTER(TrunkDims), _i32, _i32]),
     "cg_trunk_prepare": (_i32, [ctypes.POINTER(TrunkDims), _p, _p]),

@@ -1,4 +1,6 @@
 // KV pool maintenance: per-row writes and row copies (cardgym/nn/kv_cache.py:84-105, 122-138).
+#include <mutex>
+
 #include "common.cuh"
 
 namespace cg {
@@ -105,4 +107,75 @@ extern "C" int cg_kv_copy_rows(void* k_pool, void* v_pool, int kv_dtype, int n_l
                                          static_cast<unsigned char*>(workspace), n_layers, capacity, kv_heads, max_len,
                                          row_bytes_pos, targets, count, length, 0);
   return check_launch("kv_stage_kernel(scatter)");
+}
+
+// ---------------------------------------------------------------------------------------
+// Row copies without any allocation.
+//
+// Some callers cannot allocate device memory around a copy: a collector loop that steps
+// games on the host while the device works cannot afford cudaMalloc (it synchronizes the
+// device), and a host embedding this library through its C ABI may have no allocator of
+// its own (the device memory belongs to another framework's pool). For them the staging
+// buffer lives in this file-scope array, which every GPU that loads the library holds
+// until the process exits.
+// ---------------------------------------------------------------------------------------
+namespace {
+constexpr int64_t kNoAllocScratchBytes = 16LL << 20;  // 16 MiB
+static __device__ __align__(256) unsigned char g_copy_scratch[kNoAllocScratchBytes];
+
+std::mutex g_scratch_mutex;
+unsigned char* g_scratch_ptr[64] = {nullptr};
+
+// Device address of g_copy_scratch on the current device. The host-side name is only a
+// stand-in for the symbol, so the address is looked up once per device with that device
+// current (the first call on a device does this).
+int scratch_address(unsigned char** out) {
+  int device = 0;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err != cudaSuccess) return cg::set_error(CG_ERR_CUDA, "cg_kv_copy_rows_noalloc: %s", cudaGetErrorString(err));
+  if (device < 0 || device >= 64) return cg::set_error(CG_ERR_ARGUMENT, "cg_kv_copy_rows_noalloc: device %d", device);
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (!g_scratch_ptr[device]) {
+    void* ptr = nullptr;
+    err = cudaGetSymbolAddress(&ptr, g_copy_scratch);
+    if (err != cudaSuccess)
+      return cg::set_error(CG_ERR_CUDA, "cg_kv_copy_rows_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(err));
+    g_scratch_ptr[device] = static_cast<unsigned char*>(ptr);
+  }
+  *out = g_scratch_ptr[device];
+  return CG_OK;
+}
+}  // namespace
+
+extern "C" int64_t cg_kv_copy_rows_noalloc_max_bytes(void) { return kNoAllocScratchBytes; }
+
+extern "C" int cg_kv_copy_rows_noalloc(void* k_pool, void* v_pool, int kv_dtype, int n_layers, int64_t capacity,
+                                       int kv_heads, int max_len, int head_dim, const int64_t* sources,
+                                       const int64_t* targets, int64_t count, int length, void* stream) {
+  using namespace cg;
+  CG_REQUIRE(valid_dtype(kv_dtype), "cg_kv_copy_rows_noalloc: bad dtype");
+  CG_REQUIRE(count >= 0 && length >= 0 && length <= max_len, "cg_kv_copy_rows_noalloc: bad count/length");
+  if (count == 0 || length == 0) return CG_OK;
+  CG_REQUIRE(k_pool && v_pool && sources && targets, "cg_kv_copy_rows_noalloc: NULL pointer");
+  const int64_t row_bytes_pos = static_cast<int64_t>(head_dim) * dtype_size(kv_dtype);
+  const int64_t need = count * n_layers * 2LL * kv_heads * length * row_bytes_pos;
+  if (need > kNoAllocScratchBytes)
+    return set_error(CG_ERR_ARGUMENT,
+                     "cg_kv_copy_rows_noalloc: %lld rows x %d positions need %lld staging bytes, above its fixed "
+                     "%lld-byte buffer; split the copy into smaller calls",
+                     (long long)count, length, (long long)need, (long long)kNoAllocScratchBytes);
+  unsigned char* scratch = nullptr;
+  int rc = scratch_address(&scratch);
+  if (rc) return rc;
+  // The gather writes every staged byte before the scatter reads it: nothing needs clearing.
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int blocks = sm_count() * 8;
+  kv_stage_kernel<<<blocks, 256, 0, s>>>(static_cast<unsigned char*>(k_pool), static_cast<unsigned char*>(v_pool),
+                                         scratch, n_layers, capacity, kv_heads, max_len, row_bytes_pos, sources, count,
+                                         length, 1);
+  if ((rc = check_launch("kv_stage_kernel(gather, no-alloc)"))) return rc;
+  kv_stage_kernel<<<blocks, 256, 0, s>>>(static_cast<unsigned char*>(k_pool), static_cast<unsigned char*>(v_pool),
+                                         scratch, n_layers, capacity, kv_heads, max_len, row_bytes_pos, targets, count,
+                                         length, 0);
+  return check_launch("kv_stage_kernel(scatter, no-alloc)");
 }

@@ -88,6 +88,22 @@ int cg_kv_copy_rows(void* k_pool, void* v_pool, int kv_dtype, int n_layers, int6
                     int max_len, int head_dim, const int64_t* sources, const int64_t* targets, int64_t count,
                     int length, void* workspace, int64_t workspace_bytes, void* stream);
 
+/* cg_kv_copy_rows for callers that cannot allocate device memory (no counterpart in the
+ * reference). A collector loop that overlaps host game stepping with device work cannot
+ * call cudaMalloc, which synchronizes the device, and a host that drives this library
+ * through the C ABI may have no allocator of its own. This variant stages the rows through
+ * a fixed buffer inside the library instead of a caller workspace, and allocates nothing.
+ * Limit: the staged bytes, count * n_layers * 2 * kv_heads * length * head_dim * element
+ * size, must not exceed cg_kv_copy_rows_noalloc_max_bytes() (16 MiB); larger copies are
+ * rejected with CG_ERR_ARGUMENT and should be split into several calls. The buffer is
+ * shared by every call in the process on a device: calls whose copies overlap in time on
+ * the GPU (on different streams) race with each other. The first call on each device
+ * looks up the buffer's device address, so make that first call before any stream capture. */
+int64_t cg_kv_copy_rows_noalloc_max_bytes(void);
+int cg_kv_copy_rows_noalloc(void* k_pool, void* v_pool, int kv_dtype, int n_layers, int64_t capacity, int kv_heads,
+                            int max_len, int head_dim, const int64_t* sources, const int64_t* targets, int64_t count,
+                            int length, void* stream);
+
 /* ---------------------------------------------------------------------------------
  * Trunk weights: one device blob. Its fp32 section holds the reference's parameters
  * (cardgym/nn/trunk.py:124-139,259-270 names) at the offsets below; cg_trunk_prepare
