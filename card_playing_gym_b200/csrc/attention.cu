@@ -6,11 +6,14 @@
 // a KV head is g * T + t (trunk.py:243-254).
 //
 // Two kernels:
-//  * attn_tc: fp16/bf16 caches, head_dim a multiple of 8, G*T <= 16. One warp per
-//    (row, KV head) unit, persistent over units. Each warp streams its unit's keys in
-//    chunks of 64 through a two-stage shared-memory ring filled by bulk async copies
-//    (cp.async.bulk, completion on an mbarrier), computes Q K^T and P V with
-//    mma.sync m16n8k16/k8 (fp32 accumulation) and keeps an online softmax in fp32.
+//  * attn_tc: fp16/bf16 caches, head_dim in {16, 24, 32, 40, 48, 64}, G*T <= 16. One
+//    warp per (row, KV head) unit, persistent over units. Each warp streams its units'
+//    keys in chunks of 64 through a two-stage shared-memory ring filled with 16-byte
+//    cp.async copies (zero-filled past the row's length, L2 evict-first), computes Q K^T
+//    and P V with mma.sync m16n8k16/k8 (fp32 accumulation) and keeps an online softmax
+//    in fp32. Bulk-engine copies (cp.async.bulk) were measured to cost ~0.13 us each on
+//    this part whatever their size below 16 KB, which capped 3 KB K/V chunks near
+//    3.4 TB/s chip-wide; per-lane copies have no such per-copy cost.
 //  * attn_simt: any cache dtype and shape; one warp per (row, query head, step),
 //    fp32 arithmetic. Used for fp32 caches (the strict-parity mode) and shapes the
 //    tensor-core kernel does not take.
@@ -95,75 +98,39 @@ __global__ void __launch_bounds__(128) attn_simt_kernel(AttnParams p) {
 // Tensor-core kernel.
 // ------------------------------------------------------------------------------------
 constexpr int kChunk = 64;   // keys per staged chunk
-constexpr int kStages = 2;   // chunks in flight per warp
+constexpr int kStages = 2;   // chunk stages per warp: one computed while the next loads
 constexpr int kTcWarps = 4;  // warps per CTA
-constexpr uint64_t kWaitLimitNs = 1000000000ull;  // bounded mbarrier wait: 1 s
 
 __device__ __forceinline__ uint32_t smem_addr(const void* ptr) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(ptr));
 }
 
-__device__ __forceinline__ uint64_t global_timer() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t done;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(done)
-      : "r"(smem_addr(bar)), "r"(parity)
-      : "memory");
-  return done != 0;
-}
-
-// Returns false (and records a fault) if the phase does not complete within the limit.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int fault_code) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t start = global_timer();
-  while (!mbar_try_wait(bar, parity)) {
-    if (global_timer() - start > kWaitLimitNs) {
-      raise_fault(fault_code);
-      return false;
-    }
-  }
-  return true;
-}
-
-__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_addr(dst)),
-      "l"(src), "r"(bytes), "r"(smem_addr(bar))
-      : "memory");
-}
-
 // The KV stream is read once per layer: evict it from L2 first so that weights stay resident.
-__device__ __forceinline__ void bulk_copy_g2s_stream(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
-                                                     uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
-          smem_addr(dst)),
-      "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
-      : "memory");
-}
-
 __device__ __forceinline__ uint64_t evict_first_policy() {
   uint64_t policy;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
   return policy;
 }
 
-__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// One 16-byte asynchronous copy global -> shared; valid == false writes 16 zero bytes and reads nothing.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid, uint64_t policy) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2, %3;" ::"r"(smem_addr(dst)), "l"(src),
+               "r"(valid ? 16 : 0), "l"(policy)
+               : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 template <typename T>
 struct MmaOps;
@@ -173,6 +140,9 @@ struct MmaOps<__half> {
   static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
     __half2 v = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&v);
+  }
+  static __device__ __forceinline__ float2 unpack(uint32_t w) {
+    return __half22float2(*reinterpret_cast<__half2*>(&w));
   }
   static __device__ __forceinline__ void k16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
     asm volatile(
@@ -193,6 +163,9 @@ struct MmaOps<__nv_bfloat16> {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&v);
   }
+  static __device__ __forceinline__ float2 unpack(uint32_t w) {
+    return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&w));
+  }
   static __device__ __forceinline__ void k16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
@@ -205,6 +178,16 @@ struct MmaOps<__nv_bfloat16> {
                  : "r"(a0), "r"(a1), "r"(b0));
   }
 };
+
+__device__ __forceinline__ void ldmatrix_x2(uint32_t& r0, uint32_t& r1, uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3, uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
 
 __device__ __forceinline__ void ldmatrix_x2_trans(uint32_t& r0, uint32_t& r1, uint32_t addr) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
@@ -221,6 +204,7 @@ struct TcShape {
   static constexpr int kTiles = D / 16;          // full k16 blocks of Q K^T
   static constexpr bool kTail = (D % 16) != 0;   // one trailing k8 block
   static constexpr int kDTiles = D / 8;          // n8 tiles of the output
+  static constexpr int kPieces = D / 8;          // 16-byte pieces per key row
   static constexpr int kStageElems = kChunk * D; // per K or V
   static constexpr int kWarpBytes = kStages * 2 * kStageElems * static_cast<int>(sizeof(KV));
 };
@@ -237,202 +221,275 @@ __device__ void zero_unit(const AttnParams& p, int64_t b, int kvh, int M, int la
   }
 }
 
-template <typename KV, int D>
+// A warp's walk over (row, KV head) units and their key chunks.
+struct UnitCursor {
+  int64_t unit;
+  int chunk;
+  int keys;  // keys visible to the unit's last query
+};
+
+__device__ __forceinline__ int unit_keys(const AttnParams& p, int64_t unit) {
+  const int64_t b = unit / p.kv_heads;
+  const int64_t last = p.lengths[b] + p.steps - 1;
+  return static_cast<int>(last < p.span ? last : p.span);
+}
+
+constexpr int kRing = 8;  // units claimed ahead by the issue cursor, per warp
+
+// kHalf: G * T <= 8, so rows 8..15 of the m16 tile are padding and are never processed.
+// kBlocked: the output goes to the tile-blocked bf16 operand layout; otherwise it has the
+// cache dtype and q's [B, H, T, D] strides.
+template <typename KV, int D, bool kHalf, bool kBlocked>
 __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
   using Shape = TcShape<KV, D>;
   using Ops = MmaOps<KV>;
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  __shared__ __align__(8) uint64_t bars[kTcWarps][kStages];
-
   const int lane = threadIdx.x & 31;
   const int wib = threadIdx.x >> 5;
   const int gid = lane >> 2, tid4 = lane & 3;
   KV* stage_base = reinterpret_cast<KV*>(smem_raw + wib * Shape::kWarpBytes);
-  if (lane == 0) {
-    for (int s = 0; s < kStages; ++s) mbar_init(&bars[wib][s], 1);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  __syncwarp();
+  const uint64_t policy = evict_first_policy();
 
   const int64_t units = p.batch * p.kv_heads;
-  const int64_t warp0 = static_cast<int64_t>(blockIdx.x) * kTcWarps + wib;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kTcWarps;
   const int M = p.group * p.steps;
   const float scale_log2 = p.scale * 1.4426950408889634f;
+  const KV* kc = static_cast<const KV*>(p.k);
+  const KV* vc = static_cast<const KV*>(p.v);
 
-  // Visible-key count of the unit's last query (the chunk loop bound).
-  auto unit_keys = [&](int64_t unit) -> int {
-    const int64_t b = unit / p.kv_heads;
-    const int64_t last = p.lengths[b] + p.steps - 1;
-    return static_cast<int>(last < p.span ? last : p.span);
-  };
-  auto issue = [&](int64_t unit, int chunk, int keys, int stage) {
-    // Every lane fences its own earlier generic accesses to the stage before the
-    // asynchronous copy overwrites it; lane 0 then issues both copies.
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) {
-      const int64_t b = unit / p.kv_heads;
-      const int kvh = static_cast<int>(unit % p.kv_heads);
-      const int64_t row = p.rows ? p.rows[b] : b;
-      const int first = chunk * kChunk;
-      const int n = min(kChunk, keys - first);
-      const uint32_t bytes = static_cast<uint32_t>(n * D * sizeof(KV));
-      const int64_t off = row * p.kv_row + kvh * p.kv_head + static_cast<int64_t>(first) * p.kv_pos;
-      KV* ks = stage_base + stage * 2 * Shape::kStageElems;
-      mbar_expect_tx(&bars[wib][stage], 2 * bytes);
-      const uint64_t policy = evict_first_policy();
-      bulk_copy_g2s_stream(ks, static_cast<const KV*>(p.k) + off, bytes, &bars[wib][stage], policy);
-      bulk_copy_g2s_stream(ks + Shape::kStageElems, static_cast<const KV*>(p.v) + off, bytes, &bars[wib][stage], policy);
+  // Units are claimed from p.counter (or by a static stride); the issue cursor runs
+  // kStages - 1 chunks ahead of the compute cursor and hands it the claimed units through
+  // a small per-warp ring. Units without visible keys get zero outputs when claimed.
+  __shared__ int64_t ring_unit[kTcWarps][kRing];
+  __shared__ int ring_keys[kTcWarps][kRing];
+  int64_t static_next = static_cast<int64_t>(blockIdx.x) * kTcWarps + wib;
+  int head = 0, tail = 0;
+  auto claim = [&]() -> int64_t {
+    if (p.counter) {
+      long long u = 0;
+      if (lane == 0) u = atomicAdd(p.counter, 1);
+      return __shfl_sync(0xffffffffu, u, 0);
     }
+    const int64_t u = static_next;
+    static_next += stride;
+    return u;
+  };
+  auto issue_next_unit = [&](UnitCursor& c) {
+    c.unit = units;
+    while (true) {
+      const int64_t u = claim();
+      if (u >= units) break;
+      const int k = unit_keys(p, u);
+      if (k <= 0) {
+        zero_unit(p, u / p.kv_heads, static_cast<int>(u % p.kv_heads), M, lane);
+        continue;
+      }
+      c.unit = u;
+      c.keys = k;
+      break;
+    }
+    c.chunk = 0;
+    if (lane == 0) {
+      ring_unit[wib][head % kRing] = c.unit;
+      ring_keys[wib][head % kRing] = c.keys;
+    }
+    ++head;
+  };
+  auto issue_advance = [&](UnitCursor& c) {
+    if (c.unit >= units) return;
+    if (++c.chunk * kChunk < c.keys) return;
+    issue_next_unit(c);
+  };
+  auto compute_advance = [&](UnitCursor& c) {
+    if (++c.chunk * kChunk < c.keys) return;
+    __syncwarp();
+    c.unit = ring_unit[wib][tail % kRing];
+    c.keys = ring_keys[wib][tail % kRing];
+    c.chunk = 0;
+    ++tail;
+  };
+  UnitCursor issue{units, 0, 0};
+  issue_next_unit(issue);
+  UnitCursor comp{0, 0, 0};
+  comp.keys = 0;
+  comp.chunk = -1;
+  compute_advance(comp);  // pops the first claimed unit
+
+  // A chunk of K (and of V) is one contiguous range of n * D elements in the pool and in
+  // the stage; lanes copy it in 16-byte pieces, zero-filled up to the 16-key MMA block.
+  auto issue_chunk = [&](const UnitCursor& c, int stage) {
+    if (c.unit < units) {
+      const int64_t b = c.unit / p.kv_heads;
+      const int kvh = static_cast<int>(c.unit % p.kv_heads);
+      const int64_t row = p.rows ? p.rows[b] : b;
+      const int first = c.chunk * kChunk;
+      const int n = min(kChunk, c.keys - first);
+      const int valid_pieces = n * Shape::kPieces;
+      const int pieces = ((n + 15) & ~15) * Shape::kPieces;
+      const int64_t off = row * p.kv_row + kvh * p.kv_head + static_cast<int64_t>(first) * D;
+      const uint4* ksrc = reinterpret_cast<const uint4*>(kc + off);
+      const uint4* vsrc = reinterpret_cast<const uint4*>(vc + off);
+      uint4* kdst = reinterpret_cast<uint4*>(stage_base + stage * 2 * Shape::kStageElems);
+      uint4* vdst = kdst + Shape::kStageElems * static_cast<int>(sizeof(KV)) / 16;
+      for (int i = lane; i < pieces; i += 32) {
+        const bool valid = i < valid_pieces;
+        cp_async16(kdst + i, ksrc + (valid ? i : 0), valid, policy);
+        cp_async16(vdst + i, vsrc + (valid ? i : 0), valid, policy);
+      }
+    }
+    cp_async_commit();  // one group per chunk slot, empty or not: keeps the group count in step
   };
 
-  // Find this warp's first unit with at least one key.
-  int64_t unit = warp0;
-  int keys = 0;
-  while (unit < units && (keys = unit_keys(unit)) <= 0) {
-    // No visible key: the output is defined as zero.
-    const int64_t b = unit / p.kv_heads;
-    const int kvh = static_cast<int>(unit % p.kv_heads);
-    zero_unit(p, b, kvh, M, lane);
-    unit += stride;
+  int issue_stage = 0;
+#pragma unroll
+  for (int s = 0; s < kStages - 1; ++s) {
+    issue_chunk(issue, issue_stage);
+    issue_advance(issue);
+    issue_stage = issue_stage + 1 == kStages ? 0 : issue_stage + 1;
   }
-  if (unit >= units) return;
-  int chunk = 0, stage = 0;
-  uint32_t phase[kStages] = {0, 0};
-  issue(unit, 0, keys, 0);
 
   uint32_t qa[Shape::kTiles > 0 ? Shape::kTiles : 1][4];
-  uint32_t qt[2];
+  uint32_t qt[2] = {0, 0};
   float o[Shape::kDTiles][4];
   float mrow[2], lrow[2];
   int limit_r[2];
+  int lim_min = 0;
+  int comp_stage = 0;
 
-  while (true) {
-    // Next item: the next chunk of this unit, or the first chunk of the next unit with keys.
-    int64_t next_unit = unit;
-    int next_chunk = chunk + 1, next_keys = keys;
-    if (next_chunk * kChunk >= keys) {
-      next_chunk = 0;
-      next_unit = unit + stride;
-      while (next_unit < units && (next_keys = unit_keys(next_unit)) <= 0) {
-        const int64_t b = next_unit / p.kv_heads;
-        const int kvh = static_cast<int>(next_unit % p.kv_heads);
-        zero_unit(p, b, kvh, M, lane);
-        next_unit += stride;
-      }
-    }
-    const bool has_next = next_unit < units;
-    if (has_next) issue(next_unit, next_chunk, next_keys, stage ^ 1);
+  while (comp.unit < units) {
+    issue_chunk(issue, issue_stage);
+    issue_advance(issue);
+    issue_stage = issue_stage + 1 == kStages ? 0 : issue_stage + 1;
 
-    const int64_t b = unit / p.kv_heads;
-    const int kvh = static_cast<int>(unit % p.kv_heads);
-    if (chunk == 0) {
+    const int64_t b = comp.unit / p.kv_heads;
+    const int kvh = static_cast<int>(comp.unit % p.kv_heads);
+    if (comp.chunk == 0) {
       // Unit start: Q fragments (rows m >= M are zero), softmax state, limits.
-      auto qval = [&](int m, int d) -> float {
-        if (m >= M) return 0.f;
+      const KV* qbase = static_cast<const KV*>(p.q);
+      auto qpair = [&](int m, int c) -> uint32_t {
+        if (m >= M) return 0u;
         const int h = kvh * p.group + m / p.steps, t = m % p.steps;
-        return load_as_float(p.q, b * p.q_sb + h * p.q_sh + t * p.q_st + d, p.q_dtype);
+        return *reinterpret_cast<const uint32_t*>(qbase + b * p.q_sb + h * p.q_sh + t * p.q_st + c);
       };
 #pragma unroll
       for (int kb = 0; kb < Shape::kTiles; ++kb) {
         const int c = kb * 16 + 2 * tid4;
-        qa[kb][0] = Ops::pack(qval(gid, c), qval(gid, c + 1));
-        qa[kb][1] = Ops::pack(qval(gid + 8, c), qval(gid + 8, c + 1));
-        qa[kb][2] = Ops::pack(qval(gid, c + 8), qval(gid, c + 9));
-        qa[kb][3] = Ops::pack(qval(gid + 8, c + 8), qval(gid + 8, c + 9));
+        qa[kb][0] = qpair(gid, c);
+        qa[kb][1] = kHalf ? 0u : qpair(gid + 8, c);
+        qa[kb][2] = qpair(gid, c + 8);
+        qa[kb][3] = kHalf ? 0u : qpair(gid + 8, c + 8);
       }
       if (Shape::kTail) {
         const int c = Shape::kTiles * 16 + 2 * tid4;
-        qt[0] = Ops::pack(qval(gid, c), qval(gid, c + 1));
-        qt[1] = Ops::pack(qval(gid + 8, c), qval(gid + 8, c + 1));
+        qt[0] = qpair(gid, c);
+        qt[1] = kHalf ? 0u : qpair(gid + 8, c);
       }
 #pragma unroll
       for (int j = 0; j < Shape::kDTiles; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+      const int64_t len = p.lengths[b];
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
         const int m = gid + 8 * r;
         // Padding rows (m >= M) attend to every visible key: finite, never stored.
         const int t = m < M ? m % p.steps : p.steps - 1;
-        const int64_t lim = p.lengths[b] + t;
+        const int64_t lim = len + t;
         limit_r[r] = static_cast<int>(lim < p.span ? lim : p.span);
         mrow[r] = -INFINITY;
         lrow[r] = 0.f;
       }
+      lim_min = static_cast<int>(len < p.span ? len : p.span);  // the t = 0 queries see the fewest keys
     }
 
-    if (!mbar_wait_bounded(&bars[wib][stage], phase[stage], 0x100 + wib)) return;
-    phase[stage] ^= 1u;
-    const KV* ks = stage_base + stage * 2 * Shape::kStageElems;
+    cp_async_wait<kStages - 1>();
+    __syncwarp();
+    const KV* ks = stage_base + comp_stage * 2 * Shape::kStageElems;
     const KV* vs = ks + Shape::kStageElems;
-    const int first = chunk * kChunk;
-    const int n = min(kChunk, keys - first);
-    if (n < kChunk && (n & 15)) {
-      // Zero the V rows the last partial 16-key block would read: stale shared memory
-      // times a zero probability must not turn into NaN.
-      KV* vz = const_cast<KV*>(vs);
-      const int end = min(kChunk, (n + 15) & ~15);
-      for (int i = n * D + lane; i < end * D; i += 32) vz[i] = KV(0.f);
-      __syncwarp();
-    }
-    const int nblocks = (n + 15) >> 4;  // 16-key blocks with any valid key
+    const int first = comp.chunk * kChunk;
+    const int n = min(kChunk, comp.keys - first);
+    const int nblocks = (n + 15) >> 4;
+    constexpr int kRows = kHalf ? 1 : 2;
+    // Every row sees every processed key of this chunk (a zero-filled tail block needs the mask).
+    const bool full = (n & 15) == 0 && first + n <= lim_min;
 
-    // S = Q K^T over the chunk, masked; online softmax update.
+    // S = Q K^T over the chunk, 16 keys (two n8 tiles) per step; K fragments by ldmatrix.
+    // Scores stay unscaled until the exponent: scale > 0 keeps the max where it is.
     float s[kChunk / 8][4];
     float cmax[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-    for (int j = 0; j < kChunk / 8; ++j) {
-      s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
-      if (j < 2 * nblocks) {
-        const KV* krow = ks + (j * 8 + gid) * D;
+    for (int kk = 0; kk < kChunk / 16; ++kk) {
+      float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
+      if (kk < nblocks) {
+        const KV* kbase = ks + (kk * 16 + (lane & 15)) * D;
 #pragma unroll
         for (int kb = 0; kb < Shape::kTiles; ++kb) {
-          const uint32_t b0 = *reinterpret_cast<const uint32_t*>(krow + kb * 16 + 2 * tid4);
-          const uint32_t b1 = *reinterpret_cast<const uint32_t*>(krow + kb * 16 + 8 + 2 * tid4);
-          Ops::k16(s[j], qa[kb], b0, b1);
+          uint32_t r0, r1, r2, r3;
+          ldmatrix_x4(r0, r1, r2, r3, smem_addr(kbase + kb * 16 + (lane >> 4) * 8));
+          Ops::k16(acc0, qa[kb], r0, r2);
+          Ops::k16(acc1, qa[kb], r1, r3);
         }
         if (Shape::kTail) {
-          const uint32_t b0 = *reinterpret_cast<const uint32_t*>(krow + Shape::kTiles * 16 + 2 * tid4);
-          Ops::k8(s[j], qt[0], qt[1], b0);
+          uint32_t r0, r1;
+          ldmatrix_x2(r0, r1, smem_addr(kbase + Shape::kTiles * 16));
+          Ops::k8(acc0, qt[0], qt[1], r0);
+          Ops::k8(acc1, qt[0], qt[1], r1);
         }
       }
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const int key = first + j * 8 + 2 * tid4 + (e & 1);
-        const int r = e >> 1;
-        const float v = key < limit_r[r] ? s[j][e] * scale_log2 : -INFINITY;
-        s[j][e] = v;
-        cmax[r] = fmaxf(cmax[r], v);
+        s[2 * kk][e] = -INFINITY;
+        s[2 * kk + 1][e] = -INFINITY;
+      }
+      if (kk < nblocks) {
+#pragma unroll
+        for (int e = 0; e < 2 * kRows; ++e) {
+          const int r = e >> 1;
+          float v0 = acc0[e], v1 = acc1[e];
+          if (!full) {
+            const int key = first + kk * 16 + 2 * tid4 + (e & 1);
+            v0 = key < limit_r[r] ? v0 : -INFINITY;
+            v1 = key + 8 < limit_r[r] ? v1 : -INFINITY;
+          }
+          s[2 * kk][e] = v0;
+          s[2 * kk + 1][e] = v1;
+          cmax[r] = fmaxf(cmax[r], fmaxf(v0, v1));
+        }
       }
     }
-    float alpha[2];
+    float alpha[2] = {1.f, 1.f};
+    float psum[2] = {0.f, 0.f};
+    float neg_max[2];
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
+    for (int r = 0; r < kRows; ++r) {
       cmax[r] = fmaxf(cmax[r], __shfl_xor_sync(0xffffffffu, cmax[r], 1));
       cmax[r] = fmaxf(cmax[r], __shfl_xor_sync(0xffffffffu, cmax[r], 2));
-      const float m_new = fmaxf(mrow[r], cmax[r]);
-      alpha[r] = m_new == -INFINITY ? 1.f : exp2f(mrow[r] - m_new);
+      const float m_new = fmaxf(mrow[r], cmax[r] * scale_log2);  // running max, in log2 units
+      // A row with no visible key so far keeps m = -inf: its scores are all -inf, so any
+      // finite offset gives p = 0, and its (zero) accumulators need no rescaling.
+      const bool empty = m_new == -INFINITY;
+      alpha[r] = empty ? 1.f : fast_exp2(mrow[r] - m_new);  // exp2(-inf) = 0 on the first chunk
       mrow[r] = m_new;
+      neg_max[r] = empty ? 0.f : -m_new;
     }
-    float psum[2] = {0.f, 0.f};
 #pragma unroll
     for (int j = 0; j < kChunk / 8; ++j) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
+      for (int e = 0; e < 2 * kRows; ++e) {
         const int r = e >> 1;
-        const float pe = s[j][e] == -INFINITY ? 0.f : exp2f(s[j][e] - mrow[r]);
+        const float pe = fast_exp2(fmaf(s[j][e], scale_log2, neg_max[r]));  // masked keys: exp2(-inf) = 0
         s[j][e] = pe;
         psum[r] += pe;
       }
     }
 #pragma unroll
-    for (int r = 0; r < 2; ++r) lrow[r] = lrow[r] * alpha[r] + psum[r];
+    for (int r = 0; r < kRows; ++r) lrow[r] = lrow[r] * alpha[r] + psum[r];
 #pragma unroll
     for (int j = 0; j < Shape::kDTiles; ++j) {
       o[j][0] *= alpha[0];
       o[j][1] *= alpha[0];
-      o[j][2] *= alpha[1];
-      o[j][3] *= alpha[1];
+      if (!kHalf) {
+        o[j][2] *= alpha[1];
+        o[j][3] *= alpha[1];
+      }
     }
 
     // O += P V, 16 keys at a time.
@@ -441,9 +498,9 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
       if (kk < nblocks) {
         uint32_t pa[4];
         pa[0] = Ops::pack(s[2 * kk][0], s[2 * kk][1]);
-        pa[1] = Ops::pack(s[2 * kk][2], s[2 * kk][3]);
+        pa[1] = kHalf ? 0u : Ops::pack(s[2 * kk][2], s[2 * kk][3]);
         pa[2] = Ops::pack(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-        pa[3] = Ops::pack(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+        pa[3] = kHalf ? 0u : Ops::pack(s[2 * kk + 1][2], s[2 * kk + 1][3]);
         const int key = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
 #pragma unroll
         for (int dt = 0; dt < Shape::kDTiles; dt += 2) {
@@ -461,76 +518,85 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
         }
       }
     }
+    __syncwarp();  // every lane is done with this stage before it is refilled
 
-    if (next_chunk == 0) {
+    const bool last_chunk = (comp.chunk + 1) * kChunk >= comp.keys;
+    if (last_chunk) {
       // Unit done: normalise and store rows m < M.
 #pragma unroll
-      for (int r = 0; r < 2; ++r) {
+      for (int r = 0; r < kRows; ++r) {
         lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 1);
         lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 2);
       }
 #pragma unroll
-      for (int r = 0; r < 2; ++r) {
+      for (int r = 0; r < kRows; ++r) {
         const int m = gid + 8 * r;
         if (m < M) {
           const float inv = 1.f / lrow[r];
           const int h = kvh * p.group + m / p.steps, t = m % p.steps;
-          const int64_t ooff = b * p.o_sb + h * p.o_sh + t * p.o_st;
 #pragma unroll
           for (int j = 0; j < Shape::kDTiles; ++j) {
             const int d = j * 8 + 2 * tid4;
-            if (p.out_blocked) {
+            const float x0 = o[j][2 * r] * inv, x1 = o[j][2 * r + 1] * inv;
+            if (kBlocked) {
               // even column pair inside one 8-column chunk: one 32-bit store of two bf16
               const int64_t off = blocked_offset(b * p.steps + t, h * D + d, p.blocked_width);
               *reinterpret_cast<__nv_bfloat162*>(static_cast<__nv_bfloat16*>(p.out) + off) =
-                  __floats2bfloat162_rn(o[j][2 * r] * inv, o[j][2 * r + 1] * inv);
+                  __floats2bfloat162_rn(x0, x1);
             } else {
-              store_from_float(p.out, ooff + d, p.out_dtype, o[j][2 * r] * inv);
-              store_from_float(p.out, ooff + d + 1, p.out_dtype, o[j][2 * r + 1] * inv);
+              KV* out = static_cast<KV*>(p.out) + b * p.o_sb + h * p.o_sh + t * p.o_st + d;
+              *reinterpret_cast<uint32_t*>(out) = Ops::pack(x0, x1);
             }
           }
         }
       }
     }
-    __syncwarp();
-    if (!has_next) break;
-    unit = next_unit;
-    chunk = next_chunk;
-    keys = next_keys;
-    stage ^= 1;
+    compute_advance(comp);
+    comp_stage = comp_stage + 1 == kStages ? 0 : comp_stage + 1;
   }
+  cp_async_wait<0>();  // no copy may still target shared memory when the warp exits
 }
 
-template <typename KV, int D>
+template <typename KV, int D, bool kHalf, bool kBlocked>
 int launch_tc(const AttnParams& p, cudaStream_t stream) {
   using Shape = TcShape<KV, D>;
+  auto kernel = attn_tc_kernel<KV, D, kHalf, kBlocked>;
   const int smem = kTcWarps * Shape::kWarpBytes;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(attn_tc_kernel<KV, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    configured = true;
+  static int per_sm[64] = {0};
+  int device = 0;
+  cudaGetDevice(&device);
+  int& occupancy = per_sm[device & 63];
+  if (!occupancy) {
+    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (err != cudaSuccess) return set_error(CG_ERR_CUDA, "attn_tc_kernel smem: %s", cudaGetErrorString(err));
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occupancy, kernel, kTcWarps * 32, smem);
+    if (occupancy < 1) occupancy = 1;
   }
-  int per_sm = 0;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attn_tc_kernel<KV, D>, kTcWarps * 32, smem);
-  if (per_sm < 1) per_sm = 1;
   const int64_t units = p.batch * p.kv_heads;
-  int64_t blocks = static_cast<int64_t>(sm_count()) * per_sm;
+  int64_t blocks = static_cast<int64_t>(sm_count()) * occupancy;
   const int64_t needed = (units + kTcWarps - 1) / kTcWarps;
   if (blocks > needed) blocks = needed;
   if (blocks < 1) return CG_OK;
-  attn_tc_kernel<KV, D><<<static_cast<unsigned>(blocks), kTcWarps * 32, smem, stream>>>(p);
+  kernel<<<static_cast<unsigned>(blocks), kTcWarps * 32, smem, stream>>>(p);
   return check_launch("attn_tc_kernel");
+}
+
+template <typename KV, int D>
+int dispatch_layout(const AttnParams& p, cudaStream_t stream) {
+  const bool half = p.group * p.steps <= 8;
+  if (p.out_blocked) return half ? launch_tc<KV, D, true, true>(p, stream) : launch_tc<KV, D, false, true>(p, stream);
+  return half ? launch_tc<KV, D, true, false>(p, stream) : launch_tc<KV, D, false, false>(p, stream);
 }
 
 template <typename KV>
 int dispatch_tc(const AttnParams& p, cudaStream_t stream) {
   switch (p.head_dim) {
-    case 16: return launch_tc<KV, 16>(p, stream);
-    case 24: return launch_tc<KV, 24>(p, stream);
-    case 32: return launch_tc<KV, 32>(p, stream);
-    case 40: return launch_tc<KV, 40>(p, stream);
-    case 48: return launch_tc<KV, 48>(p, stream);
-    case 64: return launch_tc<KV, 64>(p, stream);
+    case 16: return dispatch_layout<KV, 16>(p, stream);
+    case 24: return dispatch_layout<KV, 24>(p, stream);
+    case 32: return dispatch_layout<KV, 32>(p, stream);
+    case 40: return dispatch_layout<KV, 40>(p, stream);
+    case 48: return dispatch_layout<KV, 48>(p, stream);
+    case 64: return dispatch_layout<KV, 64>(p, stream);
     default: return -1;
   }
 }
@@ -540,10 +606,16 @@ bool tc_eligible(const AttnParams& p) {
   if (p.group * p.steps > 16) return false;
   const int d = p.head_dim;
   if (!(d == 16 || d == 24 || d == 32 || d == 40 || d == 48 || d == 64)) return false;
-  // Bulk copies need 16-byte aligned sources: contiguous key rows, aligned row/head strides.
+  // q (and the non-blocked output) in the cache dtype, with even element strides for 32-bit pair access.
+  if (p.q_dtype != p.kv_dtype) return false;
+  if (!p.out_blocked && p.out_dtype != p.kv_dtype) return false;
+  if ((p.q_sb | p.q_sh | p.q_st) & 1) return false;
+  if (!p.out_blocked && ((p.o_sb | p.o_sh | p.o_st) & 1)) return false;
+  // 16-byte copies: contiguous key rows, aligned row/head strides and bases.
   if (p.kv_pos != d) return false;
   if ((p.kv_row % 8) || (p.kv_head % 8)) return false;
   if ((reinterpret_cast<uintptr_t>(p.k) & 15) || (reinterpret_cast<uintptr_t>(p.v) & 15)) return false;
+  if (reinterpret_cast<uintptr_t>(p.q) & 3 || reinterpret_cast<uintptr_t>(p.out) & 3) return false;
   return true;
 }
 

@@ -13,7 +13,8 @@ int run_tc_forward(const cg_trunk_dims& dims, const void* blob, const BlobLayout
                    const int64_t* positions, const int64_t* key_lengths, const int64_t* rows, int span, void* k_pool,
                    void* v_pool, int kv_dtype, int64_t capacity, int max_len, const float* lookup, int lookup_width,
                    const float* x_in, const float* ple_in, const float* val_in, unsigned char* scratch,
-                   int64_t scratch_bytes, const int64_t* readout_offsets, float* hidden_out, cudaStream_t s);
+                   int64_t scratch_bytes, const int64_t* readout_offsets, float* hidden_out, int* attn_counters,
+                   cudaStream_t s);
 int64_t tc_layers_scratch_bytes(const cg_trunk_dims& dims, int64_t batch, int steps);
 bool tc_layers_available(const cg_trunk_dims& dims);
 int tc_pack(const cg_trunk_dims& dims, void* blob, const BlobLayout& L, cudaStream_t stream);
@@ -226,9 +227,12 @@ __global__ void ple_add_kernel(float* x, const float* __restrict__ ple, int64_t 
   }
 }
 
-__global__ void key_lengths_kernel(const int64_t* positions, int64_t* key_lengths, int64_t batch) {
+// Key lengths (positions + 1) and zeroed per-layer attention work counters.
+__global__ void key_lengths_kernel(const int64_t* positions, int64_t* key_lengths, int64_t batch, int* counters,
+                                   int n_counters) {
   const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   if (i < batch) key_lengths[i] = positions[i] + 1;
+  if (i < n_counters) counters[i] = 0;
 }
 
 inline unsigned grid_for(int64_t total, int threads = 256) {
@@ -253,6 +257,7 @@ struct StepWorkspace {
   void* q;        // [B, H, T, D] fp32 or cache dtype
   float* attn;    // [B, T, H, D]
   int64_t* key_lengths;  // [B]
+  int* attn_counters;    // [kMaxLayers]: one work counter per layer's attention launch
   unsigned char* tc;     // tensor-core path scratch
   int64_t tc_bytes;
   int64_t total;
@@ -270,6 +275,7 @@ StepWorkspace plan_step(const cg_trunk_dims& dims, int64_t batch, int steps, int
   };
   w.x = reinterpret_cast<float*>(take(nt * d * 4));
   w.key_lengths = reinterpret_cast<int64_t*>(take(batch * 8));
+  w.attn_counters = reinterpret_cast<int*>(take(64 * sizeof(int)));
   if (precision == CG_PREC_BF16 && tc_layers_available(dims)) {
     w.tc_bytes = tc_layers_scratch_bytes(dims, batch, steps);
     w.tc = take(w.tc_bytes);
@@ -334,6 +340,7 @@ int run_fp32_layers(const cg_trunk_dims& dims, const void* blob, const BlobLayou
     p.kv_row = static_cast<int64_t>(KVH) * max_len * D;
     p.rows = rows;
     p.lengths = w.key_lengths;
+    p.counter = w.attn_counters + layer;
     p.batch = batch;
     p.heads = H;
     p.kv_heads = KVH;
@@ -396,12 +403,13 @@ int forward_ragged_impl(const cg_trunk_dims* dims_p, const void* blob, const flo
                      (long long)w.total);
   const BlobLayout L = blob_layout(dims);
   const int64_t nt = batch * steps;
-  key_lengths_kernel<<<static_cast<unsigned>((batch + 255) / 256), 256, 0, s>>>(positions, w.key_lengths, batch);
+  key_lengths_kernel<<<static_cast<unsigned>((batch + 255) / 256), 256, 0, s>>>(positions, w.key_lengths, batch,
+                                                                                  w.attn_counters, 64);
   if ((rc = check_launch("key_lengths_kernel"))) return rc;
   if (precision == CG_PREC_BF16 && tc_layers_available(dims)) {
     return run_tc_forward(dims, blob, L, batch, steps, positions, w.key_lengths, rows, span, k_pool, v_pool, kv_dtype,
                           capacity, max_len, lookup, lookup_width, x_in, ple, values, w.tc, w.tc_bytes,
-                          readout_offsets, hidden_out, s);
+                          readout_offsets, hidden_out, w.attn_counters, s);
   }
   CG_REQUIRE(!lookup, "internal: the CUDA-core path takes conditioned inputs");
   if (!x_in_workspace) {

@@ -26,6 +26,9 @@ struct AttnParams {
   // W = blocked_width (= heads * head_dim).
   int out_blocked;
   int blocked_width;
+  // Dynamic work distribution: warps claim (row, KV head) units from this counter, which
+  // must be zero at launch (nullptr: a static stride over the units).
+  int* counter;
 };
 
 __host__ __device__ inline int64_t blocked_offset(int64_t r, int k, int width) {

@@ -756,7 +756,8 @@ int run_tc_forward(const cg_trunk_dims& dims, const void* blob, const BlobLayout
                    const int64_t* positions, const int64_t* key_lengths, const int64_t* rows, int span, void* k_pool,
                    void* v_pool, int kv_dtype, int64_t capacity, int max_len, const float* lookup, int lookup_width,
                    const float* x_in, const float* ple_in, const float* val_in, unsigned char* scratch,
-                   int64_t scratch_bytes, const int64_t* readout_offsets, float* hidden_out, cudaStream_t s) {
+                   int64_t scratch_bytes, const int64_t* readout_offsets, float* hidden_out, int* attn_counters,
+                   cudaStream_t s) {
   TcScratch w = plan_tc(dims, batch, steps, scratch);
   if (scratch_bytes < w.total) return set_error(CG_ERR_WORKSPACE, "tensor-core scratch too small");
   const int d = dims.d_model, f = dims.d_ff, H = dims.n_heads, KVH = dims.n_kv_heads, D = head_dim(dims);
@@ -873,6 +874,7 @@ int run_tc_forward(const cg_trunk_dims& dims, const void* blob, const BlobLayout
     a.kv_row = static_cast<int64_t>(KVH) * max_len * D;
     a.rows = rows;
     a.lengths = key_lengths;
+    a.counter = attn_counters + layer;
     a.batch = batch;
     a.heads = H;
     a.kv_heads = KVH;
