@@ -105,6 +105,18 @@ __device__ __forceinline__ void store16(float* base, int64_t tile, int width, in
     *blk(base, tile, width, col + 4 * q, t) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
 }
 
+// 16 consecutive floats from a 16-byte aligned parameter vector.
+__device__ __forceinline__ void load16_vec(const float* src, float (&v)[16]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float4 x = __ldg(reinterpret_cast<const float4*>(src) + q);
+    v[4 * q] = x.x;
+    v[4 * q + 1] = x.y;
+    v[4 * q + 2] = x.z;
+    v[4 * q + 3] = x.w;
+  }
+}
+
 // 16 consecutive columns (col % 16 == 0) of row t as bf16 into the operand layout.
 __device__ __forceinline__ void store_operand16(unsigned char* buf, int col, int t, const float (&v)[16]) {
 #pragma unroll
@@ -185,15 +197,45 @@ __device__ void layer_norm_regs(const float (&x)[kMaxRowChunks][16], int lo, int
   for (int c = 0; c < kMaxRowChunks; ++c) {
     if (lo + c >= hi) continue;
     const int col = (lo + c) * 16;
+    float wv[16], bv[16];
+    load16_vec(w + col, wv);
+    load16_vec(b + col, bv);
     float y[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) y[i] = (x[c][i] - mean) * rstd * w[col + i] + b[col + i];
+    for (int i = 0; i < 16; ++i) y[i] = (x[c][i] - mean) * rstd * wv[i] + bv[i];
     store_operand16(abuf, col, e.t, y);
   }
 }
 
 // ---- the QKV epilogue: q out, K/V (+ value embedding) into the pool ------------------------------------
-__device__ void qkv_epilogue(const TcParams& p, const EpiThread& e, int64_t tile) {
+// Eight consecutive values (a 16-byte fp16/bf16 piece) to base[off..off+7], off % 8 == 0.
+__device__ __forceinline__ void store8(void* base, int64_t off, int dtype, const float* v) {
+  if (dtype == CG_F32) {
+    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(base) + off);
+    dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+    dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+    return;
+  }
+  uint4 packed;
+  uint32_t* words = reinterpret_cast<uint32_t*>(&packed);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (dtype == CG_F16) {
+      __half2 h2 = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+      words[i] = *reinterpret_cast<uint32_t*>(&h2);
+    } else {
+      __nv_bfloat162 h2 = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+      words[i] = *reinterpret_cast<uint32_t*>(&h2);
+    }
+  }
+  *reinterpret_cast<uint4*>(static_cast<uint16_t*>(base) + off) = packed;
+}
+
+// Columns [0, H*D) are q, then K and V (kvw = KVH*D each). With D % 8 == 0 every 8-column
+// piece lies inside one head, so it is 8 contiguous elements of q's [B, H, T, D] layout or
+// of one pool position: one 16-byte store. val_tile: this tile's value-embedding block in
+// shared memory (blocked layout, [kvw/4][128] float4), or null to read it from val_blk.
+__device__ void qkv_epilogue(const TcParams& p, const EpiThread& e, int64_t tile, const float4* val_tile) {
   const int t = e.t;
   const int64_t row = tile * kTile + t;
   const bool valid = row < p.nt;
@@ -206,59 +248,53 @@ __device__ void qkv_epilogue(const TcParams& p, const EpiThread& e, int64_t tile
     cache_row = p.rows ? p.rows[b] : b;
   }
   const int hd = p.H * p.D;
+  // Row bases; a piece adds h * T * D + dd (q) or kvh * max_len * D + dd (K/V).
+  const int64_t q_row = (b * p.H * p.T + tt) * p.D;
+  const int64_t kv_row = (cache_row * p.KVH * p.max_len + pos) * p.D;
+  const int q_head = p.T * p.D, kv_head = p.max_len * p.D;
+  const float4* val_rows = val_tile ? val_tile + t
+                                    : reinterpret_cast<const float4*>(p.val_blk) +
+                                          (static_cast<int64_t>(p.value_index) * p.ntiles + tile) * (p.kvw / 4) * kTile + t;
   int lo, hi;
   part_chunks(p.qw, e.qd, lo, hi);
   for (int c = lo; c < hi; ++c) {
     float v[16];
     tc::tmem_ld16(e.lane_tmem + c * 16, v);
     if (!valid) continue;
-    const int col0 = c * 16;
-    if (p.T == 1 && p.q_dtype != CG_F32 && col0 + 16 <= hd) {
-      // one row's q is contiguous when T == 1: two 16-byte stores
-      uint4 packed[2];
-      uint32_t* words = reinterpret_cast<uint32_t*>(packed);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        if (p.q_dtype == CG_F16) {
-          __half2 h2 = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
-          words[i] = *reinterpret_cast<uint32_t*>(&h2);
-        } else {
-          __nv_bfloat162 h2 = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
-          words[i] = *reinterpret_cast<uint32_t*>(&h2);
-        }
-      }
-      uint4* dst = reinterpret_cast<uint4*>(static_cast<unsigned char*>(p.q) + (b * hd + col0) * 2);
-      dst[0] = packed[0];
-      dst[1] = packed[1];
-      continue;
-    }
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const int col = col0 + i;
+    for (int half = 0; half < 2; ++half) {
+      const int col = c * 16 + half * 8;
+      float* w = v + half * 8;
       if (col < hd) {
-        const int h = col / p.D, dd = col % p.D;
-        store_from_float(p.q, ((b * p.H + h) * p.T + tt) * p.D + dd, p.q_dtype, v[i]);
-      } else {
-        const int cc = col - hd;
-        const int which = cc / p.kvw, rem = cc % p.kvw;
-        const int kvh = rem / p.D, dd = rem % p.D;
-        float value = v[i];
-        if (which == 1 && p.value_index >= 0) {
-          const float4 ev = *blk(p.val_blk, static_cast<int64_t>(p.value_index) * p.ntiles + tile, p.kvw, rem, t);
-          const int lanei = rem & 3;
-          value += lanei == 0 ? ev.x : lanei == 1 ? ev.y : lanei == 2 ? ev.z : ev.w;
-        }
-        const int64_t dst = ((cache_row * p.KVH + kvh) * p.max_len + pos) * p.D + dd;
-        store_from_float(which ? p.v_layer : p.k_layer, dst, p.kv_dtype, value);
+        const int h = col / p.D, dd = col - h * p.D;
+        store8(p.q, q_row + (h * q_head + dd), p.q_dtype, w);
+        continue;
       }
+      const int cc = col - hd;
+      const int which = cc >= p.kvw ? 1 : 0;
+      const int rem = cc - which * p.kvw;
+      const int kvh = rem / p.D, dd = rem - kvh * p.D;
+      if (which && p.value_index >= 0) {
+        const float4 e0 = val_rows[(rem / 4) * kTile];
+        const float4 e1 = val_rows[(rem / 4 + 1) * kTile];
+        w[0] += e0.x;
+        w[1] += e0.y;
+        w[2] += e0.z;
+        w[3] += e0.w;
+        w[4] += e1.x;
+        w[5] += e1.y;
+        w[6] += e1.z;
+        w[7] += e1.w;
+      }
+      store8(which ? p.v_layer : p.k_layer, kv_row + (kvh * kv_head + dd), p.kv_dtype, w);
     }
   }
 }
 
 // ---- epilogue warps ----------------------------------------------------------------------------------------
 __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned char* hbuf, uint32_t tmem,
-                               uint64_t* a_ready_bar, uint64_t* acc_ready_bar, uint64_t* attn_full_bar, int abytes,
-                               float (*red)[kTile]) {
+                               uint64_t* a_ready_bar, uint64_t* acc_ready_bar, uint64_t* attn_full_bar,
+                               uint64_t* val_full_bar, int abytes, float (*red)[kTile]) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t tile = blockIdx.x;
   EpiThread e;
@@ -305,7 +341,8 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
       if (lo + c < hi) load16(p.x_blk, tile, d, (lo + c) * 16, t, x[c]);
     if (!group_wait(attn_full_bar, 0, 0x404)) return;
     publish();
-    // E1: x += out_proj; LN_mlp(x) -> A.
+    // E1: x += out_proj (written back: the MLP phase runs without the row in registers);
+    // LN_mlp(x) -> A.
     if (!wait_acc()) return;
 #pragma unroll
     for (int c = 0; c < kMaxRowChunks; ++c) {
@@ -313,6 +350,7 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
       tc::tmem_ld16(e.lane_tmem + p.ops[0].tmem_col + (lo + c) * 16, v16);
 #pragma unroll
       for (int i = 0; i < 16; ++i) x[c][i] += v16[i];
+      store16(p.x_blk, tile, d, (lo + c) * 16, t, x[c]);
     }
     layer_norm_regs(x, lo, hi, d, e, p.ln_mlp_w, p.ln_mlp_b, abuf, red);
     publish();
@@ -324,21 +362,32 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
       for (int c = 0; c < kMaxRowChunks; ++c) {
         if (lo + c >= hi) continue;
         const int col = (lo + c) * 16;
+        float bias[16];
+        load16_vec(p.up_b + uc * d + col, bias);
         tc::tmem_ld16(e.lane_tmem + 256 + col, v16);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) v16[i] = gelu_erf(v16[i] + p.up_b[uc * d + col + i]);
+        for (int i = 0; i < 16; ++i) v16[i] = gelu_erf(v16[i] + bias[i]);
         store_operand16(hbuf, col, t, v16);
       }
       publish();
     }
     // E3: x += down + b; x += PLE(l); store; then LN_attn(l+1) -> A.
-    // The PLE update and the bias do not depend on the GEMM: fold them into x first.
+    // The residual (this thread's own E1 stores), the PLE update and the bias do not
+    // depend on the GEMM: fold them into x while it runs. (Every x[c] is redefined here, so
+    // the row is dead in registers from E1's stores to this point.)
 #pragma unroll
     for (int c = 0; c < kMaxRowChunks; ++c) {
-      if (lo + c >= hi) continue;
-      const int col = (lo + c) * 16;
+      if (lo + c >= hi) {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) x[c][i] += p.down_b[col + i];
+        for (int i = 0; i < 16; ++i) x[c][i] = 0.f;
+        continue;
+      }
+      const int col = (lo + c) * 16;
+      load16(p.x_blk, tile, d, col, t, x[c]);
+      float bias[16];
+      load16_vec(p.down_b + col, bias);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) x[c][i] += bias[i];
       if (p.P) {
 #pragma unroll
         for (int i = 0; i < 16; i += 4) {
@@ -352,6 +401,15 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
       }
     }
     if (!wait_acc()) return;
+    // Every GEMM that reads H has completed: H takes the next layer's value-embedding tile.
+    const int vbytes = kTile * p.kvw * 4;
+    const bool val_smem = p.has_next && p.value_index >= 0 && vbytes <= abytes;
+    if (val_smem && threadIdx.x == 0) {
+      tc::bar_expect_tx(val_full_bar, vbytes);
+      tc::bulk_g2s(hbuf, reinterpret_cast<const unsigned char*>(p.val_blk) +
+                             (static_cast<int64_t>(p.value_index) * p.ntiles + tile) * vbytes,
+                   vbytes, val_full_bar);
+    }
 #pragma unroll
     for (int c = 0; c < kMaxRowChunks; ++c) {
       if (lo + c >= hi) continue;
@@ -364,8 +422,9 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
     if (p.has_next) {
       layer_norm_regs(x, lo, hi, d, e, p.ln_next_w, p.ln_next_b, abuf, red);
       publish();
+      if (val_smem && !group_wait(val_full_bar, 0, 0x405)) return;
       if (!wait_acc()) return;
-      qkv_epilogue(p, e, tile);
+      qkv_epilogue(p, e, tile, val_smem ? reinterpret_cast<const float4*>(hbuf) : nullptr);
     }
     return;
   }
@@ -454,14 +513,14 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
   layer_norm_regs(x, lo, hi, d, e, p.ln_next_w, p.ln_next_b, abuf, red);
   publish();
   if (!wait_acc()) return;
-  qkv_epilogue(p, e, tile);
+  qkv_epilogue(p, e, tile, nullptr);  // the value streams were written by this CTA just above
 }
 
 // ---- the kernel ------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(kTcThreads, 1) tc_dense_kernel(const __grid_constant__ TcParams p) {
   extern __shared__ __align__(1024) unsigned char smem[];
   __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages];
-  __shared__ __align__(8) uint64_t a_ready, acc_ready, attn_full;
+  __shared__ __align__(8) uint64_t a_ready, acc_ready, attn_full, val_full;
   __shared__ uint32_t tmem_base;
   __shared__ float red[2 * kParts + 1][kTile];  // row reductions across a row's threads; last row: wait status
 
@@ -479,6 +538,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dense_kernel(const __grid_co
     tc::bar_init(&a_ready, 1);
     tc::bar_init(&acc_ready, 1);
     tc::bar_init(&attn_full, 1);
+    tc::bar_init(&val_full, 1);
     tc::bar_fence_init();
   }
   if (warp == kMmaWarp) {
@@ -562,7 +622,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dense_kernel(const __grid_co
       }
     }
   } else {
-    dense_epilogue(p, abuf, hbuf, tmem, &a_ready, &acc_ready, &attn_full, abytes, red);
+    dense_epilogue(p, abuf, hbuf, tmem, &a_ready, &acc_ready, &attn_full, &val_full, abytes, red);
   }
   tc::fence_before_sync();
   __syncthreads();
