@@ -72,70 +72,172 @@ __global__ void masked_sample_kernel(const float* __restrict__ logits, const uin
               probs_out ? probs_out + row * width : nullptr, actions_out + row);
 }
 
-// One CTA (4 warps) per decision.
-__global__ void __launch_bounds__(128) decide_kernel(cg_heads_desc desc, const float* __restrict__ blob,
-                                                      const float* __restrict__ hidden,
-                                                      const int64_t* __restrict__ hidden_rows, int64_t decisions,
-                                                      const int32_t* __restrict__ head_of,
-                                                      const uint8_t* __restrict__ legal,
-                                                      const double* __restrict__ uniforms, float* logits_out,
-                                                      float* probs_out, int64_t* actions_out, float* values_out) {
-  extern __shared__ float sm[];
+// ---- decisions in tiles --------------------------------------------------------------------------------
+// One CTA takes kDecTile decisions. Every weight row the tile needs — the value MLP's first
+// layer (d rows) and every policy head's rows — forms one fused fp32 GEMM
+//   out[i, r] = sum_k hidden[i, k] * row_r[k]
+// whose weights are staged through shared memory once per CTA in k-slices (instead of once
+// per decision), then each decision picks its head's columns. The GEMM computes the logits of
+// heads a decision does not use; for the plump heads that is 63 extra rows next to 240.
+constexpr int kDecTile = 32;                 // decisions per CTA
+constexpr int kDecWarps = 8;                 // warp w owns decisions 4w .. 4w+3 of the tile
+constexpr int kDecThreads = kDecWarps * 32;
+constexpr int kDecK = 16;                    // k-slice of staged weights
+constexpr int kDecJ = 10;                    // output columns per lane per pass
+constexpr int kDecCols = 32 * kDecJ;         // output columns per pass
+constexpr int kDecStage = kDecCols * kDecK / kDecThreads;  // staged weights per thread per slice
+constexpr int kDecHStride = kDecTile + 4;    // h_s row stride (floats): float4-aligned, fewer conflicts
+
+struct DecideGeometry {
+  int n_value;  // rows of the value MLP's first layer in the GEMM (d, or 0 without values)
+  int n_rows;   // GEMM output columns: n_value + sum of head widths
+  int out_stride;
+  int d_pad;    // d rounded up to kDecK
+  int head_base[8];
+};
+
+__host__ __device__ inline size_t decide_smem_bytes(const DecideGeometry& g, int max_width) {
+  return static_cast<size_t>(g.d_pad) * kDecHStride * 4     // h_s
+         + static_cast<size_t>(kDecK) * kDecCols * 4        // w_s
+         + static_cast<size_t>(kDecTile) * g.out_stride * 4 // out_s
+         + static_cast<size_t>(g.n_rows + kDecCols) * 8     // row offsets
+         + static_cast<size_t>(kDecWarps) * max_width * 9;  // per-warp logits, probs, mask
+}
+
+__global__ void __launch_bounds__(kDecThreads) decide_kernel(cg_heads_desc desc, DecideGeometry g,
+                                                              const float* __restrict__ blob,
+                                                              const float* __restrict__ hidden,
+                                                              const int64_t* __restrict__ hidden_rows,
+                                                              int64_t decisions, const int32_t* __restrict__ head_of,
+                                                              const uint8_t* __restrict__ legal,
+                                                              const double* __restrict__ uniforms, float* logits_out,
+                                                              float* probs_out, int64_t* actions_out,
+                                                              float* values_out) {
+  extern __shared__ __align__(16) unsigned char dec_smem[];
   const int d = desc.d_model, W = desc.max_width;
-  float* h = sm;                // [d]
-  float* hid = h + d;           // [d] value MLP hidden
-  float* logit_s = hid + d;     // [W]
-  float* probs_s = logit_s + W; // [W]
-  const int64_t i = blockIdx.x;
-  if (i >= decisions) return;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t src = hidden_rows ? hidden_rows[i] : i;
-  for (int k = threadIdx.x; k < d; k += blockDim.x) h[k] = hidden[src * d + k];
-  __syncthreads();
-  const int head = head_of ? head_of[i] : 0;
-  const bool head_ok = head >= 0 && head < desc.n_policy;
-  if (!head_ok && threadIdx.x == 0) raise_fault(0x300);
-  const int A = head_ok ? desc.width[head] : 0;
-  const float* Wh = blob + (head_ok ? desc.weight_offset[head] : 0);
-  const float* bh = blob + (head_ok ? desc.bias_offset[head] : 0);
-  for (int a = warp; a < W; a += 4) {
-    float acc = 0.f;
-    if (a < A) {
-      for (int k = lane; k < d; k += 32) acc = fmaf(Wh[static_cast<int64_t>(a) * d + k], h[k], acc);
-      acc = warp_sum(acc) + bh[a];
+  float* h_s = reinterpret_cast<float*>(dec_smem);             // [d_pad][kDecHStride], column i = decision
+  float* w_s = h_s + static_cast<size_t>(g.d_pad) * kDecHStride;  // [kDecK][kDecCols]
+  float* out_s = w_s + kDecK * kDecCols;                         // [kDecTile][out_stride]
+  int64_t* row_off = reinterpret_cast<int64_t*>(out_s + static_cast<size_t>(kDecTile) * g.out_stride);
+  float* logit_w = reinterpret_cast<float*>(row_off + g.n_rows + kDecCols);  // [kDecWarps][W]
+  float* probs_w = logit_w + kDecWarps * W;                                 // [kDecWarps][W]
+  uint8_t* mask_w = reinterpret_cast<uint8_t*>(probs_w + kDecWarps * W);  // [kDecWarps][W]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kDecTile;
+  const int tile_n = static_cast<int>(decisions - base < kDecTile ? decisions - base : kDecTile);
+
+  // Blob offset of each GEMM row (-1: padding column).
+  for (int r = tid; r < g.n_rows + kDecCols; r += kDecThreads) {
+    int64_t off = -1;
+    if (r < g.n_value) {
+      off = desc.value_w1 + static_cast<int64_t>(r) * d;
+    } else if (r < g.n_rows) {
+      for (int h = 0; h < desc.n_policy; ++h) {
+        const int a = r - g.head_base[h];
+        if (a >= 0 && a < desc.width[h]) off = desc.weight_offset[h] + static_cast<int64_t>(a) * d;
+      }
     }
-    if (lane == 0) {
-      logit_s[a] = a < A ? acc : -INFINITY;
-      if (logits_out) logits_out[i * W + a] = a < A ? acc : 0.f;
+    row_off[r] = off;
+  }
+  // The tile's hidden rows, transposed (k-major) and zero-padded.
+  for (int idx = tid; idx < kDecTile * g.d_pad; idx += kDecThreads) {
+    const int i = idx / g.d_pad, k = idx - i * g.d_pad;
+    float v = 0.f;
+    if (i < tile_n && k < d) {
+      const int64_t src = hidden_rows ? hidden_rows[base + i] : base + i;
+      v = hidden[src * d + k];
+    }
+    h_s[k * kDecHStride + i] = v;
+  }
+  __syncthreads();
+
+  for (int col0 = 0; col0 < g.n_rows; col0 += kDecCols) {
+    float acc[4][kDecJ];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int j = 0; j < kDecJ; ++j) acc[r][j] = 0.f;
+    float next[kDecStage];
+    auto fetch = [&](int k0) {  // element (kk, c) of the slice: c = idx % kDecCols, kk = idx / kDecCols
+#pragma unroll
+      for (int m = 0; m < kDecStage; ++m) {
+        const int idx = tid + m * kDecThreads;
+        const int c = idx % kDecCols, kk = idx / kDecCols;
+        const int64_t off = row_off[col0 + c];
+        next[m] = (off >= 0 && k0 + kk < d) ? __ldg(blob + off + k0 + kk) : 0.f;
+      }
+    };
+    fetch(0);
+    for (int k0 = 0; k0 < g.d_pad; k0 += kDecK) {
+#pragma unroll
+      for (int m = 0; m < kDecStage; ++m) w_s[tid + m * kDecThreads] = next[m];
+      __syncthreads();
+      if (k0 + kDecK < g.d_pad) fetch(k0 + kDecK);  // in flight during the slice's FMAs
+#pragma unroll
+      for (int kk = 0; kk < kDecK; ++kk) {
+        const float4 hv = *reinterpret_cast<const float4*>(h_s + (k0 + kk) * kDecHStride + 4 * warp);
+        const float hr[4] = {hv.x, hv.y, hv.z, hv.w};
+#pragma unroll
+        for (int j = 0; j < kDecJ; ++j) {
+          const float wv = w_s[kk * kDecCols + lane + 32 * j];
+#pragma unroll
+          for (int r = 0; r < 4; ++r) acc[r][j] = fmaf(hr[r], wv, acc[r][j]);
+        }
+      }
+      __syncthreads();
+    }
+#pragma unroll
+    for (int j = 0; j < kDecJ; ++j) {
+      const int col = col0 + lane + 32 * j;
+      if (col < g.n_rows)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) out_s[(4 * warp + r) * g.out_stride + col] = acc[r][j];
     }
   }
   __syncthreads();
-  if (warp == 0) {
-    // Entries past the head's width are never legal.
-    const uint8_t* mask = legal + i * W;
-    __shared__ uint8_t mask_s[kMaxSampleWidth];
-    for (int a = lane; a < W; a += 32) mask_s[a] = a < A ? mask[a] : 0;
-    __syncwarp();
-    warp_sample(logit_s, mask_s, W, uniforms[i], probs_s, probs_out ? probs_out + i * W : nullptr, actions_out + i);
-  }
-  if (desc.value_outputs > 0 && values_out) {
-    const float* W1 = blob + desc.value_w1;
+
+  // Value MLP: hid = GELU(out[:, :d] + b1) in place, then values = hid W2^T + b2.
+  if (g.n_value > 0) {
     const float* b1 = blob + desc.value_b1;
-    for (int o = warp; o < d; o += 4) {
-      float acc = 0.f;
-      for (int k = lane; k < d; k += 32) acc = fmaf(W1[static_cast<int64_t>(o) * d + k], h[k], acc);
-      acc = warp_sum(acc) + b1[o];
-      if (lane == 0) hid[o] = gelu_erf(acc);
+    for (int idx = tid; idx < tile_n * d; idx += kDecThreads) {
+      const int i = idx / d, o = idx - i * d;
+      float* cell = out_s + i * g.out_stride + o;
+      *cell = gelu_erf(*cell + b1[o]);
     }
     __syncthreads();
     const float* W2 = blob + desc.value_w2;
     const float* b2 = blob + desc.value_b2;
-    for (int o = warp; o < desc.value_outputs; o += 4) {
+    const int V = desc.value_outputs;
+    for (int idx = tid; idx < tile_n * V; idx += kDecThreads) {
+      const int i = idx / V, o = idx - i * V;
+      const float* hid = out_s + i * g.out_stride;
+      const float* w2 = W2 + static_cast<int64_t>(o) * d;
       float acc = 0.f;
-      for (int k = lane; k < d; k += 32) acc = fmaf(W2[static_cast<int64_t>(o) * d + k], hid[k], acc);
-      acc = warp_sum(acc) + b2[o];
-      if (lane == 0) values_out[i * desc.value_outputs + o] = acc;
+      for (int k = 0; k < d; ++k) acc = fmaf(hid[k], w2[k], acc);
+      values_out[(base + i) * V + o] = acc + b2[o];
     }
+  }
+
+  // Policy: warp w takes decisions w, w + 8, ...: its head's columns, mask, sample.
+  float* lw = logit_w + warp * W;
+  float* pw = probs_w + warp * W;
+  uint8_t* mw = mask_w + warp * W;
+  for (int i = warp; i < tile_n; i += kDecWarps) {
+    const int64_t di = base + i;
+    const int head = head_of ? head_of[di] : 0;
+    const bool head_ok = head >= 0 && head < desc.n_policy;
+    if (!head_ok && lane == 0) raise_fault(0x300);
+    const int A = head_ok ? desc.width[head] : 0;
+    const float* bh = blob + (head_ok ? desc.bias_offset[head] : 0);
+    const float* row = out_s + i * g.out_stride + (head_ok ? g.head_base[head] : 0);
+    for (int a = lane; a < W; a += 32) {
+      const float logit = a < A ? row[a] + bh[a] : 0.f;
+      lw[a] = a < A ? logit : -INFINITY;
+      mw[a] = a < A ? legal[di * W + a] : 0;  // entries past the head's width are never legal
+      if (logits_out) logits_out[di * W + a] = logit;
+    }
+    __syncwarp();
+    warp_sample(lw, mw, W, uniforms[di], pw, probs_out ? probs_out + di * W : nullptr, actions_out + di);
   }
 }
 
@@ -167,10 +269,30 @@ extern "C" int cg_plump_decide(const cg_heads_desc* desc, const float* heads_blo
   if (decisions == 0) return CG_OK;
   CG_REQUIRE(heads_blob && hidden && legal && uniforms && actions_out, "cg_plump_decide: NULL pointer");
   CG_REQUIRE(decisions <= 0x7fffffff, "cg_plump_decide: too many decisions");
-  const size_t smem = (2 * desc->d_model + 2 * desc->max_width) * sizeof(float);
-  CG_REQUIRE(smem <= 48 * 1024, "cg_plump_decide: d_model too large");
-  decide_kernel<<<static_cast<unsigned>(decisions), 128, smem, static_cast<cudaStream_t>(stream)>>>(
-      *desc, heads_blob, hidden, hidden_rows, decisions, head_of, legal, uniforms, logits_out, probs_out, actions_out,
-      values_out);
+  DecideGeometry g{};
+  g.n_value = desc->value_outputs > 0 && values_out ? desc->d_model : 0;
+  g.n_rows = g.n_value;
+  for (int h = 0; h < desc->n_policy; ++h) {
+    g.head_base[h] = g.n_rows;
+    g.n_rows += desc->width[h];
+  }
+  g.out_stride = (g.n_rows + 31) / 32 * 32;
+  g.d_pad = (desc->d_model + kDecK - 1) / kDecK * kDecK;
+  const size_t smem = decide_smem_bytes(g, desc->max_width);
+  CG_REQUIRE(smem <= 227 * 1024, "cg_plump_decide: d_model %d with %d GEMM rows needs %zu bytes of shared memory",
+             desc->d_model, g.n_rows, smem);
+  static size_t configured[64] = {0};
+  int device = 0;
+  cudaGetDevice(&device);
+  if (configured[device & 63] < smem) {
+    cudaError_t err = cudaFuncSetAttribute(decide_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(smem));
+    if (err != cudaSuccess) return set_error(CG_ERR_CUDA, "decide_kernel smem: %s", cudaGetErrorString(err));
+    configured[device & 63] = smem;
+  }
+  const unsigned blocks = static_cast<unsigned>((decisions + kDecTile - 1) / kDecTile);
+  decide_kernel<<<blocks, kDecThreads, smem, static_cast<cudaStream_t>(stream)>>>(
+      *desc, g, heads_blob, hidden, hidden_rows, decisions, head_of, legal, uniforms, logits_out, probs_out,
+      actions_out, values_out);
   return check_launch("decide_kernel");
 }

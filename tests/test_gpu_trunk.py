@@ -130,29 +130,36 @@ def test_bf16_ragged_decode_tracks_the_oracle_and_beats_reference_bf16_error(nam
     assert mine_err <= 2.0 * ref_err + 1e-4, (mine_err, ref_err)
 
 
-def test_decide_matches_the_oracle_heads_and_sampler():
+@pytest.mark.parametrize("count,gather", [(4096, False), (77, True), (1, False)])
+def test_decide_matches_the_oracle_heads_and_sampler(count, gather):
+    """Decisions in tiles of 32: full tiles, a ragged last tile, and hidden rows picked by index."""
+
     from card_playing_gym_b200.plump import PlumpActor
 
     config = PlumpModelConfig()
     state = synthetic_plump_actor_state(config, seed=21)
     actor = PlumpActor(config, state, precision="fp32")
     heads = oplump.Heads.from_state(state)
-    rng = np.random.default_rng(4)
-    count = 4096
-    hidden = rng.standard_normal((count, config.d_model)).astype(np.float32)
+    rng = np.random.default_rng(4 + count)
+    source = rng.standard_normal((3 * count if gather else count, config.d_model)).astype(np.float32)
+    pick = rng.choice(source.shape[0], count, replace=False).astype(np.int64) if gather else None
+    hidden = source[pick] if gather else source
     which = rng.integers(0, 2, count).astype(np.int32)
     legal = rng.random((count, 52)) < 0.3
     legal[np.arange(count), rng.integers(0, 11, count)] = True
     legal[which == 0, 11:] = False
     uniforms = rng.random(count)
     logits, probs, actions, values = actor.decide(
-        torch.from_numpy(hidden).cuda(), torch.from_numpy(which).cuda(), torch.from_numpy(legal).cuda(),
-        torch.from_numpy(uniforms).cuda(),
+        torch.from_numpy(source).cuda(), torch.from_numpy(which).cuda(), torch.from_numpy(legal).cuda(),
+        torch.from_numpy(uniforms).cuda(), torch.from_numpy(pick).cuda() if gather else None,
     )
     logits, probs, actions = logits.cpu().numpy(), probs.cpu().numpy(), actions.cpu().numpy()
+    assert not np.any(logits[which == 0, 11:])  # zero past a head's width
     h64 = hidden.astype(np.float64)
     for head, width in ((0, 11), (1, 52)):
         rows = which == head
+        if not rows.any():
+            continue
         expected = heads.policy_logits(h64[rows], ("bid", "play")[head])
         np.testing.assert_allclose(logits[rows, :width], expected, atol=2e-5, rtol=1e-5)
         # The reference samples on the host from these same logits (selfplay.py:539-548).
