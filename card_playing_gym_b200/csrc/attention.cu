@@ -9,7 +9,8 @@
 //  * attn_tc: fp16/bf16 caches, head_dim in {16, 24, 32, 40, 48, 64}, G*T <= 16. One
 //    warp per (row, KV head) unit, persistent over units. Each warp streams its units'
 //    keys in chunks of 64 through a two-stage shared-memory ring filled with 16-byte
-//    cp.async copies (zero-filled past the row's length, L2 evict-first), computes Q K^T
+//    cp.async copies (zero-filled past the row's length, L2 evict-first; a unit's query
+//    rows travel with its first chunk), computes Q K^T
 //    and P V with mma.sync m16n8k16/k8 (fp32 accumulation) and keeps an online softmax
 //    in fp32. Bulk-engine copies (cp.async.bulk) were measured to cost ~0.13 us each on
 //    this part whatever their size below 16 KB, which capped 3 KB K/V chunks near
@@ -179,6 +180,10 @@ struct MmaOps<__nv_bfloat16> {
   }
 };
 
+__device__ __forceinline__ void ldmatrix_x1(uint32_t& r0, uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x1.shared.b16 {%0}, [%1];" : "=r"(r0) : "r"(addr));
+}
+
 __device__ __forceinline__ void ldmatrix_x2(uint32_t& r0, uint32_t& r1, uint32_t addr) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
 }
@@ -199,14 +204,16 @@ __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t& r0, uint32_t& r1, ui
                : "r"(addr));
 }
 
-template <typename KV, int D>
+template <typename KV, int D, bool kHalf>
 struct TcShape {
   static constexpr int kTiles = D / 16;          // full k16 blocks of Q K^T
   static constexpr bool kTail = (D % 16) != 0;   // one trailing k8 block
   static constexpr int kDTiles = D / 8;          // n8 tiles of the output
-  static constexpr int kPieces = D / 8;          // 16-byte pieces per key row
-  static constexpr int kStageElems = kChunk * D; // per K or V
-  static constexpr int kWarpBytes = kStages * 2 * kStageElems * static_cast<int>(sizeof(KV));
+  static constexpr int kPieces = D / 8;          // 16-byte pieces per key (or query) row
+  static constexpr int kQRows = kHalf ? 8 : 16;  // query rows staged (rows >= G*T zero-filled)
+  static constexpr int kChunkElems = kChunk * D; // per K or V
+  static constexpr int kStageElems = 2 * kChunkElems + kQRows * D;  // K, V, then the unit's q
+  static constexpr int kWarpBytes = kStages * kStageElems * static_cast<int>(sizeof(KV));
 };
 
 // Rows with no visible key get a zero output.
@@ -221,18 +228,14 @@ __device__ void zero_unit(const AttnParams& p, int64_t b, int kvh, int M, int la
   }
 }
 
-// A warp's walk over (row, KV head) units and their key chunks.
-struct UnitCursor {
-  int64_t unit;
-  int chunk;
-  int keys;  // keys visible to the unit's last query
+// A claimed (row, KV head) unit: decoded once, handed from the issue cursor to the compute
+// cursor through a small per-warp ring.
+struct TcUnit {
+  int b;     // batch index
+  int kvh;   // KV head
+  int keys;  // keys visible to the unit's last query (> 0)
+  int len;   // min(lengths[b], span): keys visible to its first step
 };
-
-__device__ __forceinline__ int unit_keys(const AttnParams& p, int64_t unit) {
-  const int64_t b = unit / p.kv_heads;
-  const int64_t last = p.lengths[b] + p.steps - 1;
-  return static_cast<int>(last < p.span ? last : p.span);
-}
 
 constexpr int kRing = 8;  // units claimed ahead by the issue cursor, per warp
 
@@ -241,7 +244,7 @@ constexpr int kRing = 8;  // units claimed ahead by the issue cursor, per warp
 // cache dtype and q's [B, H, T, D] strides.
 template <typename KV, int D, bool kHalf, bool kBlocked>
 __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
-  using Shape = TcShape<KV, D>;
+  using Shape = TcShape<KV, D, kHalf>;
   using Ops = MmaOps<KV>;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   const int lane = threadIdx.x & 31;
@@ -250,167 +253,182 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
   KV* stage_base = reinterpret_cast<KV*>(smem_raw + wib * Shape::kWarpBytes);
   const uint64_t policy = evict_first_policy();
 
-  const int64_t units = p.batch * p.kv_heads;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * kTcWarps;
+  const int units = static_cast<int>(p.batch * p.kv_heads);  // < 2^31: checked by the host
   const int M = p.group * p.steps;
   const float scale_log2 = p.scale * 1.4426950408889634f;
   const KV* kc = static_cast<const KV*>(p.k);
   const KV* vc = static_cast<const KV*>(p.v);
+  const KV* qg = static_cast<const KV*>(p.q);
 
-  // Units are claimed from p.counter (or by a static stride); the issue cursor runs
-  // kStages - 1 chunks ahead of the compute cursor and hands it the claimed units through
-  // a small per-warp ring. Units without visible keys get zero outputs when claimed.
-  __shared__ int64_t ring_unit[kTcWarps][kRing];
-  __shared__ int ring_keys[kTcWarps][kRing];
-  int64_t static_next = static_cast<int64_t>(blockIdx.x) * kTcWarps + wib;
+  // Units are claimed from p.counter (or by a static stride). The issue cursor runs
+  // kStages - 1 chunks ahead of the compute cursor and passes each claimed unit on through
+  // the ring. Units without visible keys get zero outputs when claimed.
+  __shared__ int4 ring[kTcWarps][kRing];
+  int static_next = blockIdx.x * kTcWarps + wib;
+  const int stride = gridDim.x * kTcWarps;
   int head = 0, tail = 0;
-  auto claim = [&]() -> int64_t {
-    if (p.counter) {
-      long long u = 0;
-      if (lane == 0) u = atomicAdd(p.counter, 1);
-      return __shfl_sync(0xffffffffu, u, 0);
-    }
-    const int64_t u = static_next;
-    static_next += stride;
-    return u;
-  };
-  auto issue_next_unit = [&](UnitCursor& c) {
-    c.unit = units;
+  auto claim = [&](TcUnit& u) -> bool {
     while (true) {
-      const int64_t u = claim();
-      if (u >= units) break;
-      const int k = unit_keys(p, u);
-      if (k <= 0) {
-        zero_unit(p, u / p.kv_heads, static_cast<int>(u % p.kv_heads), M, lane);
+      int x;
+      if (p.counter) {
+        int v = 0;
+        if (lane == 0) v = atomicAdd(p.counter, 1);
+        x = __shfl_sync(0xffffffffu, v, 0);
+      } else {
+        x = static_next;
+        static_next += stride;
+      }
+      if (x >= units) return false;
+      const int b = x / p.kv_heads, kvh = x - b * p.kv_heads;
+      const int64_t len = p.lengths[b];
+      const int64_t last = len + p.steps - 1;
+      const int keys = static_cast<int>(last < p.span ? last : p.span);
+      if (keys <= 0) {
+        zero_unit(p, b, kvh, M, lane);
         continue;
       }
-      c.unit = u;
-      c.keys = k;
-      break;
+      u.b = b;
+      u.kvh = kvh;
+      u.keys = keys;
+      u.len = static_cast<int>(len < p.span ? len : p.span);
+      return true;
     }
-    c.chunk = 0;
-    if (lane == 0) {
-      ring_unit[wib][head % kRing] = c.unit;
-      ring_keys[wib][head % kRing] = c.keys;
+  };
+
+  // Issue cursor.
+  bool issue_live = true;
+  TcUnit iu{0, 0, 0, 0};
+  int issue_chunk_no = 0;
+  int64_t issue_kv = 0;  // element offset of the unit's (row, KV head) block in the pool
+  auto issue_next_unit = [&]() {
+    issue_live = claim(iu);
+    issue_chunk_no = 0;
+    if (issue_live) {
+      const int64_t row = p.rows ? p.rows[iu.b] : iu.b;
+      issue_kv = row * p.kv_row + iu.kvh * p.kv_head;
     }
+    if (lane == 0) ring[wib][head % kRing] = issue_live ? make_int4(iu.b, iu.kvh, iu.keys, iu.len)
+                                                        : make_int4(0, 0, 0, -1);
     ++head;
   };
-  auto issue_advance = [&](UnitCursor& c) {
-    if (c.unit >= units) return;
-    if (++c.chunk * kChunk < c.keys) return;
-    issue_next_unit(c);
-  };
-  auto compute_advance = [&](UnitCursor& c) {
-    if (++c.chunk * kChunk < c.keys) return;
-    __syncwarp();
-    c.unit = ring_unit[wib][tail % kRing];
-    c.keys = ring_keys[wib][tail % kRing];
-    c.chunk = 0;
-    ++tail;
-  };
-  UnitCursor issue{units, 0, 0};
-  issue_next_unit(issue);
-  UnitCursor comp{0, 0, 0};
-  comp.keys = 0;
-  comp.chunk = -1;
-  compute_advance(comp);  // pops the first claimed unit
-
   // A chunk of K (and of V) is one contiguous range of n * D elements in the pool and in
   // the stage; lanes copy it in 16-byte pieces, zero-filled up to the 16-key MMA block.
-  auto issue_chunk = [&](const UnitCursor& c, int stage) {
-    if (c.unit < units) {
-      const int64_t b = c.unit / p.kv_heads;
-      const int kvh = static_cast<int>(c.unit % p.kv_heads);
-      const int64_t row = p.rows ? p.rows[b] : b;
-      const int first = c.chunk * kChunk;
-      const int n = min(kChunk, c.keys - first);
+  // A unit's first chunk also brings its query rows (rows >= G*T zero-filled).
+  auto issue_chunk = [&](int stage) {
+    if (issue_live) {
+      const int first = issue_chunk_no * kChunk;
+      const int n = min(kChunk, iu.keys - first);
       const int valid_pieces = n * Shape::kPieces;
       const int pieces = ((n + 15) & ~15) * Shape::kPieces;
-      const int64_t off = row * p.kv_row + kvh * p.kv_head + static_cast<int64_t>(first) * D;
-      const uint4* ksrc = reinterpret_cast<const uint4*>(kc + off);
-      const uint4* vsrc = reinterpret_cast<const uint4*>(vc + off);
-      uint4* kdst = reinterpret_cast<uint4*>(stage_base + stage * 2 * Shape::kStageElems);
-      uint4* vdst = kdst + Shape::kStageElems * static_cast<int>(sizeof(KV)) / 16;
+      const uint4* ksrc = reinterpret_cast<const uint4*>(kc + issue_kv + static_cast<int64_t>(first) * D);
+      const uint4* vsrc = reinterpret_cast<const uint4*>(vc + issue_kv + static_cast<int64_t>(first) * D);
+      KV* sbase = stage_base + stage * Shape::kStageElems;
+      uint4* kdst = reinterpret_cast<uint4*>(sbase);
+      uint4* vdst = reinterpret_cast<uint4*>(sbase + Shape::kChunkElems);
       for (int i = lane; i < pieces; i += 32) {
         const bool valid = i < valid_pieces;
         cp_async16(kdst + i, ksrc + (valid ? i : 0), valid, policy);
         cp_async16(vdst + i, vsrc + (valid ? i : 0), valid, policy);
       }
+      if (issue_chunk_no == 0) {
+        uint4* qdst = reinterpret_cast<uint4*>(sbase + 2 * Shape::kChunkElems);
+        for (int i = lane; i < Shape::kQRows * Shape::kPieces; i += 32) {
+          const int m = i / Shape::kPieces, piece = i - m * Shape::kPieces;
+          const bool valid = m < M;
+          const int h = iu.kvh * p.group + (valid ? m / p.steps : 0), t = valid ? m % p.steps : 0;
+          const KV* src = qg + iu.b * p.q_sb + h * p.q_sh + t * p.q_st + piece * 8;
+          cp_async16(qdst + i, src, valid, policy);
+        }
+      }
     }
     cp_async_commit();  // one group per chunk slot, empty or not: keeps the group count in step
   };
+  auto issue_advance = [&]() {
+    if (!issue_live) return;
+    if (++issue_chunk_no * kChunk < iu.keys) return;
+    issue_next_unit();
+  };
 
+  issue_next_unit();
   int issue_stage = 0;
 #pragma unroll
   for (int s = 0; s < kStages - 1; ++s) {
-    issue_chunk(issue, issue_stage);
-    issue_advance(issue);
+    issue_chunk(issue_stage);
+    issue_advance();
     issue_stage = issue_stage + 1 == kStages ? 0 : issue_stage + 1;
   }
+
+  // Compute cursor.
+  auto pop = [&](TcUnit& u) -> bool {
+    __syncwarp();
+    const int4 r = ring[wib][tail % kRing];
+    ++tail;
+    u.b = r.x;
+    u.kvh = r.y;
+    u.keys = r.z;
+    u.len = r.w;
+    return r.w >= 0;
+  };
+  TcUnit cu;
+  bool comp_live = pop(cu);
+  int comp_chunk = 0;
 
   uint32_t qa[Shape::kTiles > 0 ? Shape::kTiles : 1][4];
   uint32_t qt[2] = {0, 0};
   float o[Shape::kDTiles][4];
   float mrow[2], lrow[2];
   int limit_r[2];
-  int lim_min = 0;
   int comp_stage = 0;
+  constexpr int kRows = kHalf ? 1 : 2;
 
-  while (comp.unit < units) {
-    issue_chunk(issue, issue_stage);
-    issue_advance(issue);
+  while (comp_live) {
+    issue_chunk(issue_stage);
+    issue_advance();
     issue_stage = issue_stage + 1 == kStages ? 0 : issue_stage + 1;
 
-    const int64_t b = comp.unit / p.kv_heads;
-    const int kvh = static_cast<int>(comp.unit % p.kv_heads);
-    if (comp.chunk == 0) {
-      // Unit start: Q fragments (rows m >= M are zero), softmax state, limits.
-      const KV* qbase = static_cast<const KV*>(p.q);
-      auto qpair = [&](int m, int c) -> uint32_t {
-        if (m >= M) return 0u;
-        const int h = kvh * p.group + m / p.steps, t = m % p.steps;
-        return *reinterpret_cast<const uint32_t*>(qbase + b * p.q_sb + h * p.q_sh + t * p.q_st + c);
-      };
+    cp_async_wait<kStages - 1>();
+    __syncwarp();
+    const KV* ks = stage_base + comp_stage * Shape::kStageElems;
+    const KV* vs = ks + Shape::kChunkElems;
+    if (comp_chunk == 0) {
+      // Unit start: Q fragments from the stage, softmax state, limits.
+      const KV* qs = ks + 2 * Shape::kChunkElems;
 #pragma unroll
       for (int kb = 0; kb < Shape::kTiles; ++kb) {
-        const int c = kb * 16 + 2 * tid4;
-        qa[kb][0] = qpair(gid, c);
-        qa[kb][1] = kHalf ? 0u : qpair(gid + 8, c);
-        qa[kb][2] = qpair(gid, c + 8);
-        qa[kb][3] = kHalf ? 0u : qpair(gid + 8, c + 8);
+        if (kHalf) {
+          ldmatrix_x2(qa[kb][0], qa[kb][2], smem_addr(qs + (lane & 7) * D + kb * 16 + ((lane >> 3) & 1) * 8));
+          qa[kb][1] = qa[kb][3] = 0u;
+        } else {
+          ldmatrix_x4(qa[kb][0], qa[kb][1], qa[kb][2], qa[kb][3],
+                      smem_addr(qs + (lane & 15) * D + kb * 16 + (lane >> 4) * 8));
+        }
       }
       if (Shape::kTail) {
-        const int c = Shape::kTiles * 16 + 2 * tid4;
-        qt[0] = qpair(gid, c);
-        qt[1] = kHalf ? 0u : qpair(gid + 8, c);
+        if (kHalf) {
+          ldmatrix_x1(qt[0], smem_addr(qs + (lane & 7) * D + Shape::kTiles * 16));
+          qt[1] = 0u;
+        } else {
+          ldmatrix_x2(qt[0], qt[1], smem_addr(qs + (lane & 15) * D + Shape::kTiles * 16));
+        }
       }
 #pragma unroll
       for (int j = 0; j < Shape::kDTiles; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-      const int64_t len = p.lengths[b];
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
         const int m = gid + 8 * r;
         // Padding rows (m >= M) attend to every visible key: finite, never stored.
         const int t = m < M ? m % p.steps : p.steps - 1;
-        const int64_t lim = len + t;
-        limit_r[r] = static_cast<int>(lim < p.span ? lim : p.span);
+        limit_r[r] = min(cu.len + t, p.span);
         mrow[r] = -INFINITY;
         lrow[r] = 0.f;
       }
-      lim_min = static_cast<int>(len < p.span ? len : p.span);  // the t = 0 queries see the fewest keys
     }
 
-    cp_async_wait<kStages - 1>();
-    __syncwarp();
-    const KV* ks = stage_base + comp_stage * 2 * Shape::kStageElems;
-    const KV* vs = ks + Shape::kStageElems;
-    const int first = comp.chunk * kChunk;
-    const int n = min(kChunk, comp.keys - first);
+    const int first = comp_chunk * kChunk;
+    const int n = min(kChunk, cu.keys - first);
     const int nblocks = (n + 15) >> 4;
-    constexpr int kRows = kHalf ? 1 : 2;
     // Every row sees every processed key of this chunk (a zero-filled tail block needs the mask).
-    const bool full = (n & 15) == 0 && first + n <= lim_min;
-
+    const bool full = (n & 15) == 0 && first + n <= cu.len;
     // S = Q K^T over the chunk, 16 keys (two n8 tiles) per step; K fragments by ldmatrix.
     // Scores stay unscaled until the exponent: scale > 0 keeps the max where it is.
     float s[kChunk / 8][4];
@@ -520,7 +538,7 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
     }
     __syncwarp();  // every lane is done with this stage before it is refilled
 
-    const bool last_chunk = (comp.chunk + 1) * kChunk >= comp.keys;
+    const bool last_chunk = first + kChunk >= cu.keys;
     if (last_chunk) {
       // Unit done: normalise and store rows m < M.
 #pragma unroll
@@ -528,12 +546,13 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
         lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 1);
         lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 2);
       }
+      const int64_t b = cu.b;
 #pragma unroll
       for (int r = 0; r < kRows; ++r) {
         const int m = gid + 8 * r;
         if (m < M) {
           const float inv = 1.f / lrow[r];
-          const int h = kvh * p.group + m / p.steps, t = m % p.steps;
+          const int h = cu.kvh * p.group + m / p.steps, t = m % p.steps;
 #pragma unroll
           for (int j = 0; j < Shape::kDTiles; ++j) {
             const int d = j * 8 + 2 * tid4;
@@ -550,8 +569,11 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
           }
         }
       }
+      comp_live = pop(cu);
+      comp_chunk = 0;
+    } else {
+      ++comp_chunk;
     }
-    compute_advance(comp);
     comp_stage = comp_stage + 1 == kStages ? 0 : comp_stage + 1;
   }
   cp_async_wait<0>();  // no copy may still target shared memory when the warp exits
@@ -559,7 +581,7 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
 
 template <typename KV, int D, bool kHalf, bool kBlocked>
 int launch_tc(const AttnParams& p, cudaStream_t stream) {
-  using Shape = TcShape<KV, D>;
+  using Shape = TcShape<KV, D, kHalf>;
   auto kernel = attn_tc_kernel<KV, D, kHalf, kBlocked>;
   const int smem = kTcWarps * Shape::kWarpBytes;
   static int per_sm[64] = {0};
@@ -606,16 +628,18 @@ bool tc_eligible(const AttnParams& p) {
   if (p.group * p.steps > 16) return false;
   const int d = p.head_dim;
   if (!(d == 16 || d == 24 || d == 32 || d == 40 || d == 48 || d == 64)) return false;
-  // q (and the non-blocked output) in the cache dtype, with even element strides for 32-bit pair access.
+  // q (and the non-blocked output) in the cache dtype; q rows are copied in 16-byte pieces,
+  // the output is written in 32-bit pairs.
   if (p.q_dtype != p.kv_dtype) return false;
   if (!p.out_blocked && p.out_dtype != p.kv_dtype) return false;
-  if ((p.q_sb | p.q_sh | p.q_st) & 1) return false;
+  if ((p.q_sb | p.q_sh | p.q_st) & 7) return false;
+  if (p.batch * p.kv_heads >= (1LL << 31)) return false;
   if (!p.out_blocked && ((p.o_sb | p.o_sh | p.o_st) & 1)) return false;
   // 16-byte copies: contiguous key rows, aligned row/head strides and bases.
   if (p.kv_pos != d) return false;
   if ((p.kv_row % 8) || (p.kv_head % 8)) return false;
   if ((reinterpret_cast<uintptr_t>(p.k) & 15) || (reinterpret_cast<uintptr_t>(p.v) & 15)) return false;
-  if (reinterpret_cast<uintptr_t>(p.q) & 3 || reinterpret_cast<uintptr_t>(p.out) & 3) return false;
+  if (reinterpret_cast<uintptr_t>(p.q) & 15 || reinterpret_cast<uintptr_t>(p.out) & 3) return false;
   return true;
 }
 

@@ -107,6 +107,138 @@ __global__ void __launch_bounds__(256) plump_embed_kernel(cg_plump_schema sc, co
   (void)total_rows;
 }
 
+// ---- the lookup with table slices in shared memory ---------------------------------------------
+// A token sums ~16-35 table rows of `width` floats; read from L2 that is ~145 KB per token.
+// Here a CTA takes a block of tokens, resolves their row ids once into shared memory, then
+// streams the table through shared memory in slices of kSliceF4 float4 columns (two slices
+// in flight), so every row read of the sums is a shared-memory read. Sums run in the same
+// order as plump_embed_kernel (fields, pattern, then the hand rows as one partial sum).
+constexpr int kEmbedThreads = 512;
+constexpr int kEmbedMaxTokens = 256;   // tokens per CTA
+constexpr int kEmbedMain = 17;         // id slots: up to 16 fields + the pattern row
+constexpr int kEmbedIds = kEmbedMain + 32;
+
+struct EmbedIds {
+  int16_t row[kEmbedIds];  // [0, n_main): fields then pattern; [kEmbedMain, +n_hand): hand rows
+  uint8_t n_main, n_hand;
+};
+
+template <int kSliceF4>  // float4 columns per slice = lanes per token
+__global__ void __launch_bounds__(kEmbedThreads, 1) plump_embed_sliced_kernel(
+    cg_plump_schema sc, const float* __restrict__ table, int width, const void* __restrict__ tokens, int token_dtype,
+    int64_t n, int tokens_per_cta, float* __restrict__ out) {
+  extern __shared__ __align__(16) unsigned char emb_smem[];
+  const int total_rows = sc.field_rows + sc.pattern_rows;
+  float4* slices = reinterpret_cast<float4*>(emb_smem);  // [2][total_rows][kSliceF4]
+  EmbedIds* ids = reinterpret_cast<EmbedIds*>(slices + 2 * total_rows * kSliceF4);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * tokens_per_cta;
+  const int count = static_cast<int>(n - first < tokens_per_cta ? n - first : tokens_per_cta);
+  const int width4 = width / 4;
+  const int n_slices = (width4 + kSliceF4 - 1) / kSliceF4;
+
+  auto load_slice = [&](int slice, int buf) {
+    const int c0 = slice * kSliceF4;
+    float4* dst = slices + buf * total_rows * kSliceF4;
+    for (int i = tid; i < total_rows * kSliceF4; i += kEmbedThreads) {
+      const int r = i / kSliceF4, c = c0 + (i - r * kSliceF4);
+      const bool valid = c < width4;
+      const float4* src = reinterpret_cast<const float4*>(table + static_cast<int64_t>(r) * width) + (valid ? c : 0);
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                       static_cast<uint32_t>(__cvta_generic_to_shared(dst + i))),
+                   "l"(src), "r"(valid ? 16 : 0)
+                   : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  load_slice(0, 0);
+
+  // Row ids, one warp per token (the same resolution as plump_embed_kernel).
+  const unsigned lt = (1u << lane) - 1u;
+  for (int t = warp; t < count; t += kEmbedThreads / 32) {
+    const int64_t base = (first + t) * sc.token_width;
+    int field_row = -1;
+    if (lane < sc.field_count) {
+      const int64_t id = token_at(tokens, token_dtype, base + sc.field_slots[lane]);
+      const bool present = sc.field_na[lane] < 0 || id != sc.field_na[lane];
+      const int64_t row = id + sc.field_offsets[lane];
+      if (present) {
+        if (id < 0 || row >= sc.field_rows) {
+          raise_fault(0x200);
+        } else {
+          field_row = static_cast<int>(row);
+        }
+      }
+    }
+    int64_t pattern = token_at(tokens, token_dtype, base + sc.slot_pattern);
+    if (pattern < 0 || pattern >= sc.pattern_rows) {
+      if (lane == 0) raise_fault(0x201);
+      pattern = 0;
+    }
+    const bool trick_win = token_at(tokens, token_dtype, base + sc.slot_type) == sc.trick_win_type;
+    int hand_row = -1;
+    if (trick_win && lane < 2 * sc.hand_slots) {
+      const int64_t card = token_at(tokens, token_dtype, base + sc.slot_hand + lane / 2);
+      if (card >= 0 && card < sc.num_cards) {
+        hand_row = (lane & 1) ? static_cast<int>(card / sc.num_ranks) + sc.suit_offset
+                              : static_cast<int>(card % sc.num_ranks) + sc.rank_offset;
+      }
+    }
+    const unsigned fields = __ballot_sync(0xffffffffu, field_row >= 0);
+    const unsigned hands = __ballot_sync(0xffffffffu, hand_row >= 0);
+    EmbedIds& e = ids[t];
+    if (field_row >= 0) e.row[__popc(fields & lt)] = static_cast<int16_t>(field_row);
+    if (hand_row >= 0) e.row[kEmbedMain + __popc(hands & lt)] = static_cast<int16_t>(hand_row);
+    if (lane == 0) {
+      const int nf = __popc(fields);
+      e.row[nf] = static_cast<int16_t>(sc.field_rows + pattern);
+      e.n_main = static_cast<uint8_t>(nf + 1);
+      e.n_hand = static_cast<uint8_t>(__popc(hands));
+    }
+  }
+
+  constexpr int kTokensPerWarp = 32 / kSliceF4;
+  const int sub = lane / kSliceF4, col = lane % kSliceF4;
+  for (int slice = 0; slice < n_slices; ++slice) {
+    if (slice + 1 < n_slices) {
+      load_slice(slice + 1, (slice + 1) & 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncthreads();  // this slice (and, on the first pass, every token's ids) is in place
+    const float4* tab = slices + (slice & 1) * total_rows * kSliceF4 + col;
+    const int c = slice * kSliceF4 + col;
+    for (int t = warp * kTokensPerWarp + sub; t < count; t += (kEmbedThreads / 32) * kTokensPerWarp) {
+      const EmbedIds& e = ids[t];
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int k = 0; k < e.n_main; ++k) {
+        const float4 v = tab[e.row[k] * kSliceF4];
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      if (e.n_hand) {
+        float4 hand = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int k = 0; k < e.n_hand; ++k) {
+          const float4 v = tab[e.row[kEmbedMain + k] * kSliceF4];
+          hand.x += v.x;
+          hand.y += v.y;
+          hand.z += v.z;
+          hand.w += v.w;
+        }
+        acc.x += hand.x;
+        acc.y += hand.y;
+        acc.z += hand.z;
+        acc.w += hand.w;
+      }
+      if (c < width4) reinterpret_cast<float4*>(out + (first + t) * width)[c] = acc;
+    }
+    __syncthreads();  // every warp is done with this buffer before it is refilled
+  }
+}
+
 int check_schema(const cg_plump_schema* sc) {
   CG_REQUIRE(sc, "NULL plump schema");
   CG_REQUIRE(sc->field_count > 0 && sc->field_count <= 16, "field_count must be 1..16");
@@ -119,9 +251,38 @@ int check_schema(const cg_plump_schema* sc) {
 int embed(const cg_plump_schema& sc, const float* table, int width, const void* tokens, int token_dtype, int64_t n,
           float* out, cudaStream_t s) {
   if (n == 0) return CG_OK;
-  const int64_t blocks = (n + 7) / 8;
-  plump_embed_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(sc, table, width, tokens, token_dtype, n, out);
-  return check_launch("plump_embed_kernel");
+  const int total_rows = sc.field_rows + sc.pattern_rows;
+  // Widest slice whose two buffers fit next to the ids: 16 float4 (64 columns) for plump.
+  int slice_f4 = 16;
+  while (slice_f4 > 4 && 2LL * total_rows * slice_f4 * 16 > 200 * 1024) slice_f4 /= 2;
+  const bool sliced = (width % 4) == 0 && 2LL * total_rows * slice_f4 * 16 <= 200 * 1024 &&
+                      (reinterpret_cast<uintptr_t>(table) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
+                      sc.hand_slots * 2 <= 32 && sc.field_count <= 16;
+  if (!sliced) {
+    const int64_t blocks = (n + 7) / 8;
+    plump_embed_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(sc, table, width, tokens, token_dtype, n, out);
+    return check_launch("plump_embed_kernel");
+  }
+  int64_t per = (n + sm_count() - 1) / sm_count();
+  if (per > kEmbedMaxTokens) per = kEmbedMaxTokens;
+  const int64_t blocks = (n + per - 1) / per;
+  const size_t smem = 2 * static_cast<size_t>(total_rows) * slice_f4 * 16 + static_cast<size_t>(per) * sizeof(EmbedIds);
+  auto launch = [&](auto kernel) {
+    static size_t configured[64] = {0};
+    int device = 0;
+    cudaGetDevice(&device);
+    if (configured[device & 63] < smem) {
+      cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+      if (err != cudaSuccess) return set_error(CG_ERR_CUDA, "plump_embed_sliced_kernel smem: %s", cudaGetErrorString(err));
+      configured[device & 63] = smem;
+    }
+    kernel<<<static_cast<unsigned>(blocks), kEmbedThreads, smem, s>>>(sc, table, width, tokens, token_dtype, n,
+                                                                      static_cast<int>(per), out);
+    return check_launch("plump_embed_sliced_kernel");
+  };
+  if (slice_f4 == 16) return launch(plump_embed_sliced_kernel<16>);
+  if (slice_f4 == 8) return launch(plump_embed_sliced_kernel<8>);
+  return launch(plump_embed_sliced_kernel<4>);
 }
 
 struct PlumpWorkspace {

@@ -116,6 +116,27 @@ def test_plump_field_lookup_matches_the_oracle():
     assert torch.equal(x16, x)
 
 
+def test_plump_field_lookup_row_per_warp_kernel_matches_the_sliced_kernel():
+    """A table width that is not a multiple of 4 takes the row-per-warp lookup: the same sums, bit for bit."""
+
+    from card_playing_gym_b200 import _native as nat
+    from card_playing_gym_b200.config import PlumpModelConfig, synthetic_plump_actor_state
+    from card_playing_gym_b200.plump import PlumpActor
+
+    config = PlumpModelConfig()
+    state = synthetic_plump_actor_state(config, seed=9)
+    actor = PlumpActor(config, state, precision="fp32")
+    streams = load_golden("plump_streams")["tokens"]
+    flat = torch.from_numpy(streams.reshape(-1, streams.shape[-1]).astype(np.int64)).cuda()
+    full = actor.embed_lookup(flat)
+    width = actor.trunk.lookup_width - 3
+    table = actor.table[:, :width].contiguous()
+    out = torch.empty((flat.shape[0], width), device="cuda")
+    nat.call("cg_plump_embed", actor.schema, nat.ptr(table), width, nat.ptr(flat), nat.INDEX_CODES[flat.dtype],
+             flat.shape[0], nat.ptr(out), nat.stream_handle(torch.device("cuda")))
+    assert torch.equal(out, full[:, :width])
+
+
 @pytest.mark.parametrize("width", (11, 52, 64))
 def test_masked_sampling_matches_the_reference(width):
     from card_playing_gym_b200.sampling import masked_sample
