@@ -120,6 +120,13 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool vali
                : "memory");
 }
 
+// Same, always copying 16 bytes.
+__device__ __forceinline__ void cp_async16_full(void* dst, const void* src, uint64_t policy) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src),
+               "l"(policy)
+               : "memory");
+}
+
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 
 template <int N>
@@ -295,6 +302,28 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
     }
   };
 
+  // Per-lane constants of the launch: the query pieces this lane stages for every unit (offset
+  // from the unit's first query row), and the step of the output rows it finalizes.
+  constexpr int kQPieces = Shape::kQRows * Shape::kPieces;
+  constexpr int kQIters = (kQPieces + 31) / 32;
+  int q_off[kQIters];
+  bool q_ok[kQIters];
+#pragma unroll
+  for (int it = 0; it < kQIters; ++it) {
+    const int i = lane + 32 * it;
+    const int m = i / Shape::kPieces, piece = i - m * Shape::kPieces;
+    q_ok[it] = i < kQPieces && m < M;
+    q_off[it] = q_ok[it] ? static_cast<int>((m / p.steps) * p.q_sh + (m % p.steps) * p.q_st) + piece * 8 : 0;
+  }
+  int row_h[2], row_t[2], row_tlim[2];  // rows gid and gid + 8: head within the group, step, step for the limit
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int m = gid + 8 * r;
+    row_h[r] = m < M ? m / p.steps : 0;
+    row_t[r] = m < M ? m % p.steps : 0;
+    row_tlim[r] = m < M ? row_t[r] : p.steps - 1;  // padding rows attend to every visible key: finite, never stored
+  }
+
   // Issue cursor.
   bool issue_live = true;
   TcUnit iu{0, 0, 0, 0};
@@ -323,22 +352,30 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
       const uint4* ksrc = reinterpret_cast<const uint4*>(kc + issue_kv + static_cast<int64_t>(first) * D);
       const uint4* vsrc = reinterpret_cast<const uint4*>(vc + issue_kv + static_cast<int64_t>(first) * D);
       KV* sbase = stage_base + stage * Shape::kStageElems;
-      uint4* kdst = reinterpret_cast<uint4*>(sbase);
-      uint4* vdst = reinterpret_cast<uint4*>(sbase + Shape::kChunkElems);
-      for (int i = lane; i < pieces; i += 32) {
-        const bool valid = i < valid_pieces;
-        cp_async16(kdst + i, ksrc + (valid ? i : 0), valid, policy);
-        cp_async16(vdst + i, vsrc + (valid ? i : 0), valid, policy);
+      uint4* kdst = reinterpret_cast<uint4*>(sbase) + lane;
+      uint4* vdst = reinterpret_cast<uint4*>(sbase + Shape::kChunkElems) + lane;
+      // Rounds of 32 pieces: whole rounds of valid keys copy without checks; the boundary
+      // round zero-fills its lanes past the valid keys (source clamped to the chunk start).
+      constexpr int kRounds = kChunk * Shape::kPieces / 32;
+#pragma unroll
+      for (int it = 0; it < kRounds; ++it) {
+        if (32 * it >= pieces) break;
+        if (32 * it + 32 <= valid_pieces) {
+          cp_async16_full(kdst + 32 * it, ksrc + lane + 32 * it, policy);
+          cp_async16_full(vdst + 32 * it, vsrc + lane + 32 * it, policy);
+        } else {
+          const int i = lane + 32 * it;
+          const bool valid = i < valid_pieces;
+          cp_async16(kdst + 32 * it, ksrc + (valid ? i : 0), valid, policy);
+          cp_async16(vdst + 32 * it, vsrc + (valid ? i : 0), valid, policy);
+        }
       }
       if (issue_chunk_no == 0) {
-        uint4* qdst = reinterpret_cast<uint4*>(sbase + 2 * Shape::kChunkElems);
-        for (int i = lane; i < Shape::kQRows * Shape::kPieces; i += 32) {
-          const int m = i / Shape::kPieces, piece = i - m * Shape::kPieces;
-          const bool valid = m < M;
-          const int h = iu.kvh * p.group + (valid ? m / p.steps : 0), t = valid ? m % p.steps : 0;
-          const KV* src = qg + iu.b * p.q_sb + h * p.q_sh + t * p.q_st + piece * 8;
-          cp_async16(qdst + i, src, valid, policy);
-        }
+        uint4* qdst = reinterpret_cast<uint4*>(sbase + 2 * Shape::kChunkElems) + lane;
+        const KV* qunit = qg + iu.b * p.q_sb + static_cast<int64_t>(iu.kvh) * p.group * p.q_sh;
+#pragma unroll
+        for (int it = 0; it < kQIters; ++it)
+          if (lane + 32 * it < kQPieces) cp_async16(qdst + 32 * it, qunit + q_off[it], q_ok[it], policy);
       }
     }
     cp_async_commit();  // one group per chunk slot, empty or not: keeps the group count in step
@@ -415,10 +452,7 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
       for (int j = 0; j < Shape::kDTiles; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
-        const int m = gid + 8 * r;
-        // Padding rows (m >= M) attend to every visible key: finite, never stored.
-        const int t = m < M ? m % p.steps : p.steps - 1;
-        limit_r[r] = min(cu.len + t, p.span);
+        limit_r[r] = min(cu.len + row_tlim[r], p.span);
         mrow[r] = -INFINITY;
         lrow[r] = 0.f;
       }
@@ -432,9 +466,10 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
     // S = Q K^T over the chunk, 16 keys (two n8 tiles) per step; K fragments by ldmatrix.
     // Scores stay unscaled until the exponent: scale > 0 keeps the max where it is.
     float s[kChunk / 8][4];
-    float cmax[2] = {-INFINITY, -INFINITY};
+    float kmax[kChunk / 16][2];  // per 16-key block, then a tree: no long max chain
 #pragma unroll
     for (int kk = 0; kk < kChunk / 16; ++kk) {
+      kmax[kk][0] = kmax[kk][1] = -INFINITY;
       float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
       if (kk < nblocks) {
         const KV* kbase = ks + (kk * 16 + (lane & 15)) * D;
@@ -469,12 +504,21 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
           }
           s[2 * kk][e] = v0;
           s[2 * kk + 1][e] = v1;
-          cmax[r] = fmaxf(cmax[r], fmaxf(v0, v1));
+          kmax[kk][r] = fmaxf(kmax[kk][r], fmaxf(v0, v1));
         }
       }
     }
+    float cmax[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+#pragma unroll
+      for (int w = kChunk / 32; w >= 1; w /= 2)
+#pragma unroll
+        for (int kk = 0; kk < w; ++kk) kmax[kk][r] = fmaxf(kmax[kk][r], kmax[kk + w][r]);
+      cmax[r] = kmax[0][r];
+    }
     float alpha[2] = {1.f, 1.f};
-    float psum[2] = {0.f, 0.f};
+    float psum[2][2] = {{0.f, 0.f}, {0.f, 0.f}};  // two partial sums per row: shorter add chains
     float neg_max[2];
 #pragma unroll
     for (int r = 0; r < kRows; ++r) {
@@ -495,11 +539,11 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
         const int r = e >> 1;
         const float pe = fast_exp2(fmaf(s[j][e], scale_log2, neg_max[r]));  // masked keys: exp2(-inf) = 0
         s[j][e] = pe;
-        psum[r] += pe;
+        psum[r][j & 1] += pe;
       }
     }
 #pragma unroll
-    for (int r = 0; r < kRows; ++r) lrow[r] = lrow[r] * alpha[r] + psum[r];
+    for (int r = 0; r < kRows; ++r) lrow[r] = lrow[r] * alpha[r] + (psum[r][0] + psum[r][1]);
 #pragma unroll
     for (int j = 0; j < Shape::kDTiles; ++j) {
       o[j][0] *= alpha[0];
@@ -552,7 +596,7 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
         const int m = gid + 8 * r;
         if (m < M) {
           const float inv = 1.f / lrow[r];
-          const int h = cu.kvh * p.group + m / p.steps, t = m % p.steps;
+          const int h = cu.kvh * p.group + row_h[r], t = row_t[r];
 #pragma unroll
           for (int j = 0; j < Shape::kDTiles; ++j) {
             const int d = j * 8 + 2 * tid4;

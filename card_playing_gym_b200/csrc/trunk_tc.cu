@@ -6,9 +6,12 @@
 // 318-333, and the KV append of kv_cache.py:84-105 with trunk.py:419-423's clamp.
 //
 // One CTA owns a tile of 128 row-tokens and carries it across a layer boundary:
-//   attention(l) output -> out_proj -> x += . -> LN -> up (d-wide chunks) -> GELU ->
+//   attention(l) output -> out_proj -> x += . -> LN -> up (128-column chunks) -> GELU ->
 //   down (accumulated over the chunks) -> x += . + b -> x += PLE(l) -> LN -> QKV(l+1)
 //   -> q for attention(l+1), K/V appended to the pool.
+// The MLP is double-buffered: up chunks alternate between two TMEM column ranges and their
+// GELU outputs between two shared-memory H buffers, so the tensor core runs up(c+1) and
+// down(c-1) while the epilogue warps compute GELU(c).
 // Roles: warps 0-11 are epilogue warps (three threads per row, each holding a third of
 // the row's columns); warp 12's lane 0 streams weight K-slices into a ring of 32 KB
 // shared-memory stages with bulk async copies; warp 13 allocates tensor memory and its
@@ -34,6 +37,10 @@ constexpr int kMaxOps = 16;
 constexpr int kMaxStages = 16;
 constexpr int kStageTarget = 32 * 1024;  // bytes per ring stage (one bulk copy)
 constexpr int kSmemBudget = 222 * 1024;  // dynamic shared memory; the static barriers and reductions need the rest of 227 KB
+constexpr int kUpCols = 128;             // up-projection chunk: columns of d_ff per GELU hand-off
+constexpr int kAccCols = 256;            // TMEM: [0, 256) out/down/QKV accumulator, then two up buffers
+// GEMM completion signals (tcgen05.commit targets).
+enum Signal { kSigNone = 0, kSigAcc = 1, kSigUp0 = 2, kSigUp1 = 3, kSigHFree0 = 4, kSigHFree1 = 5 };
 
 enum TcMode { kLayer = 0, kFirstLookup = 1, kFirstConditioned = 2 };
 
@@ -43,16 +50,16 @@ struct GemmOp {
   int ksteps;
   int ks_per_stage;  // consecutive K-slices carried by one ring stage (one bulk copy)
   int tmem_col;
-  int a_src;  // 0: A buffer, 1: H buffer
+  int a_src;  // 0: A buffer, 1: H buffer 0, 2: H buffer 1
   int accumulate_first;
   int wait_a;
-  int signal;
+  int signal;  // Signal
 };
 
 struct TcParams {
   int mode, layer, qkv_layer, has_next;
   GemmOp ops[kMaxOps];
-  int n_ops, n_ple_ops, stages, stage_bytes;
+  int n_ops, n_ple_ops, stages, stage_bytes, hbytes, n_up;
   int d, f, H, KVH, D, L, P, nv, kvw, qw;
   int64_t nt, ntiles;
   int T;
@@ -257,14 +264,16 @@ __device__ void qkv_epilogue(const TcParams& p, const EpiThread& e, int64_t tile
                                           (static_cast<int64_t>(p.value_index) * p.ntiles + tile) * (p.kvw / 4) * kTile + t;
   int lo, hi;
   part_chunks(p.qw, e.qd, lo, hi);
-  for (int c = lo; c < hi; ++c) {
-    float v[16];
-    tc::tmem_ld16(e.lane_tmem + c * 16, v);
+  for (int c = lo; c < hi; c += 2) {
+    const bool two = c + 1 < hi;
+    float v[32];
+    tc::tmem_ld_pair(e.lane_tmem + c * 16, two, v);
     if (!valid) continue;
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const int col = c * 16 + half * 8;
-      float* w = v + half * 8;
+    for (int piece = 0; piece < 4; ++piece) {
+      if (piece >= 2 && !two) break;
+      const int col = c * 16 + piece * 8;
+      float* w = v + piece * 8;
       if (col < hd) {
         const int h = col / p.D, dd = col - h * p.D;
         store8(p.q, q_row + (h * q_head + dd), p.q_dtype, w);
@@ -292,9 +301,10 @@ __device__ void qkv_epilogue(const TcParams& p, const EpiThread& e, int64_t tile
 }
 
 // ---- epilogue warps ----------------------------------------------------------------------------------------
-__device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned char* hbuf, uint32_t tmem,
-                               uint64_t* a_ready_bar, uint64_t* acc_ready_bar, uint64_t* attn_full_bar,
-                               uint64_t* val_full_bar, int abytes, float (*red)[kTile]) {
+__device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned char* h0, unsigned char* h1, uint32_t tmem,
+                               uint64_t* a_ready_bar, uint64_t* acc_ready_bar, uint64_t* up_ready_bar,
+                               uint64_t* h_free_bar, uint64_t* attn_full_bar, uint64_t* val_full_bar, int abytes,
+                               float (*red)[kTile]) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t tile = blockIdx.x;
   EpiThread e;
@@ -354,20 +364,42 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
     }
     layer_norm_regs(x, lo, hi, d, e, p.ln_mlp_w, p.ln_mlp_b, abuf, red);
     publish();
-    // E2: GELU of each up chunk into H.
-    const int chunks = p.f / d;
-    for (int uc = 0; uc < chunks; ++uc) {
-      if (!wait_acc()) return;
+    // E2: GELU of each up chunk into its H buffer. Chunk uc sits in TMEM buffer uc % 2; its
+    // H buffer is free once down(uc - 2) has completed.
+    uint32_t up_phase[2] = {0u, 0u}, free_phase[2] = {0u, 0u};
+    for (int uc = 0; uc < p.n_up; ++uc) {
+      const int buf = uc & 1;
+      if (threadIdx.x == 0) {
+        bool ok = tc::bar_wait(&up_ready_bar[buf], up_phase[buf], 0x406);
+        if (ok && uc >= 2) ok = tc::bar_wait(&h_free_bar[buf], free_phase[buf], 0x407);
+        red[2 * kParts][0] = ok ? 1.f : 0.f;
+      }
+      epi_sync();
+      if (red[2 * kParts][0] == 0.f) return;
+      up_phase[buf] ^= 1u;
+      if (uc >= 2) free_phase[buf] ^= 1u;
+      tc::fence_after_sync();
+      const int width = min(kUpCols, p.f - uc * kUpCols);
+      int plo, phi;
+      part_chunks(width, e.qd, plo, phi);
+      unsigned char* hb = buf ? h1 : h0;
+      const float* bias_base = p.up_b + uc * kUpCols;
+      const uint32_t ucol = kAccCols + buf * kUpCols;
+      for (int c = plo; c < phi; c += 2) {
+        const bool two = c + 1 < phi;
+        float bias[2][16];
+        load16_vec(bias_base + c * 16, bias[0]);
+        if (two) load16_vec(bias_base + c * 16 + 16, bias[1]);
+        float v[32];
+        tc::tmem_ld_pair(e.lane_tmem + ucol + c * 16, two, v);
 #pragma unroll
-      for (int c = 0; c < kMaxRowChunks; ++c) {
-        if (lo + c >= hi) continue;
-        const int col = (lo + c) * 16;
-        float bias[16];
-        load16_vec(p.up_b + uc * d + col, bias);
-        tc::tmem_ld16(e.lane_tmem + 256 + col, v16);
+        for (int h = 0; h < 2; ++h) {
+          if (h == 1 && !two) break;
+          float g[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) v16[i] = gelu_erf(v16[i] + bias[i]);
-        store_operand16(hbuf, col, t, v16);
+          for (int i = 0; i < 16; ++i) g[i] = gelu_erf(v[16 * h + i] + bias[h][i]);
+          store_operand16(hb, (c + h) * 16, t, g);
+        }
       }
       publish();
     }
@@ -403,10 +435,10 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
     if (!wait_acc()) return;
     // Every GEMM that reads H has completed: H takes the next layer's value-embedding tile.
     const int vbytes = kTile * p.kvw * 4;
-    const bool val_smem = p.has_next && p.value_index >= 0 && vbytes <= abytes;
+    const bool val_smem = p.has_next && p.value_index >= 0 && vbytes <= p.hbytes;
     if (val_smem && threadIdx.x == 0) {
       tc::bar_expect_tx(val_full_bar, vbytes);
-      tc::bulk_g2s(hbuf, reinterpret_cast<const unsigned char*>(p.val_blk) +
+      tc::bulk_g2s(h0, reinterpret_cast<const unsigned char*>(p.val_blk) +
                              (static_cast<int64_t>(p.value_index) * p.ntiles + tile) * vbytes,
                    vbytes, val_full_bar);
     }
@@ -424,7 +456,7 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
       publish();
       if (val_smem && !group_wait(val_full_bar, 0, 0x405)) return;
       if (!wait_acc()) return;
-      qkv_epilogue(p, e, tile, val_smem ? reinterpret_cast<const float4*>(hbuf) : nullptr);
+      qkv_epilogue(p, e, tile, val_smem ? reinterpret_cast<const float4*>(h0) : nullptr);
     }
     return;
   }
@@ -520,15 +552,16 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
 __global__ void __launch_bounds__(kTcThreads, 1) tc_dense_kernel(const __grid_constant__ TcParams p) {
   extern __shared__ __align__(1024) unsigned char smem[];
   __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages];
-  __shared__ __align__(8) uint64_t a_ready, acc_ready, attn_full, val_full;
+  __shared__ __align__(8) uint64_t a_ready, acc_ready, attn_full, val_full, up_ready[2], h_free[2];
   __shared__ uint32_t tmem_base;
   __shared__ float red[2 * kParts + 1][kTile];  // row reductions across a row's threads; last row: wait status
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int abytes = kTile * p.d * 2;
   unsigned char* abuf = smem;
-  unsigned char* hbuf = smem + abytes;
-  unsigned char* ring = smem + 2 * abytes;
+  unsigned char* h0 = smem + abytes;
+  unsigned char* h1 = smem + abytes + p.hbytes;
+  unsigned char* ring = smem + abytes + 2 * p.hbytes;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.stages; ++s) {
@@ -539,6 +572,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dense_kernel(const __grid_co
     tc::bar_init(&acc_ready, 1);
     tc::bar_init(&attn_full, 1);
     tc::bar_init(&val_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      tc::bar_init(&up_ready[b], 1);
+      tc::bar_init(&h_free[b], 1);
+    }
     tc::bar_fence_init();
   }
   if (warp == kMmaWarp) {
@@ -593,7 +630,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dense_kernel(const __grid_co
           a_phase ^= 1u;
           tc::fence_after_sync();
         }
-        const uint32_t a_addr = tc::smem_u32(op.a_src ? hbuf : abuf);
+        const uint32_t a_addr = tc::smem_u32(op.a_src == 0 ? abuf : (op.a_src == 1 ? h0 : h1));
         const uint32_t slice = static_cast<uint32_t>(op.n) * 32u;
         const uint32_t idesc = tc::idesc_bf16(128, op.n <= 256 ? op.n : 256);
         const uint32_t idesc_rest = tc::idesc_bf16(128, op.n > 256 ? op.n - 256 : 16);
@@ -618,11 +655,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dense_kernel(const __grid_co
           }
         }
         if (!ok) break;
-        if (op.signal) tc::mma_commit(&acc_ready);
+        switch (op.signal) {
+          case kSigAcc: tc::mma_commit(&acc_ready); break;
+          case kSigUp0: tc::mma_commit(&up_ready[0]); break;
+          case kSigUp1: tc::mma_commit(&up_ready[1]); break;
+          case kSigHFree0: tc::mma_commit(&h_free[0]); break;
+          case kSigHFree1: tc::mma_commit(&h_free[1]); break;
+          default: break;
+        }
       }
     }
   } else {
-    dense_epilogue(p, abuf, hbuf, tmem, &a_ready, &acc_ready, &attn_full, &val_full, abytes, red);
+    dense_epilogue(p, abuf, h0, h1, tmem, &a_ready, &acc_ready, up_ready, h_free, &attn_full, &val_full, abytes, red);
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -661,9 +705,14 @@ int64_t tc_pack_bytes_layer(const cg_trunk_dims& dims) {
 struct LayerPack {
   const __nv_bfloat16* qkv;
   const __nv_bfloat16* out;
-  const __nv_bfloat16* up;    // chunk c at c * d * d
-  const __nv_bfloat16* down;  // chunk c at c * d * d
+  const __nv_bfloat16* up;    // up chunk c (rows c*kUpCols.., K = d) at c * kUpCols * d
+  const __nv_bfloat16* down;  // down chunk c (K = columns c*kUpCols..) at c * kUpCols * d
 };
+
+inline int up_chunks(const cg_trunk_dims& dims) { return (dims.d_ff + kUpCols - 1) / kUpCols; }
+inline int up_width(const cg_trunk_dims& dims, int c) {
+  return dims.d_ff - c * kUpCols < kUpCols ? dims.d_ff - c * kUpCols : kUpCols;
+}
 
 LayerPack layer_pack(const cg_trunk_dims& dims, const void* blob, const BlobLayout& L, int layer) {
   const int64_t d = dims.d_model, f = dims.d_ff, q = qkv_width(dims);
@@ -673,13 +722,15 @@ LayerPack layer_pack(const cg_trunk_dims& dims, const void* blob, const BlobLayo
 
 bool tc_layers_available(const cg_trunk_dims& dims) {
   const int d = dims.d_model, D = head_dim(dims), q = qkv_width(dims);
-  if (d % 16 || d / 16 > kParts * kMaxRowChunks || dims.d_ff % d || q % 16 || q > 512 || D % 8) return false;
+  if (d % 16 || d / 16 > kParts * kMaxRowChunks || dims.d_ff % 16 || q % 16 || q > 512 || D % 8) return false;
+  if (d > kAccCols || 2 * up_chunks(dims) + 3 > kMaxOps) return false;
   if (q > 256 && (q - 256) % 16) return false;
   if (dims.per_layer_dim % 4 || (static_cast<int64_t>(dims.n_layers) * dims.per_layer_dim) % 16) return false;
   if ((dims.n_kv_heads * D) % 4) return false;
   const int64_t abytes = static_cast<int64_t>(kTile) * d * 2;
+  const int64_t hbytes = static_cast<int64_t>(kTile) * (dims.d_ff < kUpCols ? dims.d_ff : kUpCols) * 2;
   const int64_t stage = 32LL * (q > 256 ? q : 256);
-  return 2 * abytes + 2 * stage <= kSmemBudget;
+  return abytes + 2 * hbytes + 2 * stage <= kSmemBudget;
 }
 
 int tc_pack(const cg_trunk_dims& dims, void* blob, const BlobLayout& L, cudaStream_t s) {
@@ -708,12 +759,13 @@ int tc_pack(const cg_trunk_dims& dims, void* blob, const BlobLayout& L, cudaStre
                              const_cast<__nv_bfloat16*>(lp.qkv) + static_cast<int64_t>(256) * d)))
       return rc;
     if ((rc = pack(part(blob, L, CG_PART_OUT, layer), d, 0, d, 0, d, const_cast<__nv_bfloat16*>(lp.out)))) return rc;
-    for (int c = 0; c < f / d; ++c) {
-      if ((rc = pack(part(blob, L, CG_PART_UP, layer), d, c * d, d, 0, d,
-                     const_cast<__nv_bfloat16*>(lp.up) + static_cast<int64_t>(c) * d * d)))
+    for (int c = 0; c < up_chunks(dims); ++c) {
+      const int w = up_width(dims, c);
+      if ((rc = pack(part(blob, L, CG_PART_UP, layer), d, c * kUpCols, w, 0, d,
+                     const_cast<__nv_bfloat16*>(lp.up) + static_cast<int64_t>(c) * kUpCols * d)))
         return rc;
-      if ((rc = pack(part(blob, L, CG_PART_DOWN, layer), f, 0, d, c * d, d,
-                     const_cast<__nv_bfloat16*>(lp.down) + static_cast<int64_t>(c) * d * d)))
+      if ((rc = pack(part(blob, L, CG_PART_DOWN, layer), f, 0, d, c * kUpCols, w,
+                     const_cast<__nv_bfloat16*>(lp.down) + static_cast<int64_t>(c) * kUpCols * d)))
         return rc;
     }
   }
@@ -762,10 +814,11 @@ int launch_dense(TcParams& p, cudaStream_t s) {
   int max_slice = 0;
   for (int i = 0; i < p.n_ops; ++i) max_slice = p.ops[i].n * 32 > max_slice ? p.ops[i].n * 32 : max_slice;
   p.stage_bytes = max_slice > kStageTarget ? max_slice : kStageTarget;
-  int stages = (kSmemBudget - 2 * abytes) / p.stage_bytes;
+  const int fixed = abytes + 2 * p.hbytes;
+  int stages = (kSmemBudget - fixed) / p.stage_bytes;
   if (stages < 2) {
     p.stage_bytes = max_slice;
-    stages = (kSmemBudget - 2 * abytes) / p.stage_bytes;
+    stages = (kSmemBudget - fixed) / p.stage_bytes;
   }
   p.stages = stages > kMaxStages ? kMaxStages : stages;
   if (p.stages < 2) return set_error(CG_ERR_ARGUMENT, "tensor-core dense layer does not fit in shared memory");
@@ -773,7 +826,7 @@ int launch_dense(TcParams& p, cudaStream_t s) {
     const int per = p.stage_bytes / (p.ops[i].n * 32);
     p.ops[i].ks_per_stage = per < p.ops[i].ksteps ? per : p.ops[i].ksteps;
   }
-  const int smem = 2 * abytes + p.stages * p.stage_bytes;
+  const int smem = fixed + p.stages * p.stage_bytes;
   static int configured_smem[64] = {0};
   int device = 0;
   cudaGetDevice(&device);
@@ -853,6 +906,8 @@ int run_tc_forward(const cg_trunk_dims& dims, const void* blob, const BlobLayout
   p.max_len = max_len;
   p.positions = positions;
   p.rows = rows;
+  p.hbytes = kTile * (f < kUpCols ? f : kUpCols) * 2;
+  p.n_up = up_chunks(dims);
   p.ple_scale = [&] {
     if (!p.P || p.P == d) return 1.f;
     return static_cast<float>(1.0 / std::sqrt(static_cast<double>((d + p.P - 1) / p.P)));
@@ -866,7 +921,7 @@ int run_tc_forward(const cg_trunk_dims& dims, const void* blob, const BlobLayout
     op.ksteps = d / 16;
     op.tmem_col = 0;
     op.wait_a = 1;
-    op.signal = qw <= 256;
+    op.signal = qw <= 256 ? kSigAcc : kSigNone;
     p.ops[p.n_ops++] = op;
     if (qw > 256) {
       GemmOp rest{};
@@ -874,7 +929,7 @@ int run_tc_forward(const cg_trunk_dims& dims, const void* blob, const BlobLayout
       rest.n = qw - 256;
       rest.ksteps = d / 16;
       rest.tmem_col = 256;
-      rest.signal = 1;
+      rest.signal = kSigAcc;
       p.ops[p.n_ops++] = rest;
     }
   };
@@ -903,7 +958,7 @@ int run_tc_forward(const cg_trunk_dims& dims, const void* blob, const BlobLayout
       op.ksteps = d / 16;
       op.tmem_col = 0;
       op.wait_a = 1;
-      op.signal = 1;
+      op.signal = kSigAcc;
       p.ops[p.n_ops++] = op;
     }
   } else {
@@ -965,28 +1020,34 @@ int run_tc_forward(const cg_trunk_dims& dims, const void* blob, const BlobLayout
     out.ksteps = d / 16;
     out.tmem_col = 0;
     out.wait_a = 1;
-    out.signal = 1;
+    out.signal = kSigAcc;
     p.ops[p.n_ops++] = out;
-    const int chunks = f / d;
-    for (int c = 0; c < chunks; ++c) {
+    // MLP, double-buffered: up(0), up(1), then per chunk c: down(c) (after GELU(c)), up(c+2).
+    const int n_up = p.n_up;
+    auto push_up = [&](int c) {
       GemmOp up{};
-      up.w = lp.up + static_cast<int64_t>(c) * d * d;
-      up.n = d;
+      up.w = lp.up + static_cast<int64_t>(c) * kUpCols * d;
+      up.n = up_width(dims, c);
       up.ksteps = d / 16;
-      up.tmem_col = 256;
-      up.wait_a = c == 0;
-      up.signal = 1;
+      up.tmem_col = kAccCols + (c & 1) * kUpCols;
+      up.wait_a = c == 0;  // LN_mlp(x) in the A buffer
+      up.signal = (c & 1) ? kSigUp1 : kSigUp0;
       p.ops[p.n_ops++] = up;
+    };
+    push_up(0);
+    if (n_up > 1) push_up(1);
+    for (int c = 0; c < n_up; ++c) {
       GemmOp down{};
-      down.w = lp.down + static_cast<int64_t>(c) * d * d;
+      down.w = lp.down + static_cast<int64_t>(c) * kUpCols * d;
       down.n = d;
-      down.ksteps = d / 16;
+      down.ksteps = up_width(dims, c) / 16;
       down.tmem_col = 0;
-      down.a_src = 1;
+      down.a_src = 1 + (c & 1);
       down.accumulate_first = c > 0;
-      down.wait_a = 1;
-      down.signal = c == chunks - 1;
+      down.wait_a = 1;  // GELU(c) in H buffer c % 2
+      down.signal = c == n_up - 1 ? kSigAcc : (c + 2 < n_up ? ((c & 1) ? kSigHFree1 : kSigHFree0) : kSigNone);
       p.ops[p.n_ops++] = down;
+      if (c + 2 < n_up) push_up(c + 2);
     }
     if (p.has_next) {
       push_qkv(layer + 1);
