@@ -52,8 +52,8 @@ ATTENTION_DRAM_BYTES_PER_LAUNCH: float | None = None
 def parse_args(argv=None):
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--gpus", type=int, default=1)
-    parser.add_argument("--steps", type=int, default=30)
-    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--steps", type=int, default=300)
+    parser.add_argument("--warmup", type=int, default=10)
     parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
     parser.add_argument("--games", type=int, default=4096, help="concurrent 4-player games per GPU")
     parser.add_argument("--min-len", type=int, default=16)
@@ -63,6 +63,9 @@ def parse_args(argv=None):
     parser.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     parser.add_argument("--cpu-games", type=int, default=32, help="games per CPU-baseline wave")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--ppo-decisions", type=int, default=262144,
+                        help="PPO update batch (whole job, sharded by trajectory); 0 skips the PPO leg")
+    parser.add_argument("--ppo-steps", type=int, default=20)
     return parser.parse_args(argv)
 
 
@@ -103,6 +106,126 @@ def synthetic_wave(games: int, min_len: int, max_len: int, seed: int) -> dict[st
     uniforms = rng.random(games)
     return dict(tokens=tokens, positions=positions, offsets=np.zeros(rows, np.int64), readout_rows=readout_rows,
                 heads=heads, legal=legal.astype(np.uint8), uniforms=uniforms, lengths=lengths)
+
+
+# ---------------------------------------------------------------------------------------------
+# PPO update leg: segmented GAE -> global normalisation -> fused PPO objective + value loss
+# ---------------------------------------------------------------------------------------------
+PPO_PLAYERS = 4
+PPO_ACTIONS = 52
+TRUNK_PARAMS = 8_500_000  # the actor trunk's gradient, allreduced once per optimizer step
+
+
+def synthetic_ppo_batch(decisions: int, seed: int) -> dict[str, np.ndarray]:
+    """The PPO-update config: trajectories of U[13,52] decisions (the last one cut to the total),
+    values N(0,1), zero-sum terminal returns N(0,1), 52-way Bernoulli(0.3) legal masks with one
+    forced legal action, new logits = old + N(0,0.05), actions drawn from the old policy."""
+
+    rng = np.random.default_rng(seed)
+    lengths = []
+    while sum(lengths) < decisions:
+        lengths.append(int(rng.integers(13, 53)))
+    lengths[-1] -= sum(lengths) - decisions
+    starts = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int64)
+    games = len(lengths)
+    returns = rng.standard_normal((games, PPO_PLAYERS))
+    returns -= returns.mean(axis=1, keepdims=True)
+    legal = rng.random((decisions, PPO_ACTIONS)) < 0.3
+    legal[np.arange(decisions), rng.integers(0, PPO_ACTIONS, decisions)] = True
+    old = rng.standard_normal((decisions, PPO_ACTIONS)).astype(np.float32)
+    masked = np.where(legal, old, -np.inf)
+    probs = np.exp(masked - masked.max(axis=1, keepdims=True))
+    probs /= probs.sum(axis=1, keepdims=True)
+    cdf = np.cumsum(probs, axis=1)
+    actions = np.minimum((cdf < rng.random((decisions, 1))).sum(axis=1), PPO_ACTIONS - 1)
+    return dict(
+        starts=starts, values=rng.standard_normal((decisions, PPO_PLAYERS)), seats=rng.integers(0, 4, decisions),
+        returns=returns, logits=old + rng.normal(0.0, 0.05, old.shape).astype(np.float32),
+        old_probs=probs.astype(np.float32), actions=actions.astype(np.int64),
+        weights=np.full(decisions, 1.0 / (games * PPO_PLAYERS)),
+        prediction=rng.standard_normal((decisions, PPO_PLAYERS)).astype(np.float32),
+        targets=np.repeat(returns, lengths, axis=0).astype(np.float32),
+    )
+
+
+def run_ppo(args, device, rank: int, world_size: int) -> dict:
+    """Time the PPO advantage + loss step on this rank's trajectory shard (max over ranks)."""
+
+    import torch
+    import torch.distributed as dist
+
+    from card_playing_gym_b200 import ppo
+    from card_playing_gym_b200.data_parallel import global_weighted_mean_std, shard_games
+
+    batch = synthetic_ppo_batch(args.ppo_decisions, seed=5)
+    g0, g1 = shard_games(batch["starts"], world_size, rank)
+    d0, d1 = int(batch["starts"][g0]), int(batch["starts"][g1])
+    to = lambda a, dtype=None: torch.as_tensor(np.ascontiguousarray(a)).to(device=device, dtype=dtype)  # noqa: E731
+    values = to(batch["values"][d0:d1], torch.float64)
+    seats = to(batch["seats"][d0:d1], torch.int32)
+    starts = to(batch["starts"][g0:g1 + 1] - d0, torch.int64)
+    returns = to(batch["returns"][g0:g1], torch.float64)
+    logits = to(batch["logits"][d0:d1])
+    old_probs = to(batch["old_probs"][d0:d1])
+    actions = to(batch["actions"][d0:d1])
+    weights = to(batch["weights"][d0:d1], torch.float32)
+    weights64 = to(batch["weights"][d0:d1], torch.float64)
+    prediction = to(batch["prediction"][d0:d1])
+    targets = to(batch["targets"][d0:d1])
+    players = torch.full((d1 - d0,), PPO_PLAYERS, dtype=torch.int32, device=device)
+    gradient = torch.zeros(TRUNK_PARAMS, device=device) if world_size > 1 else None
+
+    def step():
+        advantages = ppo.segmented_gae(values, seats, starts, returns, 0.95)
+        mean, std = global_weighted_mean_std(advantages, weights64)
+        ppo.normalize_(advantages, mean, std)
+        leaf = logits.detach().requires_grad_()
+        objective, _ = ppo.policy_objective(leaf, old_probs, actions, advantages, weights, clip_ratio=0.2, alpha=0.01)
+        pred = prediction.detach().requires_grad_()
+        loss, _ = ppo.value_loss(pred, players, targets, weights, 1.0)
+        (objective + loss).backward()
+        if gradient is not None:
+            dist.all_reduce(gradient)
+        return leaf.grad, pred.grad
+
+    for _ in range(3):
+        step()
+    if world_size > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    stream = torch.cuda.current_stream(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.ppo_steps):
+        step()
+    end.record(stream)
+    torch.cuda.synchronize(device)
+    ms = start.elapsed_time(end) / args.ppo_steps
+    if world_size > 1:
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    n, g, a, pl = d1 - d0, g1 - g0, PPO_ACTIONS, PPO_PLAYERS
+    # Bytes the kernels must move on this rank: GAE, two normalisation passes + the in-place
+    # normalise, the fused objective (logits, old probs, actions, advantages, weights in; dlogits
+    # out) and the value loss (prediction, targets, players, weights in; gradient out).
+    algorithmic = (n * pl * 8 + n * 4 + g * pl * 8 + (g + 1) * 8 + n * 8) + 2 * (n * 16) + n * 16 \
+        + (3 * n * a * 4 + n * 8 + n * 4 + n * 4) + (3 * n * pl * 4 + n * 8)
+    peak, peak_kind = measured_peak()
+    achieved = algorithmic / (ms / 1000.0) / 1e9
+    return {
+        "workload": (f"PPO advantage + loss step: {args.ppo_decisions} decisions in U[13,52] trajectories, "
+                     f"{PPO_PLAYERS} seats, {PPO_ACTIONS}-way legal-masked logits, lambda 0.95, clip 0.2"),
+        "decisions": args.ppo_decisions, "decisions_per_gpu": n, "games_per_gpu": g, "ms_per_step": ms,
+        "decisions_per_s": args.ppo_decisions / (ms / 1000.0), "scaling": "strong",
+        "steps": args.ppo_steps, "algorithmic_bytes_per_gpu": algorithmic, "achieved_gbs": achieved,
+        "hbm_frac": achieved / peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+        "collectives": ("none" if world_size == 1 else
+                        f"2 x 3-scalar allreduce (global mean/std) + {TRUNK_PARAMS * 4 / 1e6:.0f} MB gradient "
+                        "allreduce (NCCL) per step"),
+        "includes": "GAE, global two-pass mean/std (two host reads), normalise, fused PPO objective fwd+grad, "
+                    "value loss fwd+grad, autograd backward",
+    }
 
 
 # ---------------------------------------------------------------------------------------------
@@ -205,7 +328,7 @@ class ClockSampler:
         self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={CLOCK_FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                ["nvidia-smi", f"--query-gpu={CLOCK_FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=self.file, stderr=subprocess.DEVNULL,
             )
         except OSError:
@@ -353,13 +476,14 @@ def run_b200(args) -> int:
     barrier()
     e2e_ms = max_over_ranks(start.elapsed_time(end))
     e2e_value = world_size * games * args.steps / (e2e_ms / 1000.0)
+    ppo_line = run_ppo(args, device, rank, world_size) if args.ppo_decisions > 0 else None
 
     if rank == 0:
         head_dim = RL_V6.trunk().head_dim
         esize = torch.tensor([], dtype=kv_dtype).element_size()
         keys = np.minimum(wave["positions"] + 1, span).sum()  # T = 1: key_length = position + 1
         kv_bytes = float(keys) * RL_V6.n_kv_heads * head_dim * esize * 2
-        qo_bytes = rows * RL_V6.n_heads * head_dim * (esize + 4)  # q in the cache dtype, fp32 output
+        qo_bytes = rows * RL_V6.n_heads * head_dim * (esize + 2)  # q in the cache dtype, bf16 output
         algorithmic = kv_bytes + qo_bytes
         mean_ms = statistics.fmean(attention_ms) if attention_ms else float("nan")
         achieved = algorithmic / (mean_ms / 1000.0) / 1e9
@@ -385,6 +509,8 @@ def run_b200(args) -> int:
             "gpu_launches": int(launches),
             "clocks": clock_info,
         }
+        if ppo_line is not None:
+            line["ppo"] = ppo_line
         if world_size == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args, args.cpu_seconds)
         print(json.dumps(line), flush=True)
