@@ -259,6 +259,8 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
   const int gid = lane >> 2, tid4 = lane & 3;
   KV* stage_base = reinterpret_cast<KV*>(smem_raw + wib * Shape::kWarpBytes);
   const uint64_t policy = evict_first_policy();
+  pdl_wait();  // q, K and V come from the kernel before
+  pdl_trigger();
 
   const int units = static_cast<int>(p.batch * p.kv_heads);  // < 2^31: checked by the host
   const int M = p.group * p.steps;
@@ -643,8 +645,8 @@ int launch_tc(const AttnParams& p, cudaStream_t stream) {
   const int64_t needed = (units + kTcWarps - 1) / kTcWarps;
   if (blocks > needed) blocks = needed;
   if (blocks < 1) return CG_OK;
-  kernel<<<static_cast<unsigned>(blocks), kTcWarps * 32, smem, stream>>>(p);
-  return check_launch("attn_tc_kernel");
+  return launch_pdl("attn_tc_kernel", kernel, dim3(static_cast<unsigned>(blocks)), dim3(kTcWarps * 32), smem, stream,
+                    p);
 }
 
 template <typename KV, int D>

@@ -1,6 +1,8 @@
 // Shared helpers for the card_playing_gym_b200 native library (sm_100a only).
 #pragma once
 
+#include <utility>
+
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
@@ -24,6 +26,32 @@ int check_launch(const char* what);
 extern __device__ int g_fault;
 
 __device__ __forceinline__ void raise_fault(int code) { atomicCAS(&g_fault, 0, code); }
+
+// Programmatic dependent launch. A kernel started by launch_pdl may begin while the kernel
+// before it in the stream is still running: it may set up (barriers, tensor memory, copies
+// of constant weights) but must call pdl_wait() before it reads or writes anything an earlier
+// kernel of the stream touches. pdl_trigger(), issued after the wait, lets the next kernel of
+// the stream start its own set-up early; so at most two kernels ever overlap.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KernelArgs, typename... Args>
+int launch_pdl(const char* what, void (*kernel)(KernelArgs...), dim3 grid, dim3 block, size_t smem,
+               cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t config = {};
+  config.gridDim = grid;
+  config.blockDim = block;
+  config.dynamicSmemBytes = smem;
+  config.stream = stream;
+  cudaLaunchAttribute attribute[1];
+  attribute[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attribute[0].val.programmaticStreamSerializationAllowed = 1;
+  config.attrs = attribute;
+  config.numAttrs = 1;
+  cudaError_t err = cudaLaunchKernelEx(&config, kernel, std::forward<Args>(args)...);
+  if (err != cudaSuccess) return set_error(CG_ERR_CUDA, "%s launch: %s", what, cudaGetErrorString(err));
+  return check_launch(what);
+}
 
 // ---- element access by runtime dtype --------------------------------------------
 __device__ __forceinline__ float load_as_float(const void* base, int64_t index, int dtype) {

@@ -139,6 +139,8 @@ __global__ void __launch_bounds__(kDecThreads) decide_kernel(cg_heads_desc desc,
     }
     row_off[r] = off;
   }
+  pdl_wait();  // hidden comes from the kernel before
+  pdl_trigger();
   // The tile's hidden rows, transposed (k-major) and zero-padded.
   for (int idx = tid; idx < kDecTile * g.d_pad; idx += kDecThreads) {
     const int i = idx / g.d_pad, k = idx - i * g.d_pad;
@@ -291,8 +293,7 @@ extern "C" int cg_plump_decide(const cg_heads_desc* desc, const float* heads_blo
     configured[device & 63] = smem;
   }
   const unsigned blocks = static_cast<unsigned>((decisions + kDecTile - 1) / kDecTile);
-  decide_kernel<<<blocks, kDecThreads, smem, static_cast<cudaStream_t>(stream)>>>(
-      *desc, g, heads_blob, hidden, hidden_rows, decisions, head_of, legal, uniforms, logits_out, probs_out,
-      actions_out, values_out);
-  return check_launch("decide_kernel");
+  return launch_pdl("decide_kernel", decide_kernel, dim3(blocks), dim3(kDecThreads), smem,
+                    static_cast<cudaStream_t>(stream), *desc, g, heads_blob, hidden, hidden_rows, decisions, head_of,
+                    legal, uniforms, logits_out, probs_out, actions_out, values_out);
 }

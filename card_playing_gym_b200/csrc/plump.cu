@@ -151,7 +151,9 @@ __global__ void __launch_bounds__(kEmbedThreads, 1) plump_embed_sliced_kernel(
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  load_slice(0, 0);
+  load_slice(0, 0);  // the table is constant: its first slice loads while the kernel before finishes
+  pdl_wait();
+  pdl_trigger();
 
   // Row ids, one warp per token (the same resolution as plump_embed_kernel).
   const unsigned lt = (1u << lane) - 1u;
@@ -276,9 +278,8 @@ int embed(const cg_plump_schema& sc, const float* table, int width, const void* 
       if (err != cudaSuccess) return set_error(CG_ERR_CUDA, "plump_embed_sliced_kernel smem: %s", cudaGetErrorString(err));
       configured[device & 63] = smem;
     }
-    kernel<<<static_cast<unsigned>(blocks), kEmbedThreads, smem, s>>>(sc, table, width, tokens, token_dtype, n,
-                                                                      static_cast<int>(per), out);
-    return check_launch("plump_embed_sliced_kernel");
+    return launch_pdl("plump_embed_sliced_kernel", kernel, dim3(static_cast<unsigned>(blocks)), dim3(kEmbedThreads),
+                      smem, s, sc, table, width, tokens, token_dtype, n, static_cast<int>(per), out);
   };
   if (slice_f4 == 16) return launch(plump_embed_sliced_kernel<16>);
   if (slice_f4 == 8) return launch(plump_embed_sliced_kernel<8>);

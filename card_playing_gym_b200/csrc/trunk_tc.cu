@@ -88,6 +88,11 @@ struct TcParams {
   int kv_dtype, max_len;
   const int64_t* positions;
   const int64_t* rows;
+  // Last layer: the final LayerNorm at each row's readout token goes straight to hidden_out.
+  const float* final_w;
+  const float* final_b;
+  const int64_t* readout_offsets;
+  float* hidden_out;
 };
 
 // ---- blocked activation helpers -------------------------------------------------------------
@@ -180,9 +185,12 @@ __device__ __forceinline__ float row_sum(float value, const EpiThread& e, float 
 }
 
 // LayerNorm (eps 1e-5, biased variance, mean then centred variance) of the row held in
-// registers (this thread's chunks lo..hi-1 of d), written as bf16 into the operand buffer.
+// registers (this thread's chunks lo..hi-1 of d), written as bf16 into the operand buffer,
+// or, with to_row, as fp32 into out_row (a row-major d-wide row; skipped when null). Every
+// epilogue thread takes part (the row statistics go through named barriers).
 __device__ void layer_norm_regs(const float (&x)[kMaxRowChunks][16], int lo, int hi, int d, const EpiThread& e,
-                                const float* w, const float* b, unsigned char* abuf, float (*red)[kTile]) {
+                                const float* w, const float* b, unsigned char* abuf, float (*red)[kTile],
+                                bool to_row = false, float* out_row = nullptr) {
   float part = 0.f;
 #pragma unroll
   for (int c = 0; c < kMaxRowChunks; ++c)
@@ -210,7 +218,13 @@ __device__ void layer_norm_regs(const float (&x)[kMaxRowChunks][16], int lo, int
     float y[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) y[i] = (x[c][i] - mean) * rstd * wv[i] + bv[i];
-    store_operand16(abuf, col, e.t, y);
+    if (!to_row) {
+      store_operand16(abuf, col, e.t, y);
+    } else if (out_row) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        reinterpret_cast<float4*>(out_row + col)[q] = make_float4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
+    }
   }
 }
 
@@ -307,6 +321,8 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
                                float (*red)[kTile]) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t tile = blockIdx.x;
+  pdl_wait();  // the epilogue reads and writes what earlier kernels of the stream touch
+  pdl_trigger();
   EpiThread e;
   e.t = (warp & 3) * 32 + lane;
   e.qd = warp >> 2;  // 0 .. kParts-1
@@ -449,7 +465,7 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
       tc::tmem_ld16(e.lane_tmem + col, v16);
 #pragma unroll
       for (int i = 0; i < 16; ++i) x[c][i] += v16[i];
-      store16(p.x_blk, tile, d, col, t, x[c]);
+      if (p.has_next) store16(p.x_blk, tile, d, col, t, x[c]);
     }
     if (p.has_next) {
       layer_norm_regs(x, lo, hi, d, e, p.ln_next_w, p.ln_next_b, abuf, red);
@@ -457,6 +473,12 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
       if (val_smem && !group_wait(val_full_bar, 0, 0x405)) return;
       if (!wait_acc()) return;
       qkv_epilogue(p, e, tile, val_smem ? reinterpret_cast<const float4*>(h0) : nullptr);
+    } else {
+      // Final LayerNorm only at each row's readout token (trunk.py:426-429), straight to hidden.
+      const int64_t b = row / p.T;
+      const int tt = static_cast<int>(row - b * p.T);
+      const bool readout = valid && (p.T == 1 || tt == p.readout_offsets[b]);
+      layer_norm_regs(x, lo, hi, d, e, p.final_w, p.final_b, abuf, red, true, readout ? p.hidden_out + b * d : nullptr);
     }
     return;
   }
@@ -835,34 +857,10 @@ int launch_dense(TcParams& p, cudaStream_t s) {
     if (err != cudaSuccess) return set_error(CG_ERR_CUDA, "tc_dense_kernel smem: %s", cudaGetErrorString(err));
     configured_smem[device & 63] = smem;
   }
-  tc_dense_kernel<<<static_cast<unsigned>(p.ntiles), kTcThreads, smem, s>>>(p);
-  return check_launch("tc_dense_kernel");
-}
-
-__global__ void readout_norm_kernel(const float* __restrict__ x_blk, int d, int steps, int64_t batch,
-                                    const int64_t* __restrict__ offsets, const float* __restrict__ w,
-                                    const float* __restrict__ b, float* __restrict__ out) {
-  const int lane = threadIdx.x & 31;
-  const int64_t bi = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  if (bi >= batch) return;
-  const int64_t row = bi * steps + offsets[bi];
-  const int64_t tile = row / kTile;
-  const int t = static_cast<int>(row % kTile);
-  auto at = [&](int k) {
-    const float4 e = reinterpret_cast<const float4*>(x_blk)[(tile * (d / 4) + k / 4) * kTile + t];
-    const int l = k & 3;
-    return l == 0 ? e.x : l == 1 ? e.y : l == 2 ? e.z : e.w;
-  };
-  float sum = 0.f;
-  for (int k = lane; k < d; k += 32) sum += at(k);
-  const float mean = warp_sum(sum) / d;
-  float var = 0.f;
-  for (int k = lane; k < d; k += 32) {
-    const float c = at(k) - mean;
-    var += c * c;
-  }
-  const float rstd = rsqrtf(warp_sum(var) / d + 1e-5f);
-  for (int k = lane; k < d; k += 32) out[bi * d + k] = (at(k) - mean) * rstd * w[k] + b[k];
+  // The producer warp streams only the constant packed weights, so it starts at once; the
+  // epilogue warps wait for the kernel before (pdl_wait in dense_epilogue).
+  return launch_pdl("tc_dense_kernel", tc_dense_kernel, dim3(static_cast<unsigned>(p.ntiles)), dim3(kTcThreads), smem,
+                    s, p);
 }
 
 int run_tc_forward(const cg_trunk_dims& dims, const void* blob, const BlobLayout& L, int64_t batch, int steps,
@@ -906,6 +904,10 @@ int run_tc_forward(const cg_trunk_dims& dims, const void* blob, const BlobLayout
   p.max_len = max_len;
   p.positions = positions;
   p.rows = rows;
+  p.final_w = part(blob, L, CG_PART_FINAL_W, 0);
+  p.final_b = part(blob, L, CG_PART_FINAL_B, 0);
+  p.readout_offsets = readout_offsets;
+  p.hidden_out = hidden_out;
   p.hbytes = kTile * (f < kUpCols ? f : kUpCols) * 2;
   p.n_up = up_chunks(dims);
   p.ple_scale = [&] {
@@ -1056,10 +1058,7 @@ int run_tc_forward(const cg_trunk_dims& dims, const void* blob, const BlobLayout
     if (p.n_ops > kMaxOps) return set_error(CG_ERR_ARGUMENT, "too many GEMM steps in one dense layer");
     if ((rc = launch_dense(p, s))) return rc;
   }
-  readout_norm_kernel<<<static_cast<unsigned>((batch + 7) / 8), 256, 0, s>>>(
-      w.x_blk, d, steps, batch, readout_offsets, part(blob, L, CG_PART_FINAL_W, 0), part(blob, L, CG_PART_FINAL_B, 0),
-      hidden_out);
-  return check_launch("readout_norm_kernel");
+  return CG_OK;  // the last layer's epilogue wrote the readout hidden states
 }
 
 int tc_condition_ple(const cg_trunk_dims&, const void*, const BlobLayout&, const float*, const float*, int64_t, int64_t,
