@@ -158,7 +158,7 @@ def run_ppo(args, device, rank: int, world_size: int) -> dict:
     import torch.distributed as dist
 
     from card_playing_gym_b200 import ppo
-    from card_playing_gym_b200.data_parallel import global_weighted_mean_std, shard_games
+    from card_playing_gym_b200.data_parallel import normalize_global_, shard_games
 
     batch = synthetic_ppo_batch(args.ppo_decisions, seed=5)
     g0, g1 = shard_games(batch["starts"], world_size, rank)
@@ -180,8 +180,7 @@ def run_ppo(args, device, rank: int, world_size: int) -> dict:
 
     def step():
         advantages = ppo.segmented_gae(values, seats, starts, returns, 0.95)
-        mean, std = global_weighted_mean_std(advantages, weights64)
-        ppo.normalize_(advantages, mean, std)
+        normalize_global_(advantages, weights64)  # batch-global two-pass mean/std, no host read
         leaf = logits.detach().requires_grad_()
         objective, _ = ppo.policy_objective(leaf, old_probs, actions, advantages, weights, clip_ratio=0.2, alpha=0.01)
         pred = prediction.detach().requires_grad_()
@@ -226,8 +225,8 @@ def run_ppo(args, device, rank: int, world_size: int) -> dict:
         "collectives": ("none" if world_size == 1 else
                         f"2 x 3-scalar allreduce (global mean/std) + {TRUNK_PARAMS * 4 / 1e6:.0f} MB gradient "
                         "allreduce (NCCL) per step"),
-        "includes": "GAE, global two-pass mean/std (two host reads), normalise, fused PPO objective fwd+grad, "
-                    "value loss fwd+grad, autograd backward",
+        "includes": "GAE, global two-pass mean/std and normalise on the device (no host read), fused PPO "
+                    "objective fwd+grad, value loss fwd+grad, autograd backward",
     }
 
 

@@ -91,6 +91,8 @@ _SIGNATURES: dict[str, tuple[type, list]] = {
     "cg_weighted_sums_workspace_bytes": (_i64, [_i64]),
     "cg_weighted_sums": (_i32, [_p, _p, _i64, _f64, _p, _p, _i64, _p]),
     "cg_normalize": (_i32, [_p, _i64, _f64, _f64, _p]),
+    "cg_weighted_sums_shifted": (_i32, [_p, _p, _i64, _p, _p, _p, _i64, _p]),
+    "cg_normalize_from_sums": (_i32, [_p, _i64, _p, _p, _p]),
     "cg_ppo_objective_workspace_bytes": (_i64, [_i64]),
     "cg_ppo_objective": (_i32, [_p, _p, _i64, _i32, _i64, _p, _p, _p, _f32, _f32, _p, _p, _p, _p, _i64, _p]),
     "cg_value_loss_workspace_bytes": (_i64, [_i64]),

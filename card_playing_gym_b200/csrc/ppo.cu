@@ -35,9 +35,16 @@ __global__ void gae_kernel(const double* __restrict__ values, int players, const
 }
 
 // ---- weighted sums ---------------------------------------------------------------------
+// mean = sum w x / sum w from a first pass's sums (0 without weight), as mean_std_from_sums.
+__device__ __forceinline__ double mean_from_sums(const double* first) {
+  return first[0] > 0 ? first[1] / first[0] : 0.0;
+}
+
+// shift_from: when non-null, the shift is the mean of a first pass's sums, read on the device.
 __global__ void weighted_sums_kernel(const double* __restrict__ x, const double* __restrict__ w, int64_t n,
-                                     double shift, double* partial) {
+                                     double shift, const double* __restrict__ shift_from, double* partial) {
   __shared__ double s[3][256];
+  if (shift_from) shift = mean_from_sums(shift_from);
   double a = 0, b = 0, c = 0;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -68,6 +75,18 @@ __global__ void sum_partials_kernel(const double* partial, int count, int width,
 }
 
 __global__ void normalize_kernel(double* x, int64_t n, double mean, double std) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    x[i] = (x[i] - mean) / std;
+}
+
+// The same with mean and std from the two passes' sums on the device (ppo.py:147-153:
+// mean = sum w x / sum w, std = sqrt(max(sum w (x - mean)^2 / sum w, 1e-12)); (0, 1) without weight).
+__global__ void normalize_from_sums_kernel(double* x, int64_t n, const double* __restrict__ first,
+                                           const double* __restrict__ second) {
+  const double total = first[0];
+  const double mean = total > 0 ? first[1] / total : 0.0;
+  const double std = total > 0 ? sqrt(fmax(second[2] / total, 1e-12)) : 1.0;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x)
     x[i] = (x[i] - mean) / std;
@@ -273,11 +292,40 @@ extern "C" int cg_weighted_sums(const double* values, const double* weights, int
     return set_error(CG_ERR_WORKSPACE, "cg_weighted_sums: workspace too small");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   double* partial = static_cast<double*>(workspace);
-  weighted_sums_kernel<<<blocks, 256, 0, s>>>(values, weights, n, shift, partial);
+  weighted_sums_kernel<<<blocks, 256, 0, s>>>(values, weights, n, shift, nullptr, partial);
   int rc = check_launch("weighted_sums_kernel");
   if (rc) return rc;
   sum_partials_kernel<<<1, 32, 0, s>>>(partial, blocks, 3, out3);
   return check_launch("sum_partials_kernel");
+}
+
+extern "C" int cg_weighted_sums_shifted(const double* values, const double* weights, int64_t n,
+                                        const double* shift_sums3, double* out3, void* workspace,
+                                        int64_t workspace_bytes, void* stream) {
+  using namespace cg;
+  CG_REQUIRE(n >= 0 && out3 && workspace && shift_sums3, "cg_weighted_sums_shifted: bad arguments");
+  CG_REQUIRE(n == 0 || (values && weights), "cg_weighted_sums_shifted: NULL input");
+  const int blocks = reduce_blocks(n, 256);
+  if (workspace_bytes < static_cast<int64_t>(blocks) * 3 * 8)
+    return set_error(CG_ERR_WORKSPACE, "cg_weighted_sums_shifted: workspace too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  double* partial = static_cast<double*>(workspace);
+  weighted_sums_kernel<<<blocks, 256, 0, s>>>(values, weights, n, 0.0, shift_sums3, partial);
+  int rc = check_launch("weighted_sums_kernel");
+  if (rc) return rc;
+  sum_partials_kernel<<<1, 32, 0, s>>>(partial, blocks, 3, out3);
+  return check_launch("sum_partials_kernel");
+}
+
+extern "C" int cg_normalize_from_sums(double* values, int64_t n, const double* first3, const double* second3,
+                                      void* stream) {
+  using namespace cg;
+  CG_REQUIRE(n >= 0 && first3 && second3, "cg_normalize_from_sums: bad arguments");
+  if (n == 0) return CG_OK;
+  CG_REQUIRE(values, "cg_normalize_from_sums: NULL values");
+  normalize_from_sums_kernel<<<reduce_blocks(n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(values, n, first3,
+                                                                                                  second3);
+  return check_launch("normalize_from_sums_kernel");
 }
 
 extern "C" int cg_normalize(double* values, int64_t n, double mean, double std, void* stream) {

@@ -144,6 +144,26 @@ __device__ __forceinline__ void store_operand16(unsigned char* buf, int col, int
   }
 }
 
+// ---- GELU of the bf16 MLP ------------------------------------------------------------------------------
+// GELU(x) = x Phi(x), with 0.5 erfc(z) (z = |x| / sqrt 2) from Abramowitz & Stegun 7.1.26:
+// erfc(z) = t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-z^2), t = 1 / (1 + p z), |error| <= 1.5e-7.
+// The GELU's absolute error stays below 5e-7, far inside the bf16 rounding of its output (the
+// down-projection operand); Phi(x) = 1 - 0.5 erfc(z) for x >= 0 and 0.5 erfc(z) below, so the
+// negative tail keeps its relative accuracy instead of cancelling.
+__device__ __forceinline__ float gelu_bf16_operand(float x) {
+  const float z = fabsf(x) * 0.70710678118654752f;
+  float t;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(fmaf(0.3275911f, z, 1.f)));
+  float q = fmaf(t, 0.5f * 1.061405429f, 0.5f * -1.453152027f);  // the 0.5 of 0.5 erfc folded in
+  q = fmaf(q, t, 0.5f * 1.421413741f);
+  q = fmaf(q, t, 0.5f * -0.284496736f);
+  q = fmaf(q, t, 0.5f * 0.254829592f);
+  float e;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-z * z * 1.4426950408889634f));
+  const float c = q * t * e;  // 0.5 erfc(z) = Phi(-|x|)
+  return x * (x >= 0.f ? 1.f - c : c);
+}
+
 // ---- epilogue geometry ---------------------------------------------------------------------------------
 // 12 epilogue warps; thread e belongs to warp w = e / 32. Warp w may only touch TMEM lanes
 // 32 * (w % 4) .. + 31, so row t = 32 * (w % 4) + lane, and the three warps with the same w % 4
@@ -316,7 +336,7 @@ __device__ void qkv_epilogue(const TcParams& p, const EpiThread& e, int64_t tile
 
 // ---- epilogue warps ----------------------------------------------------------------------------------------
 __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned char* h0, unsigned char* h1, uint32_t tmem,
-                               uint64_t* a_ready_bar, uint64_t* acc_ready_bar, uint64_t* up_ready_bar,
+                               uint64_t* a_ready_bar, uint32_t publish_to, uint64_t* acc_ready_bar, uint64_t* up_ready_bar,
                                uint64_t* h_free_bar, uint64_t* attn_full_bar, uint64_t* val_full_bar, int abytes,
                                float (*red)[kTile]) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -342,7 +362,12 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
     tc::fence_async_smem();
     tc::fence_before_sync();
     epi_sync();
-    if (threadIdx.x == 0) tc::bar_arrive(a_ready_bar);
+    if (threadIdx.x == 0) {
+      if (publish_to)
+        tc::bar_arrive_cluster(publish_to);  // the odd CTA of a pair publishes to the even CTA's issuer
+      else
+        tc::bar_arrive(a_ready_bar);
+    }
   };
   auto group_wait = [&](uint64_t* bar, uint32_t parity, int code) -> bool {
     if (threadIdx.x == 0) red[2 * kParts][0] = tc::bar_wait(bar, parity, code) ? 1.f : 0.f;
@@ -413,7 +438,7 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
           if (h == 1 && !two) break;
           float g[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) g[i] = gelu_erf(v[16 * h + i] + bias[h][i]);
+          for (int i = 0; i < 16; ++i) g[i] = gelu_bf16_operand(v[16 * h + i] + bias[h][i]);
           store_operand16(hb, (c + h) * 16, t, g);
         }
       }
@@ -571,14 +596,23 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
 }
 
 // ---- the kernel ------------------------------------------------------------------------------------------
+// kPairTiles: CTAs run in clusters of two on two SMs. Each CTA owns a 128-row tile; one M = 256
+// tcgen05.mma issued by the even CTA covers both tiles, and each CTA's shared memory holds
+// only half of every weight stage (B's N rows split in halves), so each SM streams half the
+// weights. The odd CTA's MMA warp relays its stage arrivals to the even CTA; MMA completions
+// are committed to the barriers of both CTAs; both epilogues publish to the even CTA.
+constexpr bool kPairTiles = true;
+
 __global__ void __launch_bounds__(kTcThreads, 1) tc_dense_kernel(const __grid_constant__ TcParams p) {
+  constexpr bool kPair = kPairTiles;
   extern __shared__ __align__(1024) unsigned char smem[];
-  __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages];
-  __shared__ __align__(8) uint64_t a_ready, acc_ready, attn_full, val_full, up_ready[2], h_free[2];
+  __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages], peer_full[kMaxStages];
+  __shared__ __align__(8) uint64_t a_ready, acc_ready, attn_full, val_full, up_ready[2], h_free[2], mma_done;
   __shared__ uint32_t tmem_base;
   __shared__ float red[2 * kParts + 1][kTile];  // row reductions across a row's threads; last row: wait status
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = kPair ? tc::cluster_ctarank() : 0u;
   const int abytes = kTile * p.d * 2;
   unsigned char* abuf = smem;
   unsigned char* h0 = smem + abytes;
@@ -589,11 +623,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dense_kernel(const __grid_co
     for (int s = 0; s < p.stages; ++s) {
       tc::bar_init(&full[s], 1);
       tc::bar_init(&empty[s], 1);
+      tc::bar_init(&peer_full[s], 1);
     }
-    tc::bar_init(&a_ready, 1);
+    tc::bar_init(&a_ready, kPair ? 2 : 1);  // both epilogues publish to the even CTA
     tc::bar_init(&acc_ready, 1);
     tc::bar_init(&attn_full, 1);
     tc::bar_init(&val_full, 1);
+    tc::bar_init(&mma_done, 1);
     for (int b = 0; b < 2; ++b) {
       tc::bar_init(&up_ready[b], 1);
       tc::bar_init(&h_free[b], 1);
@@ -601,29 +637,44 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dense_kernel(const __grid_co
     tc::bar_fence_init();
   }
   if (warp == kMmaWarp) {
-    tc::tmem_alloc(&tmem_base, 512);
-    tc::tmem_relinquish();
+    if (kPair) {
+      tc::tmem_alloc_pair(&tmem_base, 512);
+      tc::tmem_relinquish_pair();
+    } else {
+      tc::tmem_alloc(&tmem_base, 512);
+      tc::tmem_relinquish();
+    }
   }
   tc::fence_before_sync();
   __syncthreads();
+  if (kPair) tc::cluster_sync();  // barriers initialised and tensor memory allocated in both CTAs
   tc::fence_after_sync();
   const uint32_t tmem = tmem_base;
+  auto commit = [&](uint64_t* bar) {
+    if (kPair)
+      tc::mma_commit_pair(bar);
+    else
+      tc::mma_commit(bar);
+  };
 
   if (warp == kProducerWarp) {
     // ---- producer: weight K-slices into the ring, several slices per bulk copy ---------------------
-    // A bulk copy has a fixed cost of ~0.1 us, so each stage carries up to 32 KB of consecutive
-    // K-slices of one GEMM step (they are contiguous in the packed weights).
+    // A bulk copy has a fixed cost of ~0.2 us, so each stage carries up to 32 KB of consecutive
+    // K-slices of one GEMM step (they are contiguous in the packed weights). In pair mode this
+    // CTA loads its half of each slice (the packed op holds all its first-half slices, then
+    // all its second-half slices).
     if (lane == 0) {
       const uint64_t keep = tc::make_policy_evict_last();
       const int stages = p.stages;
       int stage = 0;
       uint32_t lap = 0;  // completed passes over the ring
       for (int o = 0; o < p.n_ops; ++o) {
-        const unsigned char* src = reinterpret_cast<const unsigned char*>(p.ops[o].w);
-        const uint32_t slice = static_cast<uint32_t>(p.ops[o].n) * 32u;
-        const int ksteps = p.ops[o].ksteps, per = p.ops[o].ks_per_stage;
-        for (int s = 0; s < ksteps; s += per) {
-          const uint32_t bytes = slice * static_cast<uint32_t>(min(per, ksteps - s));
+        const GemmOp& op = p.ops[o];
+        const uint32_t slice = static_cast<uint32_t>(kPair ? op.n / 2 : op.n) * 32u;
+        const unsigned char* src =
+            reinterpret_cast<const unsigned char*>(op.w) + rank * slice * static_cast<uint32_t>(op.ksteps);
+        for (int s = 0; s < op.ksteps; s += op.ks_per_stage) {
+          const uint32_t bytes = slice * static_cast<uint32_t>(min(op.ks_per_stage, op.ksteps - s));
           // From the second pass on, the stage must have been released by its MMAs.
           if (lap > 0 && !tc::bar_wait(&empty[stage], (lap - 1) & 1u, 0x400)) goto producer_done;
           tc::bar_expect_tx(&full[stage], bytes);
@@ -638,8 +689,26 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dense_kernel(const __grid_co
     producer_done:;
     }
   } else if (warp == kMmaWarp) {
-    // ---- MMA issuer ---------------------------------------------------------------------------------
-    if (lane == 0) {
+    if (lane == 0 && rank == 1) {
+      // ---- odd CTA of a pair: relay each stage's arrival to the even CTA's MMA issuer ------------------
+      const int stages = p.stages;
+      int stage = 0;
+      uint32_t lap = 0;
+      for (int o = 0; o < p.n_ops; ++o) {
+        bool ok = true;
+        for (int s0 = 0; s0 < p.ops[o].ksteps; s0 += p.ops[o].ks_per_stage) {
+          if (!(ok = tc::bar_wait(&full[stage], lap & 1u, 0x408))) break;
+          tc::bar_arrive_cluster(tc::map_shared(tc::smem_u32(&peer_full[stage]), 0));
+          if (++stage == stages) {
+            stage = 0;
+            ++lap;
+          }
+        }
+        if (!ok) break;
+      }
+      tc::bar_wait(&mma_done, 0, 0x409);  // the even CTA's MMAs into this CTA's TMEM have completed
+    } else if (lane == 0) {
+      // ---- MMA issuer ---------------------------------------------------------------------------------
       const int stages = p.stages;
       const uint32_t ring_addr = tc::smem_u32(ring);
       int stage = 0;
@@ -648,29 +717,35 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dense_kernel(const __grid_co
       for (int o = 0; o < p.n_ops; ++o) {
         const GemmOp op = p.ops[o];
         if (op.wait_a) {
-          if (!tc::bar_wait(&a_ready, a_phase, 0x401)) break;
+          if (!(kPair ? tc::bar_wait_cluster(&a_ready, a_phase, 0x401) : tc::bar_wait(&a_ready, a_phase, 0x401)))
+            break;
           a_phase ^= 1u;
           tc::fence_after_sync();
         }
         const uint32_t a_addr = tc::smem_u32(op.a_src == 0 ? abuf : (op.a_src == 1 ? h0 : h1));
-        const uint32_t slice = static_cast<uint32_t>(op.n) * 32u;
-        const uint32_t idesc = tc::idesc_bf16(128, op.n <= 256 ? op.n : 256);
+        const uint32_t slice = static_cast<uint32_t>(kPair ? op.n / 2 : op.n) * 32u;
+        const uint32_t idesc = tc::idesc_bf16(kPair ? 256 : 128, op.n <= 256 ? op.n : 256);
         const uint32_t idesc_rest = tc::idesc_bf16(128, op.n > 256 ? op.n - 256 : 16);
         bool ok = true;
         for (int s0 = 0; s0 < op.ksteps; s0 += op.ks_per_stage) {
           if (!(ok = tc::bar_wait(&full[stage], lap & 1u, 0x402))) break;
+          if (kPair && !(ok = tc::bar_wait_cluster(&peer_full[stage], lap & 1u, 0x40a))) break;
           tc::fence_after_sync();
           const int end = min(op.ksteps, s0 + op.ks_per_stage);
           for (int s = s0; s < end; ++s) {
             const uint64_t a_desc = tc::smem_desc(a_addr + 2 * s * (kTile * 16), kTile * 16, 128);
             const uint32_t b_addr = ring_addr + stage * p.stage_bytes + (s - s0) * slice;
             const uint32_t acc = (s > 0 || op.accumulate_first) ? 1u : 0u;
-            tc::mma_bf16(tmem + op.tmem_col, a_desc, tc::smem_desc(b_addr, 128, 256), idesc, acc);
-            if (op.n > 256)
-              tc::mma_bf16(tmem + op.tmem_col + 256, a_desc, tc::smem_desc(b_addr + 32 * 256, 128, 256), idesc_rest,
-                           acc);
+            if (kPair) {
+              tc::mma_bf16_pair(tmem + op.tmem_col, a_desc, tc::smem_desc(b_addr, 128, 256), idesc, acc);
+            } else {
+              tc::mma_bf16(tmem + op.tmem_col, a_desc, tc::smem_desc(b_addr, 128, 256), idesc, acc);
+              if (op.n > 256)
+                tc::mma_bf16(tmem + op.tmem_col + 256, a_desc, tc::smem_desc(b_addr + 32 * 256, 128, 256),
+                             idesc_rest, acc);
+            }
           }
-          tc::mma_commit(&empty[stage]);
+          commit(&empty[stage]);
           if (++stage == stages) {
             stage = 0;
             ++lap;
@@ -678,23 +753,32 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dense_kernel(const __grid_co
         }
         if (!ok) break;
         switch (op.signal) {
-          case kSigAcc: tc::mma_commit(&acc_ready); break;
-          case kSigUp0: tc::mma_commit(&up_ready[0]); break;
-          case kSigUp1: tc::mma_commit(&up_ready[1]); break;
-          case kSigHFree0: tc::mma_commit(&h_free[0]); break;
-          case kSigHFree1: tc::mma_commit(&h_free[1]); break;
+          case kSigAcc: commit(&acc_ready); break;
+          case kSigUp0: commit(&up_ready[0]); break;
+          case kSigUp1: commit(&up_ready[1]); break;
+          case kSigHFree0: commit(&h_free[0]); break;
+          case kSigHFree1: commit(&h_free[1]); break;
           default: break;
         }
       }
+      // Every MMA issued (into both CTAs' TMEM in pair mode) completes before anyone deallocates.
+      commit(&mma_done);
+      tc::bar_wait(&mma_done, 0, 0x409);
     }
   } else {
-    dense_epilogue(p, abuf, h0, h1, tmem, &a_ready, &acc_ready, up_ready, h_free, &attn_full, &val_full, abytes, red);
+    const uint32_t publish_to = kPair && rank == 1 ? tc::map_shared(tc::smem_u32(&a_ready), 0) : 0u;
+    dense_epilogue(p, abuf, h0, h1, tmem, &a_ready, publish_to, &acc_ready, up_ready, h_free, &attn_full, &val_full,
+                   abytes, red);
   }
   tc::fence_before_sync();
   __syncthreads();
+  if (kPair) tc::cluster_sync();  // neither CTA leaves while the other may still reach its memory
   if (warp == kMmaWarp) {
     tc::fence_after_sync();
-    tc::tmem_dealloc(tmem, 512);
+    if (kPair)
+      tc::tmem_dealloc_pair(tmem, 512);
+    else
+      tc::tmem_dealloc(tmem, 512);
   }
 }
 
@@ -757,11 +841,19 @@ bool tc_layers_available(const cg_trunk_dims& dims) {
 
 int tc_pack(const cg_trunk_dims& dims, void* blob, const BlobLayout& L, cudaStream_t s) {
   const int d = dims.d_model, f = dims.d_ff, q = qkv_width(dims);
-  auto pack = [&](const float* w, int ldw, int n0, int N, int k0, int K, __nv_bfloat16* dst) {
-    const int64_t total = static_cast<int64_t>(N) * K;
-    const unsigned blocks = static_cast<unsigned>((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
-    pack_kernel<<<blocks, 256, 0, s>>>(w, ldw, n0, N, k0, K, dst);
-    return check_launch("pack_kernel");
+  // One GEMM step's weights [N x K]: in pair mode as two [N/2 x K] halves one after the other
+  // (the even CTA of a pair loads the first half's slices, the odd CTA the second's).
+  auto pack = [&](const float* w, int ldw, int n0, int N, int k0, int K, __nv_bfloat16* dst) -> int {
+    const int parts = kPairTiles ? 2 : 1;
+    const int rows = N / parts;
+    for (int h = 0; h < parts; ++h) {
+      const int64_t total = static_cast<int64_t>(rows) * K;
+      const unsigned blocks = static_cast<unsigned>((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+      pack_kernel<<<blocks, 256, 0, s>>>(w, ldw, n0 + h * rows, rows, k0, K, dst + h * total);
+      const int rc = check_launch("pack_kernel");
+      if (rc) return rc;
+    }
+    return static_cast<int>(CG_OK);
   };
   if (!tc_layers_available(dims)) return CG_OK;  // the fp32 copies serve the CUDA-core path
   int rc;
@@ -806,8 +898,14 @@ struct TcScratch {
 
 static int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
 
+// Tiles of 128 row-tokens; an even number in pair mode (a pair's odd CTA may hold no rows).
+static int64_t padded_tiles(int64_t nt) {
+  const int64_t tiles = (nt + kTile - 1) / kTile;
+  return kPairTiles ? (tiles + 1) / 2 * 2 : tiles;
+}
+
 TcScratch plan_tc(const cg_trunk_dims& dims, int64_t batch, int steps, unsigned char* base) {
-  const int64_t nt = batch * steps, ntiles = (nt + kTile - 1) / kTile, rows = ntiles * kTile;
+  const int64_t nt = batch * steps, ntiles = padded_tiles(nt), rows = ntiles * kTile;
   const int64_t d = dims.d_model, P = dims.per_layer_dim, L = dims.n_layers;
   const int64_t kvw = static_cast<int64_t>(dims.n_kv_heads) * head_dim(dims), nv = value_layer_count(dims);
   TcScratch s{};
@@ -833,8 +931,9 @@ int64_t tc_layers_scratch_bytes(const cg_trunk_dims& dims, int64_t batch, int st
 int launch_dense(TcParams& p, cudaStream_t s) {
   // Ring stages of up to 32 KB (several consecutive K-slices each); as many as fit.
   const int abytes = kTile * p.d * 2;
+  const int split = kPairTiles ? 2 : 1;  // a pair's CTA holds half of each K-slice
   int max_slice = 0;
-  for (int i = 0; i < p.n_ops; ++i) max_slice = p.ops[i].n * 32 > max_slice ? p.ops[i].n * 32 : max_slice;
+  for (int i = 0; i < p.n_ops; ++i) max_slice = p.ops[i].n / split * 32 > max_slice ? p.ops[i].n / split * 32 : max_slice;
   p.stage_bytes = max_slice > kStageTarget ? max_slice : kStageTarget;
   const int fixed = abytes + 2 * p.hbytes;
   int stages = (kSmemBudget - fixed) / p.stage_bytes;
@@ -845,7 +944,7 @@ int launch_dense(TcParams& p, cudaStream_t s) {
   p.stages = stages > kMaxStages ? kMaxStages : stages;
   if (p.stages < 2) return set_error(CG_ERR_ARGUMENT, "tensor-core dense layer does not fit in shared memory");
   for (int i = 0; i < p.n_ops; ++i) {
-    const int per = p.stage_bytes / (p.ops[i].n * 32);
+    const int per = p.stage_bytes / (p.ops[i].n / split * 32);
     p.ops[i].ks_per_stage = per < p.ops[i].ksteps ? per : p.ops[i].ksteps;
   }
   const int smem = fixed + p.stages * p.stage_bytes;
@@ -859,8 +958,23 @@ int launch_dense(TcParams& p, cudaStream_t s) {
   }
   // The producer warp streams only the constant packed weights, so it starts at once; the
   // epilogue warps wait for the kernel before (pdl_wait in dense_epilogue).
-  return launch_pdl("tc_dense_kernel", tc_dense_kernel, dim3(static_cast<unsigned>(p.ntiles)), dim3(kTcThreads), smem,
-                    s, p);
+  cudaLaunchConfig_t config = {};
+  config.gridDim = dim3(static_cast<unsigned>(p.ntiles));
+  config.blockDim = dim3(kTcThreads);
+  config.dynamicSmemBytes = smem;
+  config.stream = s;
+  cudaLaunchAttribute attribute[2];
+  attribute[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attribute[0].val.programmaticStreamSerializationAllowed = 1;
+  attribute[1].id = cudaLaunchAttributeClusterDimension;
+  attribute[1].val.clusterDim.x = kPairTiles ? 2 : 1;
+  attribute[1].val.clusterDim.y = 1;
+  attribute[1].val.clusterDim.z = 1;
+  config.attrs = attribute;
+  config.numAttrs = 2;
+  cudaError_t err = cudaLaunchKernelEx(&config, tc_dense_kernel, p);
+  if (err != cudaSuccess) return set_error(CG_ERR_CUDA, "tc_dense_kernel launch: %s", cudaGetErrorString(err));
+  return check_launch("tc_dense_kernel");
 }
 
 int run_tc_forward(const cg_trunk_dims& dims, const void* blob, const BlobLayout& L, int64_t batch, int steps,
@@ -892,7 +1006,7 @@ int run_tc_forward(const cg_trunk_dims& dims, const void* blob, const BlobLayout
   p.kvw = KVH * D;
   p.qw = qw;
   p.nt = nt;
-  p.ntiles = (nt + kTile - 1) / kTile;
+  p.ntiles = padded_tiles(nt);
   p.T = steps;
   p.x_blk = w.x_blk;
   p.ple_blk = w.ple_blk;

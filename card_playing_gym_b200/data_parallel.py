@@ -26,7 +26,7 @@ from collections.abc import Callable, Iterable, Sequence
 import torch
 import torch.distributed as dist
 
-from .ppo import mean_std_from_sums, weighted_sums
+from .ppo import mean_std_from_sums, normalize_from_sums_, weighted_sums, weighted_sums_shifted
 
 
 def _world(group) -> tuple[int, int]:
@@ -88,6 +88,16 @@ def global_weighted_mean_std(values: torch.Tensor, weights: torch.Tensor, group=
     mean, _ = mean_std_from_sums(first[0], first[1])
     second = allreduce_sums(sums(values, weights, mean).to(torch.float64), group).tolist()
     return mean_std_from_sums(first[0], first[1], second[2])
+
+
+def normalize_global_(values: torch.Tensor, weights: torch.Tensor, group=None) -> torch.Tensor:
+    """global_weighted_mean_std + normalize_ with no host read: both passes' sums stay on the
+    device and are allreduced there (NCCL), so the step can run ahead of the host or inside a
+    CUDA graph. Bit-identical to the host-read path (the same float64 arithmetic)."""
+
+    first = allreduce_sums(weighted_sums(values, weights, 0.0), group)
+    second = allreduce_sums(weighted_sums_shifted(values, weights, first), group)
+    return normalize_from_sums_(values, first, second)
 
 
 def allreduce_head_entropy(observed: torch.Tensor, group=None) -> torch.Tensor:

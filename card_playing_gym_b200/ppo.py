@@ -69,6 +69,30 @@ def weighted_sums(values: torch.Tensor, weights: torch.Tensor, shift: float = 0.
     return out
 
 
+def weighted_sums_shifted(values: torch.Tensor, weights: torch.Tensor, shift_sums: torch.Tensor) -> torch.Tensor:
+    """The second pass with its shift (the mean of a first pass's sums) read on the device."""
+
+    values = values.to(torch.float64).contiguous()
+    weights = weights.to(torch.float64).contiguous()
+    n = values.numel()
+    out = torch.empty(3, dtype=torch.float64, device=values.device)
+    need = nat.query("cg_weighted_sums_workspace_bytes", n)
+    workspace = nat.Workspace.get(values.device, need, "reduce")
+    nat.call("cg_weighted_sums_shifted", nat.ptr(values), nat.ptr(weights), n, nat.ptr(shift_sums.contiguous()),
+             nat.ptr(out), nat.ptr(workspace), workspace.numel(), nat.stream_handle(values.device))
+    return out
+
+
+def normalize_from_sums_(values: torch.Tensor, first: torch.Tensor, second: torch.Tensor) -> torch.Tensor:
+    """normalize_ with mean and std computed on the device from both passes' sums (no host read)."""
+
+    if values.dtype != torch.float64 or not values.is_contiguous():
+        raise ValueError("normalize_from_sums_ works in place on a contiguous float64 tensor")
+    nat.call("cg_normalize_from_sums", nat.ptr(values), values.numel(), nat.ptr(first.contiguous()),
+             nat.ptr(second.contiguous()), nat.stream_handle(values.device))
+    return values
+
+
 def mean_std_from_sums(total: float, weighted: float, second: float | None = None) -> tuple[float, float]:
     """weighted_mean_std's arithmetic on reduced sums (ppo.py:147-153)."""
 

@@ -220,6 +220,15 @@ int cg_weighted_sums(const double* values, const double* weights, int64_t n, dou
 /* x <- (x - mean) / std in place. */
 int cg_normalize(double* values, int64_t n, double mean, double std, void* stream);
 
+/* Device-resident form of the same two passes (no host read between them; the sums may be
+ * allreduced on the device in between): the second pass takes its shift, the mean
+ * sum w x / sum w, from a first pass's sums shift_sums3 on the device; cg_normalize_from_sums
+ * takes mean and std = sqrt(max(second[2] / first[0], 1e-12)) from both passes' sums
+ * (mean 0, std 1 without weight), as ppo.py:147-153 computes them. */
+int cg_weighted_sums_shifted(const double* values, const double* weights, int64_t n, const double* shift_sums3,
+                             double* out3, void* workspace, int64_t workspace_bytes, void* stream);
+int cg_normalize_from_sums(double* values, int64_t n, const double* first3, const double* second3, void* stream);
+
 /* The fused per-head PPO objective (ppo.py:28-72 terms; trainer.py:774-797 objective):
  *   L = sum_i w_i * loss_i - alpha * sum_i w_i * eligible_i * normalized_entropy_i
  * logits/old_probs fp32 [rows, width] (row stride `stride`), actions int64, advantages and

@@ -188,6 +188,26 @@ def test_weighted_mean_std_and_normalize():
     assert weighted_mean_std(torch.zeros(4).cuda(), torch.zeros(4).cuda()) == (0.0, 1.0)
 
 
+def test_normalize_without_host_reads_is_bit_identical():
+    """The device-resident two passes (sums never read on the host) give the host path's values."""
+
+    from card_playing_gym_b200.data_parallel import normalize_global_
+    from card_playing_gym_b200.ppo import normalize_, weighted_mean_std
+
+    rng = np.random.default_rng(6)
+    values = rng.standard_normal(262_147) * 2.5 + 0.3
+    weights = rng.random(262_147)
+    x, w = torch.from_numpy(values).cuda(), torch.from_numpy(weights).cuda()
+    mean, std = weighted_mean_std(x, w)
+    expected = normalize_(x.clone(), mean, std)
+    got = normalize_global_(x.clone(), w)
+    assert torch.equal(got, expected)
+    # without weight: mean 0, std 1, values unchanged
+    zeros = torch.zeros(5, dtype=torch.float64, device="cuda")
+    same = torch.arange(5, dtype=torch.float64, device="cuda")
+    assert torch.equal(normalize_global_(same.clone(), zeros), same)
+
+
 def test_ppo_objective_matches_the_reference_autograd():
     from card_playing_gym_b200.ppo import TOTAL_KEYS, policy_objective, ppo_terms
 
