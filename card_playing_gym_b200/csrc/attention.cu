@@ -8,7 +8,7 @@
 // Two kernels:
 //  * attn_tc: fp16/bf16 caches, head_dim in {16, 24, 32, 40, 48, 64}, G*T <= 16. One
 //    warp per (row, KV head) unit, persistent over units. Each warp streams its units'
-//    keys in chunks of 64 through a two-stage shared-memory ring filled with 16-byte
+//    keys in chunks of 32 through a four-stage shared-memory ring filled with 16-byte
 //    cp.async copies (zero-filled past the row's length, L2 evict-first; a unit's query
 //    rows travel with its first chunk), computes Q K^T
 //    and P V with mma.sync m16n8k16/k8 (fp32 accumulation) and keeps an online softmax
@@ -98,8 +98,8 @@ __global__ void __launch_bounds__(128) attn_simt_kernel(AttnParams p) {
 // ------------------------------------------------------------------------------------
 // Tensor-core kernel.
 // ------------------------------------------------------------------------------------
-constexpr int kChunk = 64;   // keys per staged chunk
-constexpr int kStages = 2;   // chunk stages per warp: one computed while the next loads
+constexpr int kChunk = 32;   // keys per staged chunk
+constexpr int kStages = 4;   // chunk stages per warp: one computed while three load
 constexpr int kTcWarps = 4;  // warps per CTA
 
 __device__ __forceinline__ uint32_t smem_addr(const void* ptr) {
@@ -259,6 +259,9 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
   const int gid = lane >> 2, tid4 = lane & 3;
   KV* stage_base = reinterpret_cast<KV*>(smem_raw + wib * Shape::kWarpBytes);
   const uint64_t policy = evict_first_policy();
+  // Zeroed stages: a block past a chunk's zero-filled keys then only ever holds finite data.
+  for (int i = lane; i < Shape::kWarpBytes / 16; i += 32) reinterpret_cast<uint4*>(stage_base)[i] = make_uint4(0, 0, 0, 0);
+  __syncwarp();
   pdl_wait();  // q, K and V come from the kernel before
   pdl_trigger();
 
@@ -462,9 +465,10 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
 
     const int first = comp_chunk * kChunk;
     const int n = min(kChunk, cu.keys - first);
-    const int nblocks = (n + 15) >> 4;
-    // Every row sees every processed key of this chunk (a zero-filled tail block needs the mask).
-    const bool full = (n & 15) == 0 && first + n <= cu.len;
+    // Every 16-key block of the chunk is processed (no per-block branches); a chunk that is
+    // partial, or whose keys some row does not see yet, is masked, so keys past the unit's end
+    // (zero-filled, or finite data from an earlier chunk: the stages start zeroed) get p = 0.
+    const bool full = n == kChunk && first + n <= cu.len;
     // S = Q K^T over the chunk, 16 keys (two n8 tiles) per step; K fragments by ldmatrix.
     // Scores stay unscaled until the exponent: scale > 0 keeps the max where it is.
     float s[kChunk / 8][4];
@@ -473,7 +477,7 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
     for (int kk = 0; kk < kChunk / 16; ++kk) {
       kmax[kk][0] = kmax[kk][1] = -INFINITY;
       float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
-      if (kk < nblocks) {
+      {
         const KV* kbase = ks + (kk * 16 + (lane & 15)) * D;
 #pragma unroll
         for (int kb = 0; kb < Shape::kTiles; ++kb) {
@@ -494,7 +498,7 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
         s[2 * kk][e] = -INFINITY;
         s[2 * kk + 1][e] = -INFINITY;
       }
-      if (kk < nblocks) {
+      {
 #pragma unroll
         for (int e = 0; e < 2 * kRows; ++e) {
           const int r = e >> 1;
@@ -559,7 +563,7 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
     // O += P V, 16 keys at a time.
 #pragma unroll
     for (int kk = 0; kk < kChunk / 16; ++kk) {
-      if (kk < nblocks) {
+      {
         uint32_t pa[4];
         pa[0] = Ops::pack(s[2 * kk][0], s[2 * kk][1]);
         pa[1] = kHalf ? 0u : Ops::pack(s[2 * kk][2], s[2 * kk][3]);
