@@ -44,6 +44,7 @@ sys.path.insert(0, str(REPO))
 METRIC = "self-play decisions/sec (whole box, 1/2/4/8 B200); PPO-iteration wall time"
 UNIT = "decisions/s"
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS_SUSTAINED = 1400.0
 # DRAM bytes (read + write) per decode-attention launch divided by its algorithmic bytes,
 # from an ncu capture of the same kernel on the 2,048-game wave (profiles/
 # attn_tc_kernel_rlv6_decode.md: 219.12 MB read + 4.83 MB written against 219.24 MB
@@ -368,13 +369,13 @@ class ClockSampler:
         }
 
 
-def measured_peak() -> tuple[float, str]:
+def measured_peak(key: str = "hbm_gbs") -> tuple[float, str]:
     path = REPO / "MEASURED_PEAKS.json"
     try:
         peaks = json.loads(path.read_text())
-        return float(peaks["hbm_gbs"]), "measured"
+        return float(peaks[key]), "measured"
     except (OSError, KeyError, ValueError):
-        return FALLBACK_HBM_GBS, "fallback"
+        return {"hbm_gbs": FALLBACK_HBM_GBS, "bf16_tflops_sustained": FALLBACK_BF16_TFLOPS_SUSTAINED}[key], "fallback"
 
 
 # ---------------------------------------------------------------------------------------------
@@ -449,11 +450,14 @@ def run_b200(args) -> int:
     # while the one before drains, so the headline pass above runs without them.
     profiled_steps = min(args.steps, 100)
     nat.attention_profiling(True, capacity=profiled_steps * RL_V6.n_layers + 16)
+    nat.dense_profiling(True, capacity=profiled_steps * (RL_V6.n_layers + 1) + 16)
     for _ in range(profiled_steps):
         step()
     torch.cuda.synchronize(device)
     attention_ms = nat.attention_timings()
+    dense_ms = nat.dense_timings()
     nat.attention_profiling(False)
+    nat.dense_profiling(False)
     clock_info = clocks.stop() if clocks else None
     device_ms = max_over_ranks(device_ms)
     ms_per_step = device_ms / args.steps
@@ -520,6 +524,26 @@ def run_b200(args) -> int:
             },
             "gpu_launches": int(launches),
             "clocks": clock_info,
+        }
+        # Dense layers (tcgen05): the projections' FLOPs per wave over the summed dense-launch
+        # time per wave, against the measured sustained bf16 GEMM rate (timed inside a long step).
+        trunk = RL_V6.trunk()
+        d, f, qkv = trunk.d_model, trunk.d_ff, (trunk.n_heads + 2 * trunk.n_kv_heads) * trunk.head_dim
+        ple_w = trunk.n_layers * trunk.per_layer_dim
+        layer_flops = 2 * (d * d + 2 * d * f + d * qkv)
+        wave_flops = rows * 2 * (ple_w * d + qkv * d) + rows * (trunk.n_layers - 1) * layer_flops \
+            + rows * (layer_flops - 2 * d * qkv)
+        launches_per_wave = trunk.n_layers + 1
+        dense_wave_ms = statistics.fmean(dense_ms) * launches_per_wave if dense_ms else float("nan")
+        tflops = wave_flops / (dense_wave_ms / 1000.0) / 1e12
+        tpeak, tpeak_kind = measured_peak("bf16_tflops_sustained")
+        line["dense_layers"] = {
+            "kernel": "tc_dense_kernel (tcgen05, 2-SM pairs)", "bound": "tensor", "achieved": tflops, "peak": tpeak,
+            "unit": "TFLOP/s", "frac": tflops / tpeak,
+            "peak_source": f"{tpeak_kind} (MEASURED_PEAKS.json bf16_tflops_sustained)",
+            "flops_per_wave": wave_flops, "mean_launch_ms": statistics.fmean(dense_ms) if dense_ms else None,
+            "launches_timed": len(dense_ms),
+            "timing": "CUDA events around each dense launch in the same profiled pass as the attention roofline",
         }
         if ppo_line is not None:
             line["ppo"] = ppo_line

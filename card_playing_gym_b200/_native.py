@@ -67,6 +67,8 @@ _SIGNATURES: dict[str, tuple[type, list]] = {
     "cg_launch_count": (_i64, []),
     "cg_attention_profiling": (_i32, [_i32, _i32]),
     "cg_attention_timings": (_i32, [ctypes.POINTER(_f32), _i32]),
+    "cg_dense_profiling": (_i32, [_i32, _i32]),
+    "cg_dense_timings": (_i32, [ctypes.POINTER(_f32), _i32]),
     "cg_decode_attention": (_i32, [_p, _i32, _p, _p, _i32, _i64, _i64, _i64, _p, _p, _i64, _i32, _i32, _i32, _i32, _i32,
                                    _f32, _p, _i32, _p]),
     "cg_kv_write_step": (_i32, [_p, _p, _i32, _i64, _i32, _i32, _i32, _p, _p, _i64, _i32, _p, _p, _i32, _p]),
@@ -157,6 +159,18 @@ def attention_timings(max_count: int = 1 << 16) -> list[float]:
     count = lib().cg_attention_timings(buffer, max_count)
     if count < 0:
         raise NativeError("cg_attention_timings failed")
+    return [buffer[i] for i in range(count)]
+
+
+def dense_profiling(enable: bool, capacity: int = 4096) -> None:
+    call("cg_dense_profiling", 1 if enable else 0, capacity)
+
+
+def dense_timings(max_count: int = 1 << 16) -> list[float]:
+    buffer = (_f32 * max_count)()
+    count = lib().cg_dense_timings(buffer, max_count)
+    if count < 0:
+        raise NativeError("cg_dense_timings failed")
     return [buffer[i] for i in range(count)]
 
 

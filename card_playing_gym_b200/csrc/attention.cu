@@ -18,6 +18,7 @@
 //  * attn_simt: any cache dtype and shape; one warp per (row, query head, step),
 //    fp32 arithmetic. Used for fp32 caches (the strict-parity mode) and shapes the
 //    tensor-core kernel does not take.
+#include "launch_timer.cuh"
 #include "trunk.h"
 
 namespace cg {
@@ -694,46 +695,14 @@ bool tc_eligible(const AttnParams& p) {
 }
 
 namespace {
-struct AttentionProfile {
-  bool enabled = false;
-  int capacity = 0;
-  int count = 0;
-  cudaEvent_t* start = nullptr;
-  cudaEvent_t* stop = nullptr;
-} g_profile;
+LaunchTimer g_attention_timer;
 }  // namespace
 
 int profile_attention(int enable, int capacity) {
-  for (int i = 0; i < g_profile.capacity; ++i) {
-    cudaEventDestroy(g_profile.start[i]);
-    cudaEventDestroy(g_profile.stop[i]);
-  }
-  delete[] g_profile.start;
-  delete[] g_profile.stop;
-  g_profile = AttentionProfile{};
-  if (!enable) return CG_OK;
-  CG_REQUIRE(capacity > 0 && capacity <= (1 << 20), "cg_attention_profiling: capacity 1..2^20");
-  g_profile.start = new cudaEvent_t[capacity];
-  g_profile.stop = new cudaEvent_t[capacity];
-  for (int i = 0; i < capacity; ++i) {
-    if (cudaEventCreate(&g_profile.start[i]) != cudaSuccess || cudaEventCreate(&g_profile.stop[i]) != cudaSuccess) {
-      g_profile.capacity = i;
-      return set_error(CG_ERR_CUDA, "cg_attention_profiling: cudaEventCreate failed");
-    }
-    g_profile.capacity = i + 1;
-  }
-  g_profile.enabled = true;
-  return CG_OK;
+  return g_attention_timer.configure(enable, capacity, "cg_attention_profiling");
 }
 
-int attention_timings(float* ms_out, int max_count) {
-  if (cudaDeviceSynchronize() != cudaSuccess) return -1;
-  const int n = g_profile.count < max_count ? g_profile.count : max_count;
-  for (int i = 0; i < n; ++i) {
-    if (cudaEventElapsedTime(&ms_out[i], g_profile.start[i], g_profile.stop[i]) != cudaSuccess) return -1;
-  }
-  return n;
-}
+int attention_timings(float* ms_out, int max_count) { return g_attention_timer.timings(ms_out, max_count); }
 
 int run_attention_kernels(const AttnParams& p, cudaStream_t stream);
 
@@ -741,10 +710,9 @@ int run_attention(const AttnParams& p, cudaStream_t stream) {
   if (p.batch == 0) return CG_OK;
   if (p.out_blocked && (p.out_dtype != CG_BF16 || p.blocked_width != p.heads * p.head_dim || p.blocked_width % 8))
     return set_error(CG_ERR_ARGUMENT, "blocked attention output must be bf16 with width heads*head_dim (multiple of 8)");
-  const bool record = g_profile.enabled && g_profile.count < g_profile.capacity;
-  if (record) cudaEventRecord(g_profile.start[g_profile.count], stream);
+  const bool recorded = g_attention_timer.begin(stream);
   const int rc = run_attention_kernels(p, stream);
-  if (record) cudaEventRecord(g_profile.stop[g_profile.count++], stream);
+  g_attention_timer.end(stream, recorded);
   return rc;
 }
 

@@ -26,6 +26,7 @@
 // tile block = width/8 chunks of [128 rows x 8 columns].
 #include <cmath>
 
+#include "launch_timer.cuh"
 #include "tcgen05.cuh"
 #include "trunk.h"
 
@@ -35,7 +36,7 @@ constexpr int kTile = 128;
 constexpr int kTcThreads = 14 * 32;  // 12 epilogue warps + producer warp + MMA warp
 constexpr int kMaxOps = 16;
 constexpr int kMaxStages = 16;
-constexpr int kStageTarget = 32 * 1024;  // bytes per ring stage (one bulk copy)
+constexpr int kStageTarget = 30 * 1024;  // bytes per ring stage (one bulk copy): a whole 128-column up half
 constexpr int kSmemBudget = 222 * 1024;  // dynamic shared memory; the static barriers and reductions need the rest of 227 KB
 constexpr int kUpCols = 128;             // up-projection chunk: columns of d_ff per GELU hand-off
 constexpr int kAccCols = 256;            // TMEM: [0, 256) out/down/QKV accumulator, then two up buffers
@@ -117,11 +118,11 @@ __device__ __forceinline__ void store16(float* base, int64_t tile, int width, in
     *blk(base, tile, width, col + 4 * q, t) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
 }
 
-// 16 consecutive floats from a 16-byte aligned parameter vector.
+// 16 consecutive floats from a 16-byte aligned parameter vector (staged in shared memory).
 __device__ __forceinline__ void load16_vec(const float* src, float (&v)[16]) {
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
-    const float4 x = __ldg(reinterpret_cast<const float4*>(src) + q);
+    const float4 x = reinterpret_cast<const float4*>(src)[q];
     v[4 * q] = x.x;
     v[4 * q + 1] = x.y;
     v[4 * q + 2] = x.z;
@@ -338,9 +339,26 @@ __device__ void qkv_epilogue(const TcParams& p, const EpiThread& e, int64_t tile
 __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned char* h0, unsigned char* h1, uint32_t tmem,
                                uint64_t* a_ready_bar, uint32_t publish_to, uint64_t* acc_ready_bar, uint64_t* up_ready_bar,
                                uint64_t* h_free_bar, uint64_t* attn_full_bar, uint64_t* val_full_bar, int abytes,
-                               float (*red)[kTile]) {
+                               float (*red)[kTile], float* prm) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t tile = blockIdx.x;
+  // The layer's vectors, staged once in shared memory (constant parameters: loaded while the
+  // kernel before drains): [0,d) LN_mlp w (first kernel: input RMSNorm gain), [d,2d) LN_mlp b,
+  // [2d,3d) down bias, [3d,5d) the next LN (last layer: the final LN), [5d,5d+f) up bias.
+  {
+    const int dd = p.d;
+    for (int i = threadIdx.x; i < 5 * dd + p.f; i += kEpiThreads) {
+      const int which = i < 5 * dd ? i / dd : 5;
+      const float* src = which == 0   ? (p.mode == kLayer ? p.ln_mlp_w : p.rms_w)
+                         : which == 1 ? p.ln_mlp_b
+                         : which == 2 ? p.down_b
+                         : which == 3 ? (p.has_next ? p.ln_next_w : p.final_w)
+                         : which == 4 ? (p.has_next ? p.ln_next_b : p.final_b)
+                                      : p.up_b;
+      const int k = which < 5 ? i - which * dd : i - 5 * dd;
+      prm[i] = src ? src[k] : 0.f;
+    }
+  }
   pdl_wait();  // the epilogue reads and writes what earlier kernels of the stream touch
   pdl_trigger();
   EpiThread e;
@@ -387,23 +405,24 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
       tc::bar_expect_tx(attn_full_bar, abytes);
       tc::bulk_g2s(abuf, reinterpret_cast<const unsigned char*>(p.attn_blk) + tile * abytes, abytes, attn_full_bar);
     }
+    // The residual row goes into the accumulator columns of TMEM: the out-projection and
+    // every down-projection accumulate onto it, so x += out and x += down need no epilogue
+    // and the row never leaves TMEM inside the layer.
 #pragma unroll
-    for (int c = 0; c < kMaxRowChunks; ++c)  // the residual row, in registers until E3
-      if (lo + c < hi) load16(p.x_blk, tile, d, (lo + c) * 16, t, x[c]);
+    for (int c = 0; c < kMaxRowChunks; ++c)
+      if (lo + c < hi) {
+        load16(p.x_blk, tile, d, (lo + c) * 16, t, x[c]);
+        tc::tmem_st16(e.lane_tmem + (lo + c) * 16, x[c]);
+      }
+    tc::tmem_wait_st();
     if (!group_wait(attn_full_bar, 0, 0x404)) return;
     publish();
-    // E1: x += out_proj (written back: the MLP phase runs without the row in registers);
-    // LN_mlp(x) -> A.
+    // E1: LN_mlp(x + out_proj) -> A.
     if (!wait_acc()) return;
 #pragma unroll
-    for (int c = 0; c < kMaxRowChunks; ++c) {
-      if (lo + c >= hi) continue;
-      tc::tmem_ld16(e.lane_tmem + p.ops[0].tmem_col + (lo + c) * 16, v16);
-#pragma unroll
-      for (int i = 0; i < 16; ++i) x[c][i] += v16[i];
-      store16(p.x_blk, tile, d, (lo + c) * 16, t, x[c]);
-    }
-    layer_norm_regs(x, lo, hi, d, e, p.ln_mlp_w, p.ln_mlp_b, abuf, red);
+    for (int c = 0; c < kMaxRowChunks; ++c)
+      if (lo + c < hi) tc::tmem_ld16(e.lane_tmem + (lo + c) * 16, x[c]);
+    layer_norm_regs(x, lo, hi, d, e, prm, prm + d, abuf, red);
     publish();
     // E2: GELU of each up chunk into its H buffer. Chunk uc sits in TMEM buffer uc % 2; its
     // H buffer is free once down(uc - 2) has completed.
@@ -424,7 +443,7 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
       int plo, phi;
       part_chunks(width, e.qd, plo, phi);
       unsigned char* hb = buf ? h1 : h0;
-      const float* bias_base = p.up_b + uc * kUpCols;
+      const float* bias_base = prm + 5 * d + uc * kUpCols;
       const uint32_t ucol = kAccCols + buf * kUpCols;
       for (int c = plo; c < phi; c += 2) {
         const bool two = c + 1 < phi;
@@ -444,10 +463,8 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
       }
       publish();
     }
-    // E3: x += down + b; x += PLE(l); store; then LN_attn(l+1) -> A.
-    // The residual (this thread's own E1 stores), the PLE update and the bias do not
-    // depend on the GEMM: fold them into x while it runs. (Every x[c] is redefined here, so
-    // the row is dead in registers from E1's stores to this point.)
+    // E3: x (= x + out + down, in TMEM) + b + PLE(l); store; then LN_attn(l+1) -> A.
+    // The bias and the PLE update do not depend on the GEMM: gather them while it runs.
 #pragma unroll
     for (int c = 0; c < kMaxRowChunks; ++c) {
       if (lo + c >= hi) {
@@ -456,20 +473,16 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
         continue;
       }
       const int col = (lo + c) * 16;
-      load16(p.x_blk, tile, d, col, t, x[c]);
-      float bias[16];
-      load16_vec(p.down_b + col, bias);
-#pragma unroll
-      for (int i = 0; i < 16; ++i) x[c][i] += bias[i];
+      load16_vec(prm + 2 * d + col, x[c]);
       if (p.P) {
 #pragma unroll
         for (int i = 0; i < 16; i += 4) {
           const int k = (col + i) % p.P;  // P % 4 == 0: four columns share a float4
           const float4 ev = *blk(p.ple_blk, static_cast<int64_t>(p.layer) * p.ntiles + tile, p.P, k, t);
-          x[c][i] += ev.x * p.ple_scale;
-          x[c][i + 1] += ev.y * p.ple_scale;
-          x[c][i + 2] += ev.z * p.ple_scale;
-          x[c][i + 3] += ev.w * p.ple_scale;
+          x[c][i] = fmaf(ev.x, p.ple_scale, x[c][i]);
+          x[c][i + 1] = fmaf(ev.y, p.ple_scale, x[c][i + 1]);
+          x[c][i + 2] = fmaf(ev.z, p.ple_scale, x[c][i + 2]);
+          x[c][i + 3] = fmaf(ev.w, p.ple_scale, x[c][i + 3]);
         }
       }
     }
@@ -493,7 +506,7 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
       if (p.has_next) store16(p.x_blk, tile, d, col, t, x[c]);
     }
     if (p.has_next) {
-      layer_norm_regs(x, lo, hi, d, e, p.ln_next_w, p.ln_next_b, abuf, red);
+      layer_norm_regs(x, lo, hi, d, e, prm + 3 * d, prm + 4 * d, abuf, red);
       publish();
       if (val_smem && !group_wait(val_full_bar, 0, 0x405)) return;
       if (!wait_acc()) return;
@@ -503,7 +516,7 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
       const int64_t b = row / p.T;
       const int tt = static_cast<int>(row - b * p.T);
       const bool readout = valid && (p.T == 1 || tt == p.readout_offsets[b]);
-      layer_norm_regs(x, lo, hi, d, e, p.final_w, p.final_b, abuf, red, true, readout ? p.hidden_out + b * d : nullptr);
+      layer_norm_regs(x, lo, hi, d, e, prm + 3 * d, prm + 4 * d, abuf, red, true, readout ? p.hidden_out + b * d : nullptr);
     }
     return;
   }
@@ -589,7 +602,7 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
       *blk(p.val_blk, static_cast<int64_t>(k / p.kvw) * p.ntiles + tile, p.kvw, k % p.kvw, t) = ev;
     }
   }
-  layer_norm_regs(x, lo, hi, d, e, p.ln_next_w, p.ln_next_b, abuf, red);
+  layer_norm_regs(x, lo, hi, d, e, prm + 3 * d, prm + 4 * d, abuf, red);
   publish();
   if (!wait_acc()) return;
   qkv_epilogue(p, e, tile, nullptr);  // the value streams were written by this CTA just above
@@ -618,6 +631,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dense_kernel(const __grid_co
   unsigned char* h0 = smem + abytes;
   unsigned char* h1 = smem + abytes + p.hbytes;
   unsigned char* ring = smem + abytes + 2 * p.hbytes;
+  float* prm = reinterpret_cast<float*>(ring + p.stages * p.stage_bytes);  // 5d + f floats
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.stages; ++s) {
@@ -768,7 +782,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dense_kernel(const __grid_co
   } else {
     const uint32_t publish_to = kPair && rank == 1 ? tc::map_shared(tc::smem_u32(&a_ready), 0) : 0u;
     dense_epilogue(p, abuf, h0, h1, tmem, &a_ready, publish_to, &acc_ready, up_ready, h_free, &attn_full, &val_full,
-                   abytes, red);
+                   abytes, red, prm);
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -836,7 +850,7 @@ bool tc_layers_available(const cg_trunk_dims& dims) {
   const int64_t abytes = static_cast<int64_t>(kTile) * d * 2;
   const int64_t hbytes = static_cast<int64_t>(kTile) * (dims.d_ff < kUpCols ? dims.d_ff : kUpCols) * 2;
   const int64_t stage = 32LL * (q > 256 ? q : 256);
-  return abytes + 2 * hbytes + 2 * stage <= kSmemBudget;
+  return abytes + 2 * hbytes + 2 * stage + (5LL * d + dims.d_ff) * 4 <= kSmemBudget;
 }
 
 int tc_pack(const cg_trunk_dims& dims, void* blob, const BlobLayout& L, cudaStream_t s) {
@@ -928,14 +942,27 @@ int64_t tc_layers_scratch_bytes(const cg_trunk_dims& dims, int64_t batch, int st
   return plan_tc(dims, batch, steps, nullptr).total;
 }
 
+namespace {
+LaunchTimer g_dense_timer;
+}  // namespace
+
+int launch_dense_kernel(TcParams& p, cudaStream_t s);
+
 int launch_dense(TcParams& p, cudaStream_t s) {
+  const bool recorded = g_dense_timer.begin(s);
+  const int rc = launch_dense_kernel(p, s);
+  g_dense_timer.end(s, recorded);
+  return rc;
+}
+
+int launch_dense_kernel(TcParams& p, cudaStream_t s) {
   // Ring stages of up to 32 KB (several consecutive K-slices each); as many as fit.
   const int abytes = kTile * p.d * 2;
   const int split = kPairTiles ? 2 : 1;  // a pair's CTA holds half of each K-slice
   int max_slice = 0;
   for (int i = 0; i < p.n_ops; ++i) max_slice = p.ops[i].n / split * 32 > max_slice ? p.ops[i].n / split * 32 : max_slice;
   p.stage_bytes = max_slice > kStageTarget ? max_slice : kStageTarget;
-  const int fixed = abytes + 2 * p.hbytes;
+  const int fixed = abytes + 2 * p.hbytes + (5 * p.d + p.f) * 4;  // operands + staged layer vectors
   int stages = (kSmemBudget - fixed) / p.stage_bytes;
   if (stages < 2) {
     p.stage_bytes = max_slice;
@@ -948,6 +975,8 @@ int launch_dense(TcParams& p, cudaStream_t s) {
     p.ops[i].ks_per_stage = per < p.ops[i].ksteps ? per : p.ops[i].ksteps;
   }
   const int smem = fixed + p.stages * p.stage_bytes;
+  if ((abytes + 2 * p.hbytes + p.stages * p.stage_bytes) % 16)
+    return set_error(CG_ERR_ARGUMENT, "tensor-core dense layer: unaligned shared-memory layout");
   static int configured_smem[64] = {0};
   int device = 0;
   cudaGetDevice(&device);
@@ -1135,6 +1164,7 @@ int run_tc_forward(const cg_trunk_dims& dims, const void* blob, const BlobLayout
     out.n = d;
     out.ksteps = d / 16;
     out.tmem_col = 0;
+    out.accumulate_first = 1;  // onto the residual row the epilogue put in these columns
     out.wait_a = 1;
     out.signal = kSigAcc;
     p.ops[p.n_ops++] = out;
@@ -1159,7 +1189,7 @@ int run_tc_forward(const cg_trunk_dims& dims, const void* blob, const BlobLayout
       down.ksteps = up_width(dims, c) / 16;
       down.tmem_col = 0;
       down.a_src = 1 + (c & 1);
-      down.accumulate_first = c > 0;
+      down.accumulate_first = 1;  // onto x + out
       down.wait_a = 1;  // GELU(c) in H buffer c % 2
       down.signal = c == n_up - 1 ? kSigAcc : (c + 2 < n_up ? ((c & 1) ? kSigHFree1 : kSigHFree0) : kSigNone);
       p.ops[p.n_ops++] = down;
@@ -1181,3 +1211,9 @@ int tc_condition_ple(const cg_trunk_dims&, const void*, const BlobLayout&, const
 }
 
 }  // namespace cg
+
+extern "C" int cg_dense_profiling(int enable, int capacity) {
+  return cg::g_dense_timer.configure(enable, capacity, "cg_dense_profiling");
+}
+
+extern "C" int cg_dense_timings(float* ms_out, int max_count) { return cg::g_dense_timer.timings(ms_out, max_count); }

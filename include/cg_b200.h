@@ -53,6 +53,9 @@ int64_t cg_launch_count(void);
  * recorded launch durations in milliseconds; it returns how many it wrote (or -1). */
 int cg_attention_profiling(int enable, int capacity);
 int cg_attention_timings(float* ms_out, int max_count);
+/* The same for the tensor-core dense-layer launches of the bf16 decode step. */
+int cg_dense_profiling(int enable, int capacity);
+int cg_dense_timings(float* ms_out, int max_count);
 
 /* ---------------------------------------------------------------------------------
  * Decode attention straight from the KV pool.
