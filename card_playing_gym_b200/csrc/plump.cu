@@ -15,8 +15,11 @@ int forward_ragged_impl(const cg_trunk_dims* dims_p, const void* blob, const flo
                         const int64_t* readout_offsets, const int64_t* rows, int span, void* k_pool, void* v_pool,
                         int kv_dtype, int64_t capacity, int max_len, int precision, void* workspace,
                         int64_t workspace_bytes, float* hidden_out, cudaStream_t s, bool x_in_workspace,
-                        const float* lookup, int lookup_width);
+                        bool lookup_blocked);
 bool tc_layers_available(const cg_trunk_dims& dims);
+unsigned char* step_tc_scratch(const cg_trunk_dims& dims, int64_t batch, int steps, int precision, void* workspace);
+void tc_input_streams(const cg_trunk_dims& dims, int64_t batch, int steps, unsigned char* scratch, float** x_blk,
+                      float** ple_blk, float** val_blk, int64_t* ntiles);
 
 namespace {
 constexpr int64_t kAlign = 256;
@@ -123,10 +126,44 @@ struct EmbedIds {
   uint8_t n_main, n_hand;
 };
 
+// Destination of the lookup sums: row-major [n, width], or the trunk's tile-blocked streams
+// (x_blk non-null): columns [0, d) -> x_blk, [d, d + L*P) -> ple_blk (per layer), the rest ->
+// val_blk (per value layer), each [.. tile][width/4][128 rows][4].
+struct EmbedOut {
+  float* rows;
+  float* x_blk;
+  float* ple_blk;
+  float* val_blk;
+  int d, ple_w, P, kvw;
+  int64_t ntiles;
+};
+
+__device__ __forceinline__ void store_lookup(const EmbedOut& o, int width, int64_t token, int c4, const float4& v) {
+  if (!o.x_blk) {
+    reinterpret_cast<float4*>(o.rows + token * width)[c4] = v;
+    return;
+  }
+  const int64_t tile = token >> 7;
+  const int r = static_cast<int>(token & 127);
+  int k = 4 * c4;
+  float4* dst;
+  if (k < o.d) {
+    dst = reinterpret_cast<float4*>(o.x_blk) + ((tile * (o.d / 4) + k / 4) * 128 + r);
+  } else if ((k -= o.d) < o.ple_w) {
+    const int layer = k / o.P, q = k - layer * o.P;
+    dst = reinterpret_cast<float4*>(o.ple_blk) + (((layer * o.ntiles + tile) * (o.P / 4) + q / 4) * 128 + r);
+  } else {
+    k -= o.ple_w;
+    const int vl = k / o.kvw, q = k - vl * o.kvw;
+    dst = reinterpret_cast<float4*>(o.val_blk) + (((vl * o.ntiles + tile) * (o.kvw / 4) + q / 4) * 128 + r);
+  }
+  *dst = v;
+}
+
 template <int kSliceF4>  // float4 columns per slice = lanes per token
 __global__ void __launch_bounds__(kEmbedThreads, 1) plump_embed_sliced_kernel(
     cg_plump_schema sc, const float* __restrict__ table, int width, const void* __restrict__ tokens, int token_dtype,
-    int64_t n, int tokens_per_cta, float* __restrict__ out) {
+    int64_t n, int tokens_per_cta, EmbedOut out) {
   extern __shared__ __align__(16) unsigned char emb_smem[];
   const int total_rows = sc.field_rows + sc.pattern_rows;
   float4* slices = reinterpret_cast<float4*>(emb_smem);  // [2][total_rows][kSliceF4]
@@ -235,7 +272,7 @@ __global__ void __launch_bounds__(kEmbedThreads, 1) plump_embed_sliced_kernel(
         acc.z += hand.z;
         acc.w += hand.w;
       }
-      if (c < width4) reinterpret_cast<float4*>(out + (first + t) * width)[c] = acc;
+      if (c < width4) store_lookup(out, width, first + t, c, acc);
     }
     __syncthreads();  // every warp is done with this buffer before it is refilled
   }
@@ -251,7 +288,8 @@ int check_schema(const cg_plump_schema* sc) {
 }
 
 int embed(const cg_plump_schema& sc, const float* table, int width, const void* tokens, int token_dtype, int64_t n,
-          float* out, cudaStream_t s) {
+          const EmbedOut& dest, cudaStream_t s) {
+  float* out = dest.rows;
   if (n == 0) return CG_OK;
   const int total_rows = sc.field_rows + sc.pattern_rows;
   // Widest slice whose two buffers fit next to the ids: 16 float4 (64 columns) for plump.
@@ -260,6 +298,7 @@ int embed(const cg_plump_schema& sc, const float* table, int width, const void* 
   const bool sliced = (width % 4) == 0 && 2LL * total_rows * slice_f4 * 16 <= 200 * 1024 &&
                       (reinterpret_cast<uintptr_t>(table) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
                       sc.hand_slots * 2 <= 32 && sc.field_count <= 16;
+  if (dest.x_blk && !sliced) return set_error(CG_ERR_ARGUMENT, "blocked field-lookup output needs the sliced kernel");
   if (!sliced) {
     const int64_t blocks = (n + 7) / 8;
     plump_embed_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(sc, table, width, tokens, token_dtype, n, out);
@@ -279,7 +318,7 @@ int embed(const cg_plump_schema& sc, const float* table, int width, const void* 
       configured[device & 63] = smem;
     }
     return launch_pdl("plump_embed_sliced_kernel", kernel, dim3(static_cast<unsigned>(blocks)), dim3(kEmbedThreads),
-                      smem, s, sc, table, width, tokens, token_dtype, n, static_cast<int>(per), out);
+                      smem, s, sc, table, width, tokens, token_dtype, n, static_cast<int>(per), dest);
   };
   if (slice_f4 == 16) return launch(plump_embed_sliced_kernel<16>);
   if (slice_f4 == 8) return launch(plump_embed_sliced_kernel<8>);
@@ -326,7 +365,9 @@ extern "C" int cg_plump_embed(const cg_plump_schema* schema, const float* table,
   CG_REQUIRE(width > 0, "bad width");
   if (n_tokens == 0) return CG_OK;
   CG_REQUIRE(table && tokens && out, "cg_plump_embed: NULL pointer");
-  return embed(*schema, table, width, tokens, token_dtype, n_tokens, out, static_cast<cudaStream_t>(stream));
+  EmbedOut dest{};
+  dest.rows = out;
+  return embed(*schema, table, width, tokens, token_dtype, n_tokens, dest, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int64_t cg_plump_step_workspace_bytes(const cg_trunk_dims* dims, int64_t batch, int steps, int precision) {
@@ -356,17 +397,30 @@ extern "C" int cg_plump_forward_ragged(const cg_trunk_dims* dims, const void* bl
   const int ple_w = dims->n_layers * dims->per_layer_dim;
   const int val_w = value_layer_count(*dims) * dims->n_kv_heads * head_dim(*dims);
   const int width = dims->d_model + ple_w + val_w;
-  if ((rc = embed(*schema, table, width, tokens, token_dtype, nt, w.lookup, s))) return rc;
-  if (precision == CG_PREC_BF16 && tc_layers_available(*dims)) {
-    // The tensor-core path conditions the raw lookup inside its first kernel.
+  const int total_rows = schema->field_rows + schema->pattern_rows;
+  if (precision == CG_PREC_BF16 && tc_layers_available(*dims) && 2LL * total_rows * 4 * 16 <= 200 * 1024 &&
+      schema->hand_slots * 2 <= 32 && (reinterpret_cast<uintptr_t>(table) & 15) == 0) {
+    // Tensor-core path: the lookup writes its raw streams straight into the first dense
+    // kernel's blocked inputs (x, per-layer PLE, value streams), which conditions them.
+    EmbedOut dest{};
+    dest.d = dims->d_model;
+    dest.ple_w = ple_w;
+    dest.P = dims->per_layer_dim;
+    dest.kvw = dims->n_kv_heads * head_dim(*dims);
+    tc_input_streams(*dims, batch, steps, step_tc_scratch(*dims, batch, steps, precision, w.step), &dest.x_blk,
+                     &dest.ple_blk, &dest.val_blk, &dest.ntiles);
+    if ((rc = embed(*schema, table, width, tokens, token_dtype, nt, dest, s))) return rc;
     return forward_ragged_impl(dims, blob, nullptr, nullptr, nullptr, batch, steps, positions, readout_offsets, rows,
                                span, k_pool, v_pool, kv_dtype, capacity, max_len, precision, w.step, w.step_bytes,
-                               hidden_out, s, false, w.lookup, width);
+                               hidden_out, s, false, true);
   }
+  EmbedOut rows_out{};
+  rows_out.rows = w.lookup;
+  if ((rc = embed(*schema, table, width, tokens, token_dtype, nt, rows_out, s))) return rc;
   // The residual stream x is the first buffer of the step workspace.
   float* x = reinterpret_cast<float*>(w.step);
   if ((rc = cg_trunk_condition(dims, blob, w.lookup, nt, x, w.ple, w.values, precision, s))) return rc;
   return forward_ragged_impl(dims, blob, x, w.ple, w.values, batch, steps, positions, readout_offsets, rows, span,
                              k_pool, v_pool, kv_dtype, capacity, max_len, precision, w.step, w.step_bytes, hidden_out, s,
-                             true, nullptr, 0);
+                             true, false);
 }

@@ -11,11 +11,13 @@ namespace cg {
 
 int run_tc_forward(const cg_trunk_dims& dims, const void* blob, const BlobLayout& L, int64_t batch, int steps,
                    const int64_t* positions, const int64_t* key_lengths, const int64_t* rows, int span, void* k_pool,
-                   void* v_pool, int kv_dtype, int64_t capacity, int max_len, const float* lookup, int lookup_width,
+                   void* v_pool, int kv_dtype, int64_t capacity, int max_len, bool lookup_blocked,
                    const float* x_in, const float* ple_in, const float* val_in, unsigned char* scratch,
                    int64_t scratch_bytes, const int64_t* readout_offsets, float* hidden_out, int* attn_counters,
                    cudaStream_t s);
 int64_t tc_layers_scratch_bytes(const cg_trunk_dims& dims, int64_t batch, int steps);
+void tc_input_streams(const cg_trunk_dims& dims, int64_t batch, int steps, unsigned char* scratch, float** x_blk,
+                      float** ple_blk, float** val_blk, int64_t* ntiles);
 bool tc_layers_available(const cg_trunk_dims& dims);
 int tc_pack(const cg_trunk_dims& dims, void* blob, const BlobLayout& L, cudaStream_t stream);
 int64_t tc_pack_bytes_ple(const cg_trunk_dims& dims);
@@ -290,6 +292,11 @@ StepWorkspace plan_step(const cg_trunk_dims& dims, int64_t batch, int steps, int
   return w;
 }
 
+// The tensor-core scratch inside a step workspace (null when the step takes the CUDA-core path).
+unsigned char* step_tc_scratch(const cg_trunk_dims& dims, int64_t batch, int steps, int precision, void* workspace) {
+  return plan_step(dims, batch, steps, precision, static_cast<unsigned char*>(workspace)).tc;
+}
+
 int check_dims(const cg_trunk_dims* dims) {
   CG_REQUIRE(dims, "NULL trunk dims");
   CG_REQUIRE(dims->d_model > 0 && dims->n_layers > 0 && dims->n_heads > 0 && dims->n_kv_heads > 0 && dims->d_ff > 0,
@@ -377,14 +384,15 @@ int run_fp32_layers(const cg_trunk_dims& dims, const void* blob, const BlobLayou
 }
 
 // The layer loop from either conditioned inputs (x_in, ple, values) or, on the tensor-core
-// path, the raw field lookup (lookup != nullptr: conditioning runs inside the first kernel).
+// path, the raw field lookup already written into the step's scratch in blocked layout by the
+// lookup kernel (lookup_blocked: conditioning runs inside the first kernel).
 // x_in_workspace: x_in already is the step workspace's residual buffer (fp32 path only).
 int forward_ragged_impl(const cg_trunk_dims* dims_p, const void* blob, const float* x_in, const float* ple,
                         const float* values, int64_t batch, int steps, const int64_t* positions,
                         const int64_t* readout_offsets, const int64_t* rows, int span, void* k_pool, void* v_pool,
                         int kv_dtype, int64_t capacity, int max_len, int precision, void* workspace,
                         int64_t workspace_bytes, float* hidden_out, cudaStream_t s, bool x_in_workspace,
-                        const float* lookup, int lookup_width) {
+                        bool lookup_blocked) {
   int rc;
   if ((rc = check_dims(dims_p))) return rc;
   const cg_trunk_dims& dims = *dims_p;
@@ -394,8 +402,8 @@ int forward_ragged_impl(const cg_trunk_dims* dims_p, const void* blob, const flo
   CG_REQUIRE(max_len > 0 && capacity > 0, "bad pool shape");
   if (batch == 0) return CG_OK;
   CG_REQUIRE(blob && positions && readout_offsets && k_pool && v_pool && hidden_out && workspace, "NULL pointer");
-  CG_REQUIRE(lookup || !dims.per_layer_dim || ple, "this trunk expects a per-layer embedding lookup");
-  CG_REQUIRE(lookup || !dims.value_layers || values, "this trunk expects a value-embedding lookup");
+  CG_REQUIRE(lookup_blocked || !dims.per_layer_dim || ple, "this trunk expects a per-layer embedding lookup");
+  CG_REQUIRE(lookup_blocked || !dims.value_layers || values, "this trunk expects a value-embedding lookup");
   if (span > max_len) span = max_len;
   StepWorkspace w = plan_step(dims, batch, steps, precision, static_cast<unsigned char*>(workspace));
   if (workspace_bytes < w.total)
@@ -408,10 +416,10 @@ int forward_ragged_impl(const cg_trunk_dims* dims_p, const void* blob, const flo
   if ((rc = check_launch("key_lengths_kernel"))) return rc;
   if (precision == CG_PREC_BF16 && tc_layers_available(dims)) {
     return run_tc_forward(dims, blob, L, batch, steps, positions, w.key_lengths, rows, span, k_pool, v_pool, kv_dtype,
-                          capacity, max_len, lookup, lookup_width, x_in, ple, values, w.tc, w.tc_bytes,
+                          capacity, max_len, lookup_blocked, x_in, ple, values, w.tc, w.tc_bytes,
                           readout_offsets, hidden_out, w.attn_counters, s);
   }
-  CG_REQUIRE(!lookup, "internal: the CUDA-core path takes conditioned inputs");
+  CG_REQUIRE(!lookup_blocked, "internal: the CUDA-core path takes conditioned inputs");
   if (!x_in_workspace) {
     cudaError_t err = cudaMemcpyAsync(w.x, x_in, nt * dims.d_model * sizeof(float), cudaMemcpyDeviceToDevice, s);
     if (err != cudaSuccess) return set_error(CG_ERR_CUDA, "copy x: %s", cudaGetErrorString(err));
@@ -468,7 +476,7 @@ extern "C" int cg_trunk_forward_ragged(const cg_trunk_dims* dims, const void* bl
   if (batch > 0 && !x) return cg::set_error(CG_ERR_ARGUMENT, "cg_trunk_forward_ragged: NULL x");
   return cg::forward_ragged_impl(dims, blob, x, ple, values, batch, steps, positions, readout_offsets, rows, span,
                                  k_pool, v_pool, kv_dtype, capacity, max_len, precision, workspace, workspace_bytes,
-                                 hidden_out, static_cast<cudaStream_t>(stream), false, nullptr, 0);
+                                 hidden_out, static_cast<cudaStream_t>(stream), false, false);
 }
 
 extern "C" int cg_trunk_condition(const cg_trunk_dims* dims_p, const void* blob, const float* lookup, int64_t n,

@@ -43,7 +43,7 @@ constexpr int kAccCols = 256;            // TMEM: [0, 256) out/down/QKV accumula
 // GEMM completion signals (tcgen05.commit targets).
 enum Signal { kSigNone = 0, kSigAcc = 1, kSigUp0 = 2, kSigUp1 = 3, kSigHFree0 = 4, kSigHFree1 = 5 };
 
-enum TcMode { kLayer = 0, kFirstLookup = 1, kFirstConditioned = 2 };
+enum TcMode { kLayer = 0, kFirstBlocked = 1, kFirstConditioned = 2 };
 
 struct GemmOp {
   const __nv_bfloat16* w;  // packed K-slices: ksteps x [n rows x 16 columns]
@@ -70,8 +70,6 @@ struct TcParams {
   const __nv_bfloat16* attn_blk;
   void* q;
   int q_dtype;
-  const float* lookup;  // kFirstLookup: raw lookup rows [nt, lookup_width]
-  int lookup_width;
   const float* x_in;  // kFirstConditioned inputs
   const float* ple_in;
   const float* val_in;
@@ -525,21 +523,14 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
   const int ple_w = p.L * p.P;
   const int val_w = p.nv * p.kvw;
   const int64_t r = valid ? row : 0;
-  if (p.mode == kFirstLookup) {
-    const float* src = p.lookup + r * p.lookup_width;
-    // x = RMSNorm(lookup[:, :d]) * gain (trunk.py:297-298, 104-115)
+  if (p.mode == kFirstBlocked) {
+    // The field-lookup kernel wrote the raw streams in blocked layout: x into x_blk, the PLE
+    // lookup into ple_blk, the value lookup into val_blk (already final).
+    // x = RMSNorm(lookup x) * gain (trunk.py:297-298, 104-115) -> x_blk and the A operand;
+    // LN_attn(0)(x) -> H buffer 0, the QKV GEMM's operand.
 #pragma unroll
-    for (int c = 0; c < kMaxRowChunks; ++c) {
-      if (lo + c >= hi) continue;
-#pragma unroll
-      for (int i = 0; i < 16; i += 4) {
-        const float4 ev = *reinterpret_cast<const float4*>(src + (lo + c) * 16 + i);
-        x[c][i] = ev.x;
-        x[c][i + 1] = ev.y;
-        x[c][i + 2] = ev.z;
-        x[c][i + 3] = ev.w;
-      }
-    }
+    for (int c = 0; c < kMaxRowChunks; ++c)
+      if (lo + c < hi) load16(p.x_blk, tile, d, (lo + c) * 16, t, x[c]);
     float ss = 0.f;
 #pragma unroll
     for (int c = 0; c < kMaxRowChunks; ++c)
@@ -551,40 +542,68 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
     for (int c = 0; c < kMaxRowChunks; ++c) {
       if (lo + c >= hi) continue;
       const int col = (lo + c) * 16;
+      float gain[16];
+      load16_vec(prm + col, gain);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) x[c][i] = x[c][i] * inv * p.rms_w[col + i];
+      for (int i = 0; i < 16; ++i) x[c][i] = x[c][i] * inv * gain[i];
       store16(p.x_blk, tile, d, col, t, x[c]);
       store_operand16(abuf, col, t, x[c]);
     }
-    for (int k = e.qd * 4; k < val_w; k += 4 * kParts) {
-      const float4 ev = *reinterpret_cast<const float4*>(src + d + ple_w + k);
-      *blk(p.val_blk, static_cast<int64_t>(k / p.kvw) * p.ntiles + tile, p.kvw, k % p.kvw, t) = ev;
-    }
-    if (p.n_ple_ops > 0) publish();
-    // ple = (lookup + W_c x) / sqrt(2), one TMEM chunk of up to 256 columns at a time.
+    layer_norm_regs(x, lo, hi, d, e, prm + 3 * d, prm + 4 * d, h0, red);
+    // ple = (lookup + W_c x) / sqrt(2): each 256-column GEMM accumulates onto the raw PLE
+    // lookup preloaded into its TMEM buffer (ops alternate between two buffers).
     const float inv_sqrt2 = 0.70710678118654752f;
-    int c0 = 0;
-    for (int o = 0; o < p.n_ple_ops; ++o) {
-      const int n = p.ops[o].n;
+    const int n_ple = p.n_ple_ops;
+    auto ple_float4 = [&](int k) {  // the blocked float4 holding PLE column k (k % 4 == 0) of row t
+      const int layer = k / p.P, kk = k - layer * p.P;
+      return blk(p.ple_blk, static_cast<int64_t>(layer) * p.ntiles + tile, p.P, kk, t);
+    };
+    auto preload = [&](int o) {
       int plo, phi;
-      part_chunks(n, e.qd, plo, phi);
-      if (!wait_acc()) return;
+      part_chunks(p.ops[o].n, e.qd, plo, phi);
       for (int c = plo; c < phi; ++c) {
-        tc::tmem_ld16(e.lane_tmem + c * 16, v16);
 #pragma unroll
         for (int i = 0; i < 16; i += 4) {
-          const int k = c0 + c * 16 + i;
-          const float4 ev = *reinterpret_cast<const float4*>(src + d + k);
-          const int layer = k / p.P, kk = k % p.P;
-          *blk(p.ple_blk, static_cast<int64_t>(layer) * p.ntiles + tile, p.P, kk, t) =
-              make_float4((ev.x + v16[i]) * inv_sqrt2, (ev.y + v16[i + 1]) * inv_sqrt2,
-                          (ev.z + v16[i + 2]) * inv_sqrt2, (ev.w + v16[i + 3]) * inv_sqrt2);
+          const float4 ev = *ple_float4(o * kAccCols + c * 16 + i);
+          v16[i] = ev.x;
+          v16[i + 1] = ev.y;
+          v16[i + 2] = ev.z;
+          v16[i + 3] = ev.w;
         }
+        tc::tmem_st16(e.lane_tmem + (o & 1) * kAccCols + c * 16, v16);
       }
-      c0 += n;
-      if (o + 1 < p.n_ple_ops) publish();
+    };
+    if (n_ple > 0) preload(0);
+    if (n_ple > 1) preload(1);
+    tc::tmem_wait_st();
+    publish();
+    uint32_t buf_phase[2] = {0u, 0u};
+    for (int o = 0; o < n_ple; ++o) {
+      const int buf = o & 1;
+      if (!group_wait(&up_ready_bar[buf], buf_phase[buf], 0x406)) return;
+      buf_phase[buf] ^= 1u;
+      tc::fence_after_sync();
+      int plo, phi;
+      part_chunks(p.ops[o].n, e.qd, plo, phi);
+      for (int c = plo; c < phi; ++c) {
+        tc::tmem_ld16(e.lane_tmem + buf * kAccCols + c * 16, v16);
+#pragma unroll
+        for (int i = 0; i < 16; i += 4)
+          *ple_float4(o * kAccCols + c * 16 + i) = make_float4(v16[i] * inv_sqrt2, v16[i + 1] * inv_sqrt2,
+                                                               v16[i + 2] * inv_sqrt2, v16[i + 3] * inv_sqrt2);
+      }
+      if (o + 2 < n_ple) {
+        preload(o + 2);
+        tc::tmem_wait_st();
+        publish();
+      }
     }
-  } else {
+    if (n_ple > 0) publish();  // every PLE buffer is read: the QKV GEMM may overwrite them
+    if (!wait_acc()) return;
+    qkv_epilogue(p, e, tile, nullptr);  // the value streams came from the field lookup
+    return;
+  }
+  {
 #pragma unroll
     for (int c = 0; c < kMaxRowChunks; ++c) {
       if (lo + c >= hi) continue;
@@ -938,6 +957,16 @@ TcScratch plan_tc(const cg_trunk_dims& dims, int64_t batch, int steps, unsigned 
   return s;
 }
 
+// Where the field lookup writes its blocked raw streams for the first dense kernel.
+void tc_input_streams(const cg_trunk_dims& dims, int64_t batch, int steps, unsigned char* scratch, float** x_blk,
+                      float** ple_blk, float** val_blk, int64_t* ntiles) {
+  const TcScratch w = plan_tc(dims, batch, steps, scratch);
+  *x_blk = w.x_blk;
+  *ple_blk = w.ple_blk;
+  *val_blk = w.val_blk;
+  *ntiles = padded_tiles(batch * steps);
+}
+
 int64_t tc_layers_scratch_bytes(const cg_trunk_dims& dims, int64_t batch, int steps) {
   return plan_tc(dims, batch, steps, nullptr).total;
 }
@@ -1008,7 +1037,7 @@ int launch_dense_kernel(TcParams& p, cudaStream_t s) {
 
 int run_tc_forward(const cg_trunk_dims& dims, const void* blob, const BlobLayout& L, int64_t batch, int steps,
                    const int64_t* positions, const int64_t* key_lengths, const int64_t* rows, int span, void* k_pool,
-                   void* v_pool, int kv_dtype, int64_t capacity, int max_len, const float* lookup, int lookup_width,
+                   void* v_pool, int kv_dtype, int64_t capacity, int max_len, bool lookup_blocked,
                    const float* x_in, const float* ple_in, const float* val_in, unsigned char* scratch,
                    int64_t scratch_bytes, const int64_t* readout_offsets, float* hidden_out, int* attn_counters,
                    cudaStream_t s) {
@@ -1090,20 +1119,22 @@ int run_tc_forward(const cg_trunk_dims& dims, const void* blob, const BlobLayout
   // First kernel: conditioning (or the given conditioned streams) + layer 0's QKV.
   int rc;
   p.n_ops = 0;
-  if (lookup) {
-    p.mode = kFirstLookup;
-    p.lookup = lookup;
-    p.lookup_width = lookup_width;
+  if (lookup_blocked) {
+    // The field lookup wrote the raw streams into this scratch in blocked layout; the PLE
+    // context GEMMs (256 columns each) accumulate onto the raw PLE lookup the epilogue
+    // preloads into alternating TMEM buffers.
+    p.mode = kFirstBlocked;
     p.rms_w = part(blob, L, CG_PART_INPUT_NORM, 0);
     const int ple_w = dims.n_layers * dims.per_layer_dim;
-    for (int c0 = 0; c0 < ple_w; c0 += 256) {
+    for (int c0 = 0, o = 0; c0 < ple_w; c0 += kAccCols, ++o) {
       GemmOp op{};
       op.w = blob_ptr<__nv_bfloat16>(blob, L.bf16_ple_context) + static_cast<int64_t>(c0) * d;
-      op.n = ple_w - c0 < 256 ? ple_w - c0 : 256;
+      op.n = ple_w - c0 < kAccCols ? ple_w - c0 : kAccCols;
       op.ksteps = d / 16;
-      op.tmem_col = 0;
-      op.wait_a = 1;
-      op.signal = kSigAcc;
+      op.tmem_col = (o & 1) * kAccCols;
+      op.accumulate_first = 1;
+      op.wait_a = o != 1;  // op 0: the operands; op o >= 2: buffer o % 2 consumed and reloaded
+      op.signal = (o & 1) ? kSigUp1 : kSigUp0;
       p.ops[p.n_ops++] = op;
     }
   } else {
@@ -1114,6 +1145,8 @@ int run_tc_forward(const cg_trunk_dims& dims, const void* blob, const BlobLayout
   }
   p.n_ple_ops = p.n_ops;
   push_qkv(0);
+  if (lookup_blocked)
+    for (int o = p.n_ple_ops; o < p.n_ops; ++o) p.ops[o].a_src = 1;  // LN_attn(0)(x) sits in H buffer 0
   set_qkv_target(0);
   p.layer = 0;
   p.has_next = 1;
