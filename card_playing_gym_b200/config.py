@@ -105,6 +105,9 @@ class PlumpModelConfig:
 
 
 RL_V6 = PlumpModelConfig()
+# The piquet-scale trunk's dimensions (d 256, 16 layers, 8 query / 2 KV heads of 32, d_ff 512)
+# with the plump field lookup and heads standing in for piquet's card grid and scorers.
+PIQUET_SCALE = PlumpModelConfig(d_model=256, n_layers=16, n_heads=8, n_kv_heads=2, d_ff=512, per_layer_dim=64)
 # configs/plump/smoke.toml [model]
 SMOKE = PlumpModelConfig(d_model=32, n_layers=2, n_heads=4, n_kv_heads=2, d_ff=64, per_layer_dim=8)
 

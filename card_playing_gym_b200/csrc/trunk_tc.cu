@@ -172,7 +172,7 @@ __device__ __forceinline__ float gelu_bf16_operand(float x) {
 constexpr int kParts = 3;
 constexpr int kEpiWarps = 4 * kParts;
 constexpr int kEpiThreads = kEpiWarps * 32;
-constexpr int kMaxRowChunks = 5;  // 16-column chunks of a d <= 240 row held per thread
+constexpr int kMaxRowChunks = 6;  // 16-column chunks of a d <= 288 row held per thread (5 up to d = 240)
 constexpr int kProducerWarp = kEpiWarps;
 constexpr int kMmaWarp = kEpiWarps + 1;
 
@@ -207,19 +207,20 @@ __device__ __forceinline__ float row_sum(float value, const EpiThread& e, float 
 // registers (this thread's chunks lo..hi-1 of d), written as bf16 into the operand buffer,
 // or, with to_row, as fp32 into out_row (a row-major d-wide row; skipped when null). Every
 // epilogue thread takes part (the row statistics go through named barriers).
-__device__ void layer_norm_regs(const float (&x)[kMaxRowChunks][16], int lo, int hi, int d, const EpiThread& e,
+template <int kRC>
+__device__ void layer_norm_regs(const float (&x)[kRC][16], int lo, int hi, int d, const EpiThread& e,
                                 const float* w, const float* b, unsigned char* abuf, float (*red)[kTile],
                                 bool to_row = false, float* out_row = nullptr) {
   float part = 0.f;
 #pragma unroll
-  for (int c = 0; c < kMaxRowChunks; ++c)
+  for (int c = 0; c < kRC; ++c)
     if (lo + c < hi)
 #pragma unroll
       for (int i = 0; i < 16; ++i) part += x[c][i];
   const float mean = row_sum(part, e, red) / d;
   float sq = 0.f;
 #pragma unroll
-  for (int c = 0; c < kMaxRowChunks; ++c)
+  for (int c = 0; c < kRC; ++c)
     if (lo + c < hi)
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
@@ -228,7 +229,7 @@ __device__ void layer_norm_regs(const float (&x)[kMaxRowChunks][16], int lo, int
       }
   const float rstd = rsqrtf(row_sum(sq, e, red + kParts) / d + 1e-5f);
 #pragma unroll
-  for (int c = 0; c < kMaxRowChunks; ++c) {
+  for (int c = 0; c < kRC; ++c) {
     if (lo + c >= hi) continue;
     const int col = (lo + c) * 16;
     float wv[16], bv[16];
@@ -334,6 +335,7 @@ __device__ void qkv_epilogue(const TcParams& p, const EpiThread& e, int64_t tile
 }
 
 // ---- epilogue warps ----------------------------------------------------------------------------------------
+template <int kRC>
 __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned char* h0, unsigned char* h1, uint32_t tmem,
                                uint64_t* a_ready_bar, uint32_t publish_to, uint64_t* acc_ready_bar, uint64_t* up_ready_bar,
                                uint64_t* h_free_bar, uint64_t* attn_full_bar, uint64_t* val_full_bar, int abytes,
@@ -370,7 +372,7 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
   int lo, hi;  // this thread's 16-column chunks of a d-wide row
   part_chunks(d, e.qd, lo, hi);
   uint32_t acc_phase = 0;
-  float x[kMaxRowChunks][16];
+  float x[kRC][16];
   float v16[16];
   // One thread waits on each mbarrier and arrives for the group; the others park on a
   // hardware named barrier instead of polling shared memory.
@@ -407,7 +409,7 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
     // every down-projection accumulate onto it, so x += out and x += down need no epilogue
     // and the row never leaves TMEM inside the layer.
 #pragma unroll
-    for (int c = 0; c < kMaxRowChunks; ++c)
+    for (int c = 0; c < kRC; ++c)
       if (lo + c < hi) {
         load16(p.x_blk, tile, d, (lo + c) * 16, t, x[c]);
         tc::tmem_st16(e.lane_tmem + (lo + c) * 16, x[c]);
@@ -418,7 +420,7 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
     // E1: LN_mlp(x + out_proj) -> A.
     if (!wait_acc()) return;
 #pragma unroll
-    for (int c = 0; c < kMaxRowChunks; ++c)
+    for (int c = 0; c < kRC; ++c)
       if (lo + c < hi) tc::tmem_ld16(e.lane_tmem + (lo + c) * 16, x[c]);
     layer_norm_regs(x, lo, hi, d, e, prm, prm + d, abuf, red);
     publish();
@@ -464,7 +466,7 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
     // E3: x (= x + out + down, in TMEM) + b + PLE(l); store; then LN_attn(l+1) -> A.
     // The bias and the PLE update do not depend on the GEMM: gather them while it runs.
 #pragma unroll
-    for (int c = 0; c < kMaxRowChunks; ++c) {
+    for (int c = 0; c < kRC; ++c) {
       if (lo + c >= hi) {
 #pragma unroll
         for (int i = 0; i < 16; ++i) x[c][i] = 0.f;
@@ -495,7 +497,7 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
                    vbytes, val_full_bar);
     }
 #pragma unroll
-    for (int c = 0; c < kMaxRowChunks; ++c) {
+    for (int c = 0; c < kRC; ++c) {
       if (lo + c >= hi) continue;
       const int col = (lo + c) * 16;
       tc::tmem_ld16(e.lane_tmem + col, v16);
@@ -529,17 +531,17 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
     // x = RMSNorm(lookup x) * gain (trunk.py:297-298, 104-115) -> x_blk and the A operand;
     // LN_attn(0)(x) -> H buffer 0, the QKV GEMM's operand.
 #pragma unroll
-    for (int c = 0; c < kMaxRowChunks; ++c)
+    for (int c = 0; c < kRC; ++c)
       if (lo + c < hi) load16(p.x_blk, tile, d, (lo + c) * 16, t, x[c]);
     float ss = 0.f;
 #pragma unroll
-    for (int c = 0; c < kMaxRowChunks; ++c)
+    for (int c = 0; c < kRC; ++c)
       if (lo + c < hi)
 #pragma unroll
         for (int i = 0; i < 16; ++i) ss += x[c][i] * x[c][i];
     const float inv = rsqrtf(row_sum(ss, e, red) / d + 1e-5f);
 #pragma unroll
-    for (int c = 0; c < kMaxRowChunks; ++c) {
+    for (int c = 0; c < kRC; ++c) {
       if (lo + c >= hi) continue;
       const int col = (lo + c) * 16;
       float gain[16];
@@ -605,7 +607,7 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
   }
   {
 #pragma unroll
-    for (int c = 0; c < kMaxRowChunks; ++c) {
+    for (int c = 0; c < kRC; ++c) {
       if (lo + c >= hi) continue;
       const int col = (lo + c) * 16;
 #pragma unroll
@@ -635,6 +637,8 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
 // are committed to the barriers of both CTAs; both epilogues publish to the even CTA.
 constexpr bool kPairTiles = true;
 
+// kRC: 16-column chunks of a row per epilogue thread (5 for d <= 240, 6 up to d = 288).
+template <int kRC>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_dense_kernel(const __grid_constant__ TcParams p) {
   constexpr bool kPair = kPairTiles;
   extern __shared__ __align__(1024) unsigned char smem[];
@@ -800,7 +804,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dense_kernel(const __grid_co
     }
   } else {
     const uint32_t publish_to = kPair && rank == 1 ? tc::map_shared(tc::smem_u32(&a_ready), 0) : 0u;
-    dense_epilogue(p, abuf, h0, h1, tmem, &a_ready, publish_to, &acc_ready, up_ready, h_free, &attn_full, &val_full,
+    dense_epilogue<kRC>(p, abuf, h0, h1, tmem, &a_ready, publish_to, &acc_ready, up_ready, h_free, &attn_full, &val_full,
                    abytes, red, prm);
   }
   tc::fence_before_sync();
@@ -1006,13 +1010,15 @@ int launch_dense_kernel(TcParams& p, cudaStream_t s) {
   const int smem = fixed + p.stages * p.stage_bytes;
   if ((abytes + 2 * p.hbytes + p.stages * p.stage_bytes) % 16)
     return set_error(CG_ERR_ARGUMENT, "tensor-core dense layer: unaligned shared-memory layout");
-  static int configured_smem[64] = {0};
+  const bool wide = p.d / 16 > kParts * 5;  // rows of more than 15 chunks: six per thread
+  auto kernel = wide ? tc_dense_kernel<6> : tc_dense_kernel<5>;
+  static int configured_smem[2][64] = {{0}};
   int device = 0;
   cudaGetDevice(&device);
-  if (configured_smem[device & 63] < smem) {
-    cudaError_t err = cudaFuncSetAttribute(tc_dense_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (configured_smem[wide][device & 63] < smem) {
+    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (err != cudaSuccess) return set_error(CG_ERR_CUDA, "tc_dense_kernel smem: %s", cudaGetErrorString(err));
-    configured_smem[device & 63] = smem;
+    configured_smem[wide][device & 63] = smem;
   }
   // The producer warp streams only the constant packed weights, so it starts at once; the
   // epilogue warps wait for the kernel before (pdl_wait in dense_epilogue).
@@ -1030,7 +1036,7 @@ int launch_dense_kernel(TcParams& p, cudaStream_t s) {
   attribute[1].val.clusterDim.z = 1;
   config.attrs = attribute;
   config.numAttrs = 2;
-  cudaError_t err = cudaLaunchKernelEx(&config, tc_dense_kernel, p);
+  cudaError_t err = cudaLaunchKernelEx(&config, kernel, p);
   if (err != cudaSuccess) return set_error(CG_ERR_CUDA, "tc_dense_kernel launch: %s", cudaGetErrorString(err));
   return check_launch("tc_dense_kernel");
 }

@@ -7,6 +7,8 @@ waves, whose deviation from fp32 is the accuracy bar for the B200 bf16 mode.
 
 from __future__ import annotations
 
+import dataclasses
+
 import numpy as np
 import pytest
 import torch
@@ -15,7 +17,7 @@ from card_playing_gym_b200.config import PlumpModelConfig, synthetic_plump_actor
 from oracle import plump as oplump
 from oracle import ppo as oppo
 from oracle.trunk import Precision
-from tests.conftest import trunk_fixture
+from tests.conftest import load_golden, trunk_fixture
 
 pytestmark = pytest.mark.gpu
 
@@ -207,3 +209,32 @@ def test_trunk_forward_ragged_from_conditioned_inputs(precision, kv):
                                            offsets)
     error = np.abs(hidden.cpu().numpy() - expected).max() / np.abs(expected).max()
     assert error < (FP32_ATOL if precision == "fp32" else 1e-2), error
+
+
+def test_wide_trunk_bf16_decode_tracks_the_oracle():
+    """A d = 256 trunk (piquet-scale dims: 8 query / 2 KV heads of 32, d_ff 512; two layers)
+    through the whole bf16 path: blocked field lookup, six-chunk epilogue rows, hd-32 attention."""
+
+    from card_playing_gym_b200.config import PIQUET_SCALE
+    from card_playing_gym_b200.plump import PlumpActor
+
+    config = dataclasses.replace(PIQUET_SCALE, n_layers=2)
+    state = synthetic_plump_actor_state(config, seed=31)
+    actor = PlumpActor(config, state, precision="bf16")
+    oracle = oplump.PlumpActor(state, dataclasses.asdict(config), Precision(gemm="bf16", kv="fp16"))
+    streams = load_golden("plump_streams")["tokens"].astype(np.int64)
+    batch, length = streams.shape[:2]
+    prefix = length // 2
+    cache = actor.new_cache(batch, length + 1, torch.float16)
+    ocache = oracle.new_cache(batch, length + 1)
+    tokens = torch.from_numpy(streams).cuda()
+    got = actor.forward_prefill(tokens[:, :prefix], cache, None).cpu().numpy()
+    expected = oracle.forward_prefill(streams[:, :prefix], ocache, None)
+    assert np.abs(got - expected).max() / np.abs(expected).max() < 1e-2
+    for step in range(prefix, min(length, prefix + 3)):
+        positions = np.full(batch, step, np.int64)
+        offsets = np.zeros(batch, np.int64)
+        got = actor.forward_ragged(tokens[:, step:step + 1], torch.from_numpy(positions).cuda(), cache,
+                                   torch.from_numpy(offsets).cuda()).cpu().numpy()
+        expected = oracle.forward_ragged(streams[:, step:step + 1], positions, ocache, offsets)
+        assert np.abs(got - expected).max() / np.abs(expected).max() < 1e-2, step
