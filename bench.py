@@ -70,6 +70,8 @@ def parse_args(argv=None):
     parser.add_argument("--ppo-decisions", type=int, default=262144,
                         help="PPO update batch (whole job, sharded by trajectory); 0 skips the PPO leg")
     parser.add_argument("--ppo-steps", type=int, default=20)
+    parser.add_argument("--piquet-steps", type=int, default=20,
+                        help="waves of the piquet-scale decode leg (8,192 two-player deals); 0 skips it")
     return parser.parse_args(argv)
 
 
@@ -228,6 +230,82 @@ def run_ppo(args, device, rank: int, world_size: int) -> dict:
                         "allreduce (NCCL) per step"),
         "includes": "GAE, global two-pass mean/std and normalise on the device (no host read), fused PPO "
                     "objective fwd+grad, value loss fwd+grad, autograd backward",
+    }
+
+
+# ---------------------------------------------------------------------------------------------
+# Piquet-scale decode leg: the same wave at the piquet-scale trunk's dimensions
+# ---------------------------------------------------------------------------------------------
+def run_piquet_scale(args, device, rank: int, world_size: int) -> dict:
+    """8,192 two-player deals per GPU (16,384 KV rows), one token per row, lengths U[32, 512],
+    fp16 KV, through PlumpActor at PIQUET_SCALE dims (d 256, 16 layers, 8/2 heads of 32,
+    d_ff 512; the plump field lookup and heads stand in for piquet's)."""
+
+    import torch
+    import torch.distributed as dist
+
+    from card_playing_gym_b200 import _native as nat
+    from card_playing_gym_b200.config import PIQUET_SCALE, synthetic_plump_actor_state
+    from card_playing_gym_b200.plump import PlumpActor
+
+    deals, max_len = 8192, 512
+    actor = PlumpActor(PIQUET_SCALE, synthetic_plump_actor_state(PIQUET_SCALE, seed=1), device=device,
+                       precision="bf16")
+    wave = synthetic_wave(deals // 2, 32, max_len, seed=2000 + 7919 * rank)  # 4 rows per group of 2 deals
+    rows = 4 * (deals // 2)
+    cache = actor.new_cache(rows + 1, max_len + 1, torch.float16)
+    generator = torch.Generator(device=device).manual_seed(23 + rank)
+    for pool in (cache.k_pool, cache.v_pool):
+        for layer in range(pool.shape[0]):
+            pool[layer].normal_(generator=generator)
+    dev = {k: torch.from_numpy(v).to(device) for k, v in wave.items()}
+    # one decision per deal: the readout row of each deal's acting player
+    readout = torch.arange(0, rows, 2, device=device, dtype=torch.int64)
+    heads = torch.randint(0, 2, (deals,), device=device, dtype=torch.int32, generator=generator)
+    legal = dev["legal"].repeat_interleave(2, dim=0)
+    uniforms = dev["uniforms"].repeat_interleave(2, dim=0)
+
+    def step():
+        hidden = actor.forward_ragged(dev["tokens"], dev["positions"], cache, dev["offsets"], span=max_len + 1)
+        return actor.decide(hidden, heads, legal, uniforms, readout, logits=False, values=False)
+
+    for _ in range(3):
+        step()
+    if world_size > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    stream = torch.cuda.current_stream(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.piquet_steps):
+        step()
+    end.record(stream)
+    torch.cuda.synchronize(device)
+    ms = start.elapsed_time(end) / args.piquet_steps
+    nat.attention_profiling(True, capacity=args.piquet_steps * 16 + 16)
+    for _ in range(args.piquet_steps):
+        step()
+    attention_ms = nat.attention_timings()
+    nat.attention_profiling(False)
+    if world_size > 1:
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    trunk = PIQUET_SCALE.trunk()
+    keys = float(np.minimum(wave["positions"] + 1, max_len + 1).sum())
+    algorithmic = keys * trunk.n_kv_heads * trunk.head_dim * 2 * 2 + rows * trunk.n_heads * trunk.head_dim * 4
+    mean_ms = statistics.fmean(attention_ms)
+    achieved = algorithmic / (mean_ms / 1000.0) / 1e9
+    peak, peak_kind = measured_peak()
+    return {
+        "workload": (f"piquet-scale decode wave: {deals} two-player deals ({rows} KV rows), 1 token/row, lengths "
+                     f"U[32,{max_len}], fp16 KV, trunk d256/16L/8-2 heads of 32/d_ff 512 (plump lookup and heads "
+                     "stand in for piquet's)"),
+        "value": world_size * deals / (ms / 1000.0), "unit": "decisions/s", "rows_per_s": world_size * rows / (ms / 1000.0),
+        "ms_per_step": ms, "steps": args.piquet_steps,
+        "attention_roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                               "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                               "algorithmic_bytes_per_launch": algorithmic, "mean_launch_ms": mean_ms},
     }
 
 
@@ -490,6 +568,7 @@ def run_b200(args) -> int:
     e2e_ms = max_over_ranks(start.elapsed_time(end))
     e2e_value = world_size * games * args.steps / (e2e_ms / 1000.0)
     ppo_line = run_ppo(args, device, rank, world_size) if args.ppo_decisions > 0 else None
+    piquet_line = run_piquet_scale(args, device, rank, world_size) if args.piquet_steps > 0 else None
 
     if rank == 0:
         head_dim = RL_V6.trunk().head_dim
@@ -547,6 +626,8 @@ def run_b200(args) -> int:
         }
         if ppo_line is not None:
             line["ppo"] = ppo_line
+        if piquet_line is not None:
+            line["piquet_scale"] = piquet_line
         if world_size == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args, args.cpu_seconds)
         print(json.dumps(line), flush=True)
