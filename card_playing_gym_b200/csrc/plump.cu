@@ -138,27 +138,25 @@ struct EmbedOut {
   int64_t ntiles;
 };
 
-__device__ __forceinline__ void store_lookup(const EmbedOut& o, int width, int64_t token, int c4, const float4& v) {
-  if (!o.x_blk) {
-    reinterpret_cast<float4*>(o.rows + token * width)[c4] = v;
-    return;
-  }
-  const int64_t tile = token >> 7;
-  const int r = static_cast<int>(token & 127);
+// Blocked destination of float4 column c4 for tile 0, row 0, and the step from one tile to the
+// next: the token-independent part of store_lookup's address, computed once per column.
+struct LookupColumn {
+  float4* base;
+  int64_t tile_stride;
+};
+
+__device__ __forceinline__ LookupColumn lookup_column(const EmbedOut& o, int c4) {
   int k = 4 * c4;
-  float4* dst;
-  if (k < o.d) {
-    dst = reinterpret_cast<float4*>(o.x_blk) + ((tile * (o.d / 4) + k / 4) * 128 + r);
-  } else if ((k -= o.d) < o.ple_w) {
+  if (k < o.d) return {reinterpret_cast<float4*>(o.x_blk) + static_cast<int64_t>(k / 4) * 128, (o.d / 4) * 128};
+  if ((k -= o.d) < o.ple_w) {
     const int layer = k / o.P, q = k - layer * o.P;
-    dst = reinterpret_cast<float4*>(o.ple_blk) + (((layer * o.ntiles + tile) * (o.P / 4) + q / 4) * 128 + r);
-  } else {
-    k -= o.ple_w;
-    const int vl = k / o.kvw, q = k - vl * o.kvw;
-    dst = reinterpret_cast<float4*>(o.val_blk) + (((vl * o.ntiles + tile) * (o.kvw / 4) + q / 4) * 128 + r);
+    return {reinterpret_cast<float4*>(o.ple_blk) + (layer * o.ntiles * (o.P / 4) + q / 4) * 128, (o.P / 4) * 128};
   }
-  *dst = v;
+  k -= o.ple_w;
+  const int vl = k / o.kvw, q = k - vl * o.kvw;
+  return {reinterpret_cast<float4*>(o.val_blk) + (vl * o.ntiles * (o.kvw / 4) + q / 4) * 128, (o.kvw / 4) * 128};
 }
+
 
 template <int kSliceF4>  // float4 columns per slice = lanes per token
 __global__ void __launch_bounds__(kEmbedThreads, 1) plump_embed_sliced_kernel(
@@ -248,6 +246,7 @@ __global__ void __launch_bounds__(kEmbedThreads, 1) plump_embed_sliced_kernel(
     __syncthreads();  // this slice (and, on the first pass, every token's ids) is in place
     const float4* tab = slices + (slice & 1) * total_rows * kSliceF4 + col;
     const int c = slice * kSliceF4 + col;
+    const LookupColumn dst = out.x_blk && c < width4 ? lookup_column(out, c) : LookupColumn{nullptr, 0};
     for (int t = warp * kTokensPerWarp + sub; t < count; t += (kEmbedThreads / 32) * kTokensPerWarp) {
       const EmbedIds& e = ids[t];
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -272,7 +271,13 @@ __global__ void __launch_bounds__(kEmbedThreads, 1) plump_embed_sliced_kernel(
         acc.z += hand.z;
         acc.w += hand.w;
       }
-      if (c < width4) store_lookup(out, width, first + t, c, acc);
+      if (c < width4) {
+        const int64_t token = first + t;
+        if (dst.base)
+          dst.base[(token >> 7) * dst.tile_stride + (token & 127)] = acc;
+        else
+          reinterpret_cast<float4*>(out.rows + token * width)[c] = acc;
+      }
     }
     __syncthreads();  // every warp is done with this buffer before it is refilled
   }
