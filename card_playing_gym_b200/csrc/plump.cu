@@ -158,19 +158,31 @@ __device__ __forceinline__ LookupColumn lookup_column(const EmbedOut& o, int c4)
 }
 
 
+// Shared memory of a sliced lookup CTA: two table slices, the row ids and the token rows.
+__host__ __device__ inline size_t embed_smem_bytes(int total_rows, int slice_f4, int tokens, int token_width) {
+  return 2 * static_cast<size_t>(total_rows) * slice_f4 * 16 + static_cast<size_t>(tokens) * sizeof(EmbedIds) +
+         (static_cast<size_t>(tokens) * token_width * 4 + 15) / 16 * 16;
+}
+
+// Grid: x = token blocks of tokens_per_cta, y = column groups of slices_per_cta slices (the
+// split keeps every CTA's token passes full when the tokens alone would leave the last
+// pass of each CTA partly idle).
 template <int kSliceF4>  // float4 columns per slice = lanes per token
 __global__ void __launch_bounds__(kEmbedThreads, 1) plump_embed_sliced_kernel(
     cg_plump_schema sc, const float* __restrict__ table, int width, const void* __restrict__ tokens, int token_dtype,
-    int64_t n, int tokens_per_cta, EmbedOut out) {
+    int64_t n, int tokens_per_cta, int slices_per_cta, EmbedOut out) {
   extern __shared__ __align__(16) unsigned char emb_smem[];
   const int total_rows = sc.field_rows + sc.pattern_rows;
   float4* slices = reinterpret_cast<float4*>(emb_smem);  // [2][total_rows][kSliceF4]
   EmbedIds* ids = reinterpret_cast<EmbedIds*>(slices + 2 * total_rows * kSliceF4);
+  int* tok_s = reinterpret_cast<int*>(ids + tokens_per_cta);  // [count][token_width], clamped to int32
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t first = static_cast<int64_t>(blockIdx.x) * tokens_per_cta;
   const int count = static_cast<int>(n - first < tokens_per_cta ? n - first : tokens_per_cta);
   const int width4 = width / 4;
   const int n_slices = (width4 + kSliceF4 - 1) / kSliceF4;
+  const int s_begin = blockIdx.y * slices_per_cta;
+  const int s_end = min(n_slices, s_begin + slices_per_cta);
 
   auto load_slice = [&](int slice, int buf) {
     const int c0 = slice * kSliceF4;
@@ -186,17 +198,30 @@ __global__ void __launch_bounds__(kEmbedThreads, 1) plump_embed_sliced_kernel(
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  load_slice(0, 0);  // the table is constant: its first slice loads while the kernel before finishes
+  if (s_begin < s_end) load_slice(s_begin, 0);  // the table is constant: it loads while the kernel before finishes
   pdl_wait();
   pdl_trigger();
+  if (s_begin >= s_end) return;
+
+  // The CTA's token rows in one coalesced pass. Values are clamped to the int32 range, which
+  // keeps every range check below (ids, patterns, cards) deciding as on the full value.
+  {
+    const int64_t base = first * sc.token_width;
+    const int total = count * sc.token_width;
+    for (int i = tid; i < total; i += kEmbedThreads) {
+      const int64_t v = token_at(tokens, token_dtype, base + i);
+      tok_s[i] = static_cast<int>(v < INT32_MIN ? INT32_MIN : (v > INT32_MAX ? INT32_MAX : v));
+    }
+  }
+  __syncthreads();
 
   // Row ids, one warp per token (the same resolution as plump_embed_kernel).
   const unsigned lt = (1u << lane) - 1u;
   for (int t = warp; t < count; t += kEmbedThreads / 32) {
-    const int64_t base = (first + t) * sc.token_width;
+    const int* tok = tok_s + t * sc.token_width;
     int field_row = -1;
     if (lane < sc.field_count) {
-      const int64_t id = token_at(tokens, token_dtype, base + sc.field_slots[lane]);
+      const int64_t id = tok[sc.field_slots[lane]];
       const bool present = sc.field_na[lane] < 0 || id != sc.field_na[lane];
       const int64_t row = id + sc.field_offsets[lane];
       if (present) {
@@ -207,15 +232,15 @@ __global__ void __launch_bounds__(kEmbedThreads, 1) plump_embed_sliced_kernel(
         }
       }
     }
-    int64_t pattern = token_at(tokens, token_dtype, base + sc.slot_pattern);
+    int64_t pattern = tok[sc.slot_pattern];
     if (pattern < 0 || pattern >= sc.pattern_rows) {
       if (lane == 0) raise_fault(0x201);
       pattern = 0;
     }
-    const bool trick_win = token_at(tokens, token_dtype, base + sc.slot_type) == sc.trick_win_type;
+    const bool trick_win = tok[sc.slot_type] == sc.trick_win_type;
     int hand_row = -1;
     if (trick_win && lane < 2 * sc.hand_slots) {
-      const int64_t card = token_at(tokens, token_dtype, base + sc.slot_hand + lane / 2);
+      const int64_t card = tok[sc.slot_hand + lane / 2];
       if (card >= 0 && card < sc.num_cards) {
         hand_row = (lane & 1) ? static_cast<int>(card / sc.num_ranks) + sc.suit_offset
                               : static_cast<int>(card % sc.num_ranks) + sc.rank_offset;
@@ -236,15 +261,16 @@ __global__ void __launch_bounds__(kEmbedThreads, 1) plump_embed_sliced_kernel(
 
   constexpr int kTokensPerWarp = 32 / kSliceF4;
   const int sub = lane / kSliceF4, col = lane % kSliceF4;
-  for (int slice = 0; slice < n_slices; ++slice) {
-    if (slice + 1 < n_slices) {
-      load_slice(slice + 1, (slice + 1) & 1);
+  for (int slice = s_begin; slice < s_end; ++slice) {
+    const int buf = (slice - s_begin) & 1;
+    if (slice + 1 < s_end) {
+      load_slice(slice + 1, buf ^ 1);
       asm volatile("cp.async.wait_group 1;" ::: "memory");
     } else {
       asm volatile("cp.async.wait_group 0;" ::: "memory");
     }
     __syncthreads();  // this slice (and, on the first pass, every token's ids) is in place
-    const float4* tab = slices + (slice & 1) * total_rows * kSliceF4 + col;
+    const float4* tab = slices + buf * total_rows * kSliceF4 + col;
     const int c = slice * kSliceF4 + col;
     const LookupColumn dst = out.x_blk && c < width4 ? lookup_column(out, c) : LookupColumn{nullptr, 0};
     for (int t = warp * kTokensPerWarp + sub; t < count; t += (kEmbedThreads / 32) * kTokensPerWarp) {
@@ -299,8 +325,10 @@ int embed(const cg_plump_schema& sc, const float* table, int width, const void* 
   const int total_rows = sc.field_rows + sc.pattern_rows;
   // Widest slice whose two buffers fit next to the ids: 16 float4 (64 columns) for plump.
   int slice_f4 = 16;
-  while (slice_f4 > 4 && 2LL * total_rows * slice_f4 * 16 > 200 * 1024) slice_f4 /= 2;
-  const bool sliced = (width % 4) == 0 && 2LL * total_rows * slice_f4 * 16 <= 200 * 1024 &&
+  while (slice_f4 > 4 && embed_smem_bytes(total_rows, slice_f4, kEmbedMaxTokens, sc.token_width) > 227 * 1024)
+    slice_f4 /= 2;
+  const bool sliced = (width % 4) == 0 &&
+                      embed_smem_bytes(total_rows, slice_f4, kEmbedMaxTokens, sc.token_width) <= 227 * 1024 &&
                       (reinterpret_cast<uintptr_t>(table) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
                       sc.hand_slots * 2 <= 32 && sc.field_count <= 16;
   if (dest.x_blk && !sliced) return set_error(CG_ERR_ARGUMENT, "blocked field-lookup output needs the sliced kernel");
@@ -309,10 +337,28 @@ int embed(const cg_plump_schema& sc, const float* table, int width, const void* 
     plump_embed_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(sc, table, width, tokens, token_dtype, n, out);
     return check_launch("plump_embed_kernel");
   }
-  int64_t per = (n + sm_count() - 1) / sm_count();
-  if (per > kEmbedMaxTokens) per = kEmbedMaxTokens;
+  // Work of a CTA ~ its slices x its token passes (32 / slice_f4 tokens per warp, 16 warps):
+  // pick the column-group count whose slowest CTA does the least, with one wave of CTAs.
+  const int n_slices = (width / 4 + slice_f4 - 1) / slice_f4;
+  const int64_t pass_tokens = static_cast<int64_t>(kEmbedThreads / 32) * (32 / slice_f4);
+  int groups = 1;
+  int64_t per = 0, best = -1;
+  for (int gcount = 1; gcount <= 4 && gcount <= n_slices; ++gcount) {
+    const int64_t token_blocks = sm_count() / gcount;
+    if (token_blocks < 1) break;
+    int64_t tokens = (n + token_blocks - 1) / token_blocks;
+    if (tokens > kEmbedMaxTokens) tokens = kEmbedMaxTokens;
+    const int64_t waves = ((n + tokens - 1) / tokens * gcount + sm_count() - 1) / sm_count();
+    const int64_t work = waves * ((n_slices + gcount - 1) / gcount) * ((tokens + pass_tokens - 1) / pass_tokens);
+    if (best < 0 || work < best) {
+      best = work;
+      groups = gcount;
+      per = tokens;
+    }
+  }
+  const int slices_per = (n_slices + groups - 1) / groups;
   const int64_t blocks = (n + per - 1) / per;
-  const size_t smem = 2 * static_cast<size_t>(total_rows) * slice_f4 * 16 + static_cast<size_t>(per) * sizeof(EmbedIds);
+  const size_t smem = embed_smem_bytes(total_rows, slice_f4, static_cast<int>(per), sc.token_width);
   auto launch = [&](auto kernel) {
     static size_t configured[64] = {0};
     int device = 0;
@@ -322,8 +368,9 @@ int embed(const cg_plump_schema& sc, const float* table, int width, const void* 
       if (err != cudaSuccess) return set_error(CG_ERR_CUDA, "plump_embed_sliced_kernel smem: %s", cudaGetErrorString(err));
       configured[device & 63] = smem;
     }
-    return launch_pdl("plump_embed_sliced_kernel", kernel, dim3(static_cast<unsigned>(blocks)), dim3(kEmbedThreads),
-                      smem, s, sc, table, width, tokens, token_dtype, n, static_cast<int>(per), dest);
+    return launch_pdl("plump_embed_sliced_kernel", kernel,
+                      dim3(static_cast<unsigned>(blocks), static_cast<unsigned>(groups)), dim3(kEmbedThreads), smem,
+                      s, sc, table, width, tokens, token_dtype, n, static_cast<int>(per), slices_per, dest);
   };
   if (slice_f4 == 16) return launch(plump_embed_sliced_kernel<16>);
   if (slice_f4 == 8) return launch(plump_embed_sliced_kernel<8>);

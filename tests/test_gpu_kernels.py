@@ -116,6 +116,28 @@ def test_plump_field_lookup_matches_the_oracle():
     assert torch.equal(x16, x)
 
 
+@pytest.mark.parametrize("value", (1 << 40, -(1 << 40), 1 << 31))
+def test_plump_field_lookup_flags_ids_out_of_range(value):
+    """An id outside its field's rows (int64 values past the int32 range included) sets the
+    device fault word to 0x200, as the reference's embedding lookup raises an index error."""
+
+    from card_playing_gym_b200 import _native as nat
+    from card_playing_gym_b200.config import PlumpModelConfig, synthetic_plump_actor_state
+    from card_playing_gym_b200.plump import PlumpActor
+
+    config = PlumpModelConfig()
+    actor = PlumpActor(config, synthetic_plump_actor_state(config, seed=9), precision="fp32")
+    streams = load_golden("plump_streams")["tokens"].astype(np.int64)
+    assert nat.fault_status() == 0
+    actor.embed(torch.from_numpy(streams).cuda())
+    assert nat.fault_status() == 0
+    bad = streams.copy()
+    bad.reshape(-1, bad.shape[-1])[3, actor.schema.field_slots[0]] = value
+    actor.embed(torch.from_numpy(bad).cuda())
+    assert nat.fault_status() == 0x200
+    assert nat.fault_status() == 0  # read and cleared
+
+
 def test_plump_field_lookup_row_per_warp_kernel_matches_the_sliced_kernel():
     """A table width that is not a multiple of 4 takes the row-per-warp lookup: the same sums, bit for bit."""
 
