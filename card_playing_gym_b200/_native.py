@@ -60,6 +60,25 @@ class HeadsDesc(ctypes.Structure):
     ]
 
 
+class CardScorerWeights(ctypes.Structure):
+    _fields_ = [
+        ("d_model", ctypes.c_int32), ("card_width", ctypes.c_int32), ("dim", ctypes.c_int32), ("cards", ctypes.c_int32),
+        ("query_w", ctypes.c_void_p), ("query_b", ctypes.c_void_p), ("card_w", ctypes.c_void_p),
+        ("card_id", ctypes.c_void_p), ("norm_w", ctypes.c_void_p), ("norm_b", ctypes.c_void_p),
+        ("hidden_w", ctypes.c_void_p), ("hidden_b", ctypes.c_void_p), ("out_w", ctypes.c_void_p),
+        ("out_b", ctypes.c_void_p),
+    ]
+
+
+class CandidateScorerWeights(ctypes.Structure):
+    _fields_ = [
+        ("d_model", ctypes.c_int32), ("card_width", ctypes.c_int32), ("dim", ctypes.c_int32), ("cards", ctypes.c_int32),
+        ("kinds", ctypes.c_int32), ("sizes", ctypes.c_int32),
+    ] + [(name, ctypes.c_void_p) for name in (
+        "query_w", "query_b", "card_w", "target_w", "taken_w", "card_id", "target_id", "taken_id", "kind_emb",
+        "size_emb", "norm_w", "norm_b", "hidden_w", "hidden_b", "out_w", "out_b")]
+
+
 _SIGNATURES: dict[str, tuple[type, list]] = {
     "cg_last_error": (ctypes.c_char_p, []),
     "cg_version": (_i32, []),
@@ -80,6 +99,10 @@ _SIGNATURES: dict[str, tuple[type, list]] = {
     "cg_trunk_part_offset": (_i64, [ctypes.POINTER(TrunkDims), _i32, _i32]),
     "cg_trunk_prepare": (_i32, [ctypes.POINTER(TrunkDims), _p, _p]),
     "cg_plump_embed": (_i32, [ctypes.POINTER(PlumpSchemaC), _p, _i32, _p, _i32, _i64, _p, _p]),
+    "cg_onehot_bags": (_i32, [_p, _i32, _i64, _i64, _i32, ctypes.POINTER(_i64), _p, _i32, _i64, _i32, _p, _p]),
+    "cg_card_scorer": (_i32, [ctypes.POINTER(CardScorerWeights), _p, _i64, _p, _i32, _p, _p]),
+    "cg_candidate_scorer": (_i32, [ctypes.POINTER(CandidateScorerWeights), _p, _i64, _i32, _i32, _p, _i32, _p, _p, _p,
+                                   _p, _p, _p]),
     "cg_trunk_step_workspace_bytes": (_i64, [ctypes.POINTER(TrunkDims), _i64, _i32, _i32]),
     "cg_trunk_forward_ragged": (_i32, [ctypes.POINTER(TrunkDims), _p, _p, _p, _p, _i64, _i32, _p, _p, _p, _i32, _p, _p,
                                        _i32, _i64, _i32, _i32, _p, _i64, _p, _p]),

@@ -1,0 +1,138 @@
+"""Piquet field lookup and card pointer heads on the device.
+
+Reference: cardgym/games/piquet/model.py:255-264 (``_onehot_bags``) and the field part of
+``PiquetEmbedding.forward`` 323-345: ids = tokens[..., :NUM_FIELDS] + offsets, and every
+table's field sums as one product of one-hot token rows with the tables side by side, in
+the autocast dtype (fp32 accumulation, each sum rounded once) or the tables' own. Here the
+product is a gather-sum of each distinct selected row (``cg_onehot_bags``). The card-grid
+summary that ``PiquetEmbedding.forward`` adds to the first sum stays with the caller.
+
+``CardScorer`` mirrors cardgym/games/piquet/model.py:348-363: one logit per card from the
+readout state and the card's grid features (``cg_card_scorer``), as PiquetActor.policy_logits
+(399-411) calls it for the exchange and play heads.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _native as nat
+
+NUM_FIELDS = 32
+CARD_START = NUM_FIELDS
+# cardgym/games/piquet/tokens.py:121-128, evaluated: rows of each field in the tables.
+FIELD_VOCAB = (8, 4, 3, 2, 33, 9, 9, 4, 4, 9, 76, 9, 3, 4, 64, 5, 3, 13, 3, 5, 13, 13, 100, 100, 141, 141, 6, 2,
+               9, 16, 4, 149)
+FIELD_ROWS = sum(FIELD_VOCAB)
+
+
+def field_offsets() -> list[int]:
+    """First table row of each field (``PiquetEmbedding.offsets``)."""
+
+    return [sum(FIELD_VOCAB[:i]) for i in range(NUM_FIELDS)]
+
+
+def _lookup_dtype(tables: list[torch.Tensor]) -> torch.dtype:
+    if torch.is_autocast_enabled("cuda"):
+        return torch.get_autocast_dtype("cuda")
+    return tables[0].dtype
+
+
+def _bags(ids: torch.Tensor, id_stride: int, fields: int, offsets: list[int] | None, table: torch.Tensor,
+          lead: tuple[int, ...]) -> torch.Tensor:
+    if table.dtype not in nat.DTYPE_CODES:
+        raise TypeError(f"field tables in {table.dtype} are not supported")
+    count = ids.shape[0]
+    out = torch.empty((count, table.shape[1]), dtype=table.dtype, device=table.device)
+    offs = None
+    if offsets is not None:
+        offs = (nat._i64 * fields)(*offsets)
+    nat.call("cg_onehot_bags", nat.ptr(ids), nat.INDEX_CODES[ids.dtype], count, id_stride, fields, offs,
+             nat.ptr(table), nat.DTYPE_CODES[table.dtype], table.shape[0], table.shape[1], nat.ptr(out),
+             nat.stream_handle(table.device))
+    return out.view(*lead, table.shape[1])
+
+
+def onehot_bags(ids: torch.Tensor, tables: list[torch.Tensor]) -> list[torch.Tensor]:
+    """``_onehot_bags(ids, tables)``: ids [..., F] row ids, tables [rows, w_i] -> sums [..., w_i]."""
+
+    dtype = _lookup_dtype(tables)
+    flat = ids.reshape(-1, ids.shape[-1])
+    if flat.dtype not in nat.INDEX_CODES:
+        flat = flat.long()
+    flat = flat.contiguous()
+    table = torch.cat(tables, dim=1).to(dtype).contiguous()
+    sums = _bags(flat, flat.shape[1], flat.shape[1], None, table, tuple(ids.shape[:-1]))
+    widths = [t.shape[1] for t in tables]
+    return list(sums.split(widths, dim=-1))
+
+
+class PiquetFieldLookup:
+    """The field sums of ``PiquetEmbedding.forward`` with the tables packed once per dtype.
+
+    ``fields`` is ``embedding.fields.weight`` [FIELD_ROWS, d]; ``ple`` and ``values`` the
+    optional ``ple_fields``/``value_fields`` tables. Calling it with tokens [..., 64]
+    (int16/int32/int64) returns (fields, ple or None, values or None) sums in the lookup
+    dtype (the autocast dtype on CUDA, else the tables').
+    """
+
+    def __init__(self, fields: torch.Tensor, ple: torch.Tensor | None = None, values: torch.Tensor | None = None):
+        self.parts = [fields] + [t for t in (ple, values) if t is not None]
+        self.has = (ple is not None, values is not None)
+        self.offsets = field_offsets()
+        self._packed: dict[torch.dtype, torch.Tensor] = {}
+
+    def table(self, dtype: torch.dtype) -> torch.Tensor:
+        packed = self._packed.get(dtype)
+        if packed is None:
+            packed = torch.cat(self.parts, dim=1).to(dtype).contiguous()
+            self._packed[dtype] = packed
+        return packed
+
+    def __call__(self, tokens: torch.Tensor):
+        dtype = _lookup_dtype(self.parts)
+        flat = tokens.reshape(-1, tokens.shape[-1])
+        if flat.dtype not in nat.INDEX_CODES:
+            flat = flat.long()
+        flat = flat.contiguous()
+        sums = _bags(flat, flat.shape[1], NUM_FIELDS, self.offsets, self.table(dtype), tuple(tokens.shape[:-1]))
+        parts = iter(sums.split([t.shape[1] for t in self.parts], dim=-1))
+        first = next(parts)
+        ple = next(parts) if self.has[0] else None
+        values = next(parts) if self.has[1] else None
+        return first, ple, values
+
+
+class CardScorer:
+    """``CardScorer.forward(hidden [N, d], grid [N, 32, card_width]) -> logits fp32 [N, 32]``.
+
+    Built from the reference module's parameters (``state`` holds ``prefix + "query.weight"``
+    and the rest, as in a PiquetActor ``state_dict`` with prefix ``"play_scorer."`` or
+    ``"exchange_scorer."``). fp32 arithmetic whatever the grid's dtype.
+    """
+
+    NAMES = ("query.weight", "query.bias", "card.weight", "card_id.weight", "norm.weight", "norm.bias",
+             "hidden.weight", "hidden.bias", "out.weight", "out.bias")
+
+    def __init__(self, state: dict, prefix: str = "", device: torch.device | str = "cuda"):
+        self.params = {
+            name: torch.as_tensor(state[prefix + name]).detach().to(device=device, dtype=torch.float32).contiguous()
+            for name in self.NAMES
+        }
+        p = self.params
+        dim, d = p["query.weight"].shape
+        self.weights = nat.CardScorerWeights(
+            d, p["card.weight"].shape[1], dim, p["card_id.weight"].shape[0],
+            *[nat.ptr(p[name]) for name in self.NAMES[:8]], nat.ptr(p["out.weight"]), nat.ptr(p["out.bias"]),
+        )
+
+    def __call__(self, hidden: torch.Tensor, grid: torch.Tensor) -> torch.Tensor:
+        hidden = hidden.float().contiguous()
+        if grid.dtype not in nat.DTYPE_CODES:
+            grid = grid.float()
+        grid = grid.contiguous()
+        count = hidden.shape[0]
+        logits = torch.empty((count, self.weights.cards), dtype=torch.float32, device=hidden.device)
+        nat.call("cg_card_scorer", self.weights, nat.ptr(hidden), count, nat.ptr(grid), nat.DTYPE_CODES[grid.dtype],
+                 nat.ptr(logits), nat.stream_handle(hidden.device))
+        return logits

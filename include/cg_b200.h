@@ -152,6 +152,78 @@ int cg_plump_embed(const cg_plump_schema* schema, const float* table, int width,
                    int64_t n_tokens, float* out, void* stream);
 
 /* ---------------------------------------------------------------------------------
+ * One-hot field bags (cardgym/games/piquet/model.py:255-264 `_onehot_bags`, used by
+ * PiquetEmbedding.forward 323-345 and RummyEmbedding): for each of n_tokens tokens, the
+ * sum of the table rows its `fields` ids select (id = ids[t * ids_stride + f] + offsets[f];
+ * offsets may be NULL for ids that already carry them), each distinct row once, as the
+ * reference's `zeros(N, rows).scatter_(1, ids, 1) @ table` with fp32 accumulation.
+ * table [rows, width] and out [n_tokens, width] share table_dtype (CG_F32, CG_BF16 or
+ * CG_F16: the autocast dtype the reference's GEMM runs in); each sum is rounded once.
+ * An id outside [0, rows) sets the device fault word to 0x210 and selects nothing.
+ * ------------------------------------------------------------------------------- */
+int cg_onehot_bags(const void* ids, int ids_dtype, int64_t n_tokens, int64_t ids_stride, int fields,
+                   const int64_t* offsets, const void* table, int table_dtype, int64_t rows, int width, void* out,
+                   void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * Card pointer head (cardgym/games/piquet/model.py:348-363 `CardScorer.forward`, the
+ * exchange and play heads of PiquetActor.policy_logits 399-411): one logit per card,
+ *   out(GELU(hidden(LayerNorm(query(h)[:, None] + card(grid) + card_id)))).
+ * Weights are fp32 device pointers in the reference's [out, in] layout; dim must be 64
+ * (score_dim), cards <= 32, card_width <= 32, d_model <= 512.
+ * hidden fp32 [n, d_model]; grid [n, cards, card_width] in grid_dtype (CG_F32, CG_BF16,
+ * CG_F16); logits fp32 [n, cards]. fp32 arithmetic.
+ * ------------------------------------------------------------------------------- */
+typedef struct {
+  int32_t d_model, card_width, dim, cards;
+  const float* query_w;  /* [dim, d_model] */
+  const float* query_b;  /* [dim] */
+  const float* card_w;   /* [dim, card_width] (no bias) */
+  const float* card_id;  /* [cards, dim] */
+  const float* norm_w;   /* [dim] LayerNorm, eps 1e-5 */
+  const float* norm_b;   /* [dim] */
+  const float* hidden_w; /* [dim, dim] */
+  const float* hidden_b; /* [dim] */
+  const float* out_w;    /* [dim] (the [1, dim] output layer) */
+  const float* out_b;    /* [1] */
+} cg_card_scorer_weights;
+int cg_card_scorer(const cg_card_scorer_weights* weights, const float* hidden, int64_t n, const void* grid, int grid_dtype,
+                   float* logits, void* stream);
+
+/* Candidate pointer head (cardgym/games/rummy/model.py:292-357 `CandidateScorer.forward`,
+ * RummyActor.policy_logits 391-399): per decision n and candidate c,
+ *   candidate = card(Σ grid[cards]) + target(Σ grid[target]) + taken(taken @ grid)
+ *             + Σ card_id[cards] + Σ target_id[target] + taken @ taken_id
+ *             + kind_emb[kind] + size_emb[#cards != NO_CARD]
+ *   logit = out(GELU(hidden(LayerNorm(query(h) + candidate))))
+ * kind int64 [n, candidates]; cards/target int64 [n, candidates, list] with NO_CARD = cards
+ * as padding; taken fp32 [n, candidates, cards] counts or NULL (the play head); grid
+ * [n, cards, card_width]; logits fp32 [n, candidates]. dim 64, card_width <= 32,
+ * cards <= 64, list <= 16. Bad ids set the fault word: card 0x220, kind 0x221, size 0x222. */
+typedef struct {
+  int32_t d_model, card_width, dim, cards, kinds, sizes;
+  const float* query_w;   /* [dim, d_model] */
+  const float* query_b;   /* [dim] */
+  const float* card_w;    /* [dim, card_width] */
+  const float* target_w;  /* [dim, card_width] */
+  const float* taken_w;   /* [dim, card_width] */
+  const float* card_id;   /* [cards, dim] */
+  const float* target_id; /* [cards, dim] */
+  const float* taken_id;  /* [cards, dim] */
+  const float* kind_emb;  /* [kinds, dim] */
+  const float* size_emb;  /* [sizes, dim] */
+  const float* norm_w;
+  const float* norm_b;
+  const float* hidden_w;  /* [dim, dim] */
+  const float* hidden_b;
+  const float* out_w;     /* [dim] */
+  const float* out_b;     /* [1] */
+} cg_candidate_scorer_weights;
+int cg_candidate_scorer(const cg_candidate_scorer_weights* weights, const float* hidden, int64_t n, int candidates,
+                        int list, const void* grid, int grid_dtype, const int64_t* kind, const int64_t* cards,
+                        const int64_t* target, const float* taken, float* logits, void* stream);
+
+/* ---------------------------------------------------------------------------------
  * Ragged cached decode of the whole trunk (cardgym/nn/trunk.py:391-429, 183-223):
  * appends `steps` tokens to each of `batch` cache rows (rows[b], or b when rows is NULL)
  * at positions[b], and returns the final-normed hidden state of token readout_offsets[b]

@@ -19,6 +19,11 @@ Fixtures:
   ppo.npz             ppo_terms terms and the autograd gradient of the head objective
   gae.npz             gae_advantages per game, acting-seat advantages
   value_loss.npz      PPOTrainer._value_loss and its autograd gradient
+  piquet_bags.npz     the piquet field lookup (``_onehot_bags``) in fp32, bf16 and fp16
+  card_scorer.npz     the piquet card pointer head (``CardScorer``) in fp32 and bf16 autocast
+  candidate_scorer.npz the rummy candidate pointer head (``CandidateScorer``), draw and play calls
+
+``python tests/golden/make_golden.py piquet_bags`` regenerates one fixture.
 """
 
 from __future__ import annotations
@@ -302,7 +307,116 @@ def make_value_loss() -> None:
     )
 
 
+PIQUET_BAG_WIDTHS = {"wide": (64, 128, 64), "odd": (20, 12, 6)}
+
+
+def piquet_bag_tables(widths: tuple[int, ...], seed: int) -> list[np.ndarray]:
+    """The synthetic field tables of the piquet lookup fixture (regenerated from the seed by the tests)."""
+
+    from oracle.piquet import ROWS
+
+    rng = np.random.default_rng(seed)
+    return [(rng.standard_normal((ROWS, w)) * 0.02).astype(np.float32) for w in widths]
+
+
+def make_piquet_bags() -> None:
+    """``_onehot_bags`` and the field part of ``PiquetEmbedding.forward`` on synthetic piquet tokens."""
+
+    from cardgym.games.piquet.model import _onehot_bags
+    from cardgym.games.piquet.tokens import FIELD_VOCAB, NUM_FIELDS, WIDTH
+
+    rng = np.random.default_rng(41)
+    count = 200
+    tokens = np.zeros((count, WIDTH), dtype=np.int64)
+    for field, vocab in enumerate(FIELD_VOCAB):
+        tokens[:, field] = rng.integers(0, vocab, count)
+    tokens[:, NUM_FIELDS:] = rng.integers(0, 12, (count, WIDTH - NUM_FIELDS))
+    offsets = np.array([sum(FIELD_VOCAB[:i]) for i in range(NUM_FIELDS)], dtype=np.int64)
+    # Ids past their own field's rows land in the next field's: tokens 0..7 repeat a row there.
+    for t in range(8):
+        field = t
+        tokens[t, field + 1] = t % FIELD_VOCAB[field + 1]
+        tokens[t, field] = FIELD_VOCAB[field] + tokens[t, field + 1]
+    ids = tokens[:, :NUM_FIELDS] + offsets
+    cases = {"tokens": tokens.astype(np.int16), "seed": np.int64(43)}
+    for name, widths in PIQUET_BAG_WIDTHS.items():
+        tables = piquet_bag_tables(widths, 43)
+        for storage, dtype in (("fp32", torch.float32), ("bf16", torch.bfloat16), ("fp16", torch.float16)):
+            sums = _onehot_bags(torch.from_numpy(ids), [torch.from_numpy(t).to(dtype) for t in tables])
+            for part, values in zip(("fields", "ple", "values"), sums):
+                cases[f"{name}_{storage}_{part}"] = values.float().numpy()
+    np.savez_compressed(HERE / "piquet_bags.npz", **cases)
+
+
+def make_card_scorer() -> None:
+    """``CardScorer.forward`` (piquet pointer head) in fp32 and under bf16 autocast."""
+
+    from cardgym.games.piquet.model import CardScorer
+
+    torch.manual_seed(51)
+    scorer = CardScorer(256, 32, 64)
+    with torch.no_grad():  # the init leaves the norm at 1/0 and the biases at 0: exercise them
+        scorer.norm.weight.uniform_(0.5, 1.5)
+        for bias in (scorer.norm.bias, scorer.query.bias, scorer.hidden.bias, scorer.out.bias):
+            bias.normal_(0.0, 0.1)
+    scorer.eval()
+    hidden = torch.randn(48, 256)
+    grid = torch.randn(48, 32, 32) * 0.5
+    with torch.no_grad():
+        logits = scorer(hidden, grid)
+        with torch.autocast("cpu", dtype=torch.bfloat16):
+            logits_bf16 = scorer(hidden, grid.bfloat16())
+    state = {f"w_{k}": v.numpy() for k, v in scorer.state_dict().items()}
+    np.savez_compressed(HERE / "card_scorer.npz", hidden=hidden.numpy(), grid=grid.numpy(), logits=logits.numpy(),
+                        logits_bf16=logits_bf16.float().numpy(), **state)
+
+
+def make_candidate_scorer() -> None:
+    """``CandidateScorer.forward`` (rummy pointer head): a draw call (with taken counts) and a play call."""
+
+    from cardgym.games.rummy.cards import NO_CARD
+    from cardgym.games.rummy.model import CandidateScorer
+
+    torch.manual_seed(61)
+    scorer = CandidateScorer(256, 32, 64)
+    with torch.no_grad():
+        scorer.norm.weight.uniform_(0.5, 1.5)
+        for bias in (scorer.norm.bias, scorer.query.bias, scorer.hidden.bias, scorer.out.bias):
+            bias.normal_(0.0, 0.1)
+    scorer.eval()
+    rng = np.random.default_rng(62)
+    rows, width, listed = 12, 40, 13  # 40 candidates: more than one warp's worth of lanes
+    hidden = torch.randn(rows, 256)
+    grid = torch.randn(rows, 52, 32) * 0.5
+    kind = rng.integers(0, 7, (rows, width))
+    cards = np.full((rows, width, listed), NO_CARD, dtype=np.int64)
+    target = np.full((rows, width, listed), NO_CARD, dtype=np.int64)
+    for r in range(rows):
+        for c in range(width):
+            n_cards = rng.integers(0, listed + 1)
+            cards[r, c, :n_cards] = rng.integers(0, 52, n_cards)  # repeats allowed: they count twice
+            if rng.random() < 0.3:
+                n_target = rng.integers(1, 6)
+                target[r, c, :n_target] = rng.integers(0, 52, n_target)
+    taken = (rng.random((rows, width, 52)) < 0.1) * rng.integers(1, 3, (rows, width, 52))
+    out = {}
+    with torch.no_grad():
+        for name, extra in (("draw", torch.from_numpy(taken).to(torch.int8)), ("play", None)):
+            logits = scorer(hidden, grid, torch.from_numpy(kind), torch.from_numpy(cards).to(torch.int8),
+                            torch.from_numpy(target).to(torch.int8), extra)
+            out[f"{name}_logits"] = logits.numpy()
+    state = {f"w_{k}": v.numpy() for k, v in scorer.state_dict().items()}
+    np.savez_compressed(HERE / "candidate_scorer.npz", hidden=hidden.numpy(), grid=grid.numpy(), kind=kind,
+                        cards=cards.astype(np.int8), target=target.astype(np.int8), taken=taken.astype(np.int8),
+                        **out, **state)
+
+
 def main() -> None:
+    only = set(sys.argv[1:])
+    if only:
+        for name in sorted(only):
+            globals()[f"make_{name}"]()
+        return
     torch.manual_seed(0)
     streams = plump_streams(48, seed=0)
     padded, lengths = pad(streams)
@@ -314,6 +428,9 @@ def main() -> None:
     make_ppo()
     make_gae()
     make_value_loss()
+    make_piquet_bags()
+    make_card_scorer()
+    make_candidate_scorer()
     for path in sorted(HERE.glob("*.npz")):
         print(f"{path.name}: {path.stat().st_size / 1024:.0f} KiB")
 

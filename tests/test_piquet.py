@@ -1,0 +1,184 @@
+"""The piquet field lookup (cardgym/games/piquet/model.py:255-264, 323-345).
+
+CPU: the oracle against the reference's own ``_onehot_bags`` outputs (tests/golden/piquet_bags.npz),
+the host module's field layout against the oracle's, and the C ABI's argument checks.
+GPU: ``cg_onehot_bags`` against the same golden outputs in fp32, bf16 and fp16 (vector and
+scalar paths), repeated rows counted once, out-of-range ids flagged, strided token rows.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import piquet as opiquet
+from tests.conftest import load_golden
+from tests.golden.make_golden import PIQUET_BAG_WIDTHS, piquet_bag_tables
+
+ULP = {"bf16": 2.0 ** -8, "fp16": 2.0 ** -11}
+TORCH = {"fp32": torch.float32, "bf16": torch.bfloat16, "fp16": torch.float16}
+
+
+def _close_to_golden(got: np.ndarray, want: np.ndarray, storage: str) -> None:
+    """fp32: a few ulp of fp32 (summation order). bf16/fp16: at most one ulp of the storage
+    type, and nearly everything identical (only sums within an fp32 rounding of a midpoint differ)."""
+
+    if storage == "fp32":
+        np.testing.assert_allclose(got, want, atol=1e-6, rtol=0)
+        return
+    diff = np.abs(got.astype(np.float64) - want.astype(np.float64))
+    scale = np.maximum(np.abs(want.astype(np.float64)), 2.0 ** -14)
+    assert (diff <= ULP[storage] * scale + 1e-12).all()
+    assert (diff == 0).mean() > 0.99
+
+
+@pytest.mark.parametrize("name", sorted(PIQUET_BAG_WIDTHS))
+@pytest.mark.parametrize("storage", ("fp32", "bf16", "fp16"))
+def test_oracle_matches_the_reference_lookup(name, storage):
+    data = load_golden("piquet_bags")
+    tables = piquet_bag_tables(PIQUET_BAG_WIDTHS[name], int(data["seed"]))
+    sums = opiquet.field_sums(data["tokens"].astype(np.int64), tables, storage)
+    for part, got in zip(("fields", "ple", "values"), sums):
+        _close_to_golden(got, data[f"{name}_{storage}_{part}"], storage)
+
+
+def test_repeated_rows_count_once_in_the_oracle():
+    tables = [np.ones((opiquet.ROWS, 3), dtype=np.float32)]
+    ids = np.array([[5, 5, 7], [1, 2, 3]], dtype=np.int64)
+    (sums,) = opiquet.onehot_bags(ids, tables)
+    assert sums[:, 0].tolist() == [2.0, 3.0]
+
+
+def test_host_field_layout_matches_the_oracle():
+    from card_playing_gym_b200 import piquet
+
+    assert piquet.FIELD_VOCAB == opiquet.FIELD_VOCAB
+    assert piquet.field_offsets() == opiquet.OFFSETS.tolist()
+    assert piquet.FIELD_ROWS == opiquet.ROWS
+
+
+def test_bags_argument_checks():
+    from card_playing_gym_b200 import _native as nat
+
+    with pytest.raises(nat.NativeError, match="fields"):
+        nat.call("cg_onehot_bags", None, nat.CG_I64, 4, 40, 40, None, None, nat.CG_F32, 10, 8, None, None)
+    with pytest.raises(nat.NativeError, match="stride"):
+        nat.call("cg_onehot_bags", None, nat.CG_I64, 4, 2, 3, None, None, nat.CG_F32, 10, 8, None, None)
+    with pytest.raises(nat.NativeError, match="dtype"):
+        nat.call("cg_onehot_bags", None, nat.CG_I64, 4, 3, 3, None, None, 7, 10, 8, None, None)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", sorted(PIQUET_BAG_WIDTHS))
+@pytest.mark.parametrize("storage", ("fp32", "bf16", "fp16"))
+def test_field_lookup_matches_the_reference(name, storage):
+    from card_playing_gym_b200 import _native as nat
+    from card_playing_gym_b200.piquet import PiquetFieldLookup, onehot_bags
+
+    data = load_golden("piquet_bags")
+    tables = [torch.from_numpy(t).cuda() for t in piquet_bag_tables(PIQUET_BAG_WIDTHS[name], int(data["seed"]))]
+    tokens = torch.from_numpy(data["tokens"]).cuda()  # int16, the collector's storage
+    assert nat.fault_status() == 0
+    lookup = PiquetFieldLookup(*[t.to(TORCH[storage]) for t in tables])
+    sums = lookup(tokens)
+    for part, got in zip(("fields", "ple", "values"), sums):
+        _close_to_golden(got.float().cpu().numpy(), data[f"{name}_{storage}_{part}"], storage)
+    # The reference's call form: offset ids in, one list of sums out; int64 ids give the same sums.
+    ids = tokens[:, : opiquet.NUM_FIELDS].long() + torch.tensor(opiquet.OFFSETS, device="cuda")
+    again = onehot_bags(ids, [t.to(TORCH[storage]) for t in tables])
+    for a, b in zip(sums, again):
+        assert torch.equal(a, b)
+    assert nat.fault_status() == 0
+
+
+@pytest.mark.gpu
+def test_field_lookup_under_autocast_uses_the_autocast_dtype():
+    from card_playing_gym_b200.piquet import onehot_bags
+
+    data = load_golden("piquet_bags")
+    tables = [torch.from_numpy(t).cuda() for t in piquet_bag_tables(PIQUET_BAG_WIDTHS["wide"], int(data["seed"]))]
+    ids = torch.from_numpy(data["tokens"][:, : opiquet.NUM_FIELDS].astype(np.int64) + opiquet.OFFSETS).cuda()
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        sums = onehot_bags(ids, tables)
+    assert all(s.dtype == torch.bfloat16 for s in sums)
+    for part, got in zip(("fields", "ple", "values"), sums):
+        _close_to_golden(got.float().cpu().numpy(), data[f"wide_bf16_{part}"], "bf16")
+
+
+@pytest.mark.gpu
+def test_field_lookup_counts_repeated_rows_once_and_flags_bad_ids():
+    from card_playing_gym_b200 import _native as nat
+    from card_playing_gym_b200.piquet import onehot_bags
+
+    table = torch.arange(40 * 8, dtype=torch.float32, device="cuda").view(40, 8) / 64
+    ids = torch.tensor([[3, 3, 3, 9], [0, 1, 2, 39]], device="cuda")
+    (sums,) = onehot_bags(ids, [table])
+    want = torch.stack([table[3] + table[9], table[0] + table[1] + table[2] + table[39]])
+    assert torch.equal(sums, want)
+    assert nat.fault_status() == 0
+    for bad in (40, -1, 1 << 40):
+        onehot_bags(torch.tensor([[1, bad]], device="cuda"), [table])
+        assert nat.fault_status() == 0x210
+
+
+@pytest.mark.gpu
+def test_field_lookup_at_piquet_scale_matches_the_oracle():
+    """A wave's worth of tokens (4,096) against the full-width tables (d 256, PLE 16 x 64, values 8 x 64)."""
+
+    from card_playing_gym_b200.piquet import PiquetFieldLookup
+
+    rng = np.random.default_rng(5)
+    tokens = np.zeros((4096, 64), dtype=np.int64)
+    for field, vocab in enumerate(opiquet.FIELD_VOCAB):
+        tokens[:, field] = rng.integers(0, vocab, tokens.shape[0])
+    tables = [(rng.standard_normal((opiquet.ROWS, w)) * 0.02).astype(np.float32) for w in (256, 1024, 512)]
+    lookup = PiquetFieldLookup(*[torch.from_numpy(t).cuda().to(torch.bfloat16) for t in tables])
+    got = lookup(torch.from_numpy(tokens).cuda())
+    sample = slice(0, 4096, 37)
+    want = opiquet.field_sums(tokens[sample], tables, "bf16")
+    for g, w in zip(got, want):
+        _close_to_golden(g[sample].float().cpu().numpy(), w.astype(np.float32), "bf16")
+
+
+def _scorer_weights(data: dict) -> dict:
+    return {k[2:]: v for k, v in data.items() if k.startswith("w_")}
+
+
+def test_card_scorer_oracle_matches_the_reference():
+    data = load_golden("card_scorer")
+    got = opiquet.card_scorer(data["hidden"], data["grid"], _scorer_weights(data))
+    np.testing.assert_allclose(got, data["logits"], atol=1e-6, rtol=0)
+
+
+@pytest.mark.gpu
+def test_card_scorer_matches_the_reference():
+    from card_playing_gym_b200.piquet import CardScorer
+
+    data = load_golden("card_scorer")
+    scorer = CardScorer(_scorer_weights(data))
+    hidden = torch.from_numpy(data["hidden"]).cuda()
+    grid = torch.from_numpy(data["grid"]).cuda()
+    logits = scorer(hidden, grid).cpu().numpy()
+    np.testing.assert_allclose(logits, data["logits"], atol=2e-6, rtol=0)
+    # A bf16 grid (the card grid's output under autocast): the kernel's arithmetic stays fp32,
+    # so against the reference's fp32 logits it is no worse than the reference's own bf16 autocast.
+    half = scorer(hidden, grid.bfloat16()).cpu().numpy()
+    want = opiquet.card_scorer(data["hidden"], grid.bfloat16().float().cpu().numpy(), _scorer_weights(data))
+    np.testing.assert_allclose(half, want, atol=2e-6, rtol=0)
+    assert np.abs(half - data["logits"]).max() <= np.abs(data["logits_bf16"] - data["logits"]).max()
+
+
+@pytest.mark.gpu
+def test_card_scorer_at_wave_size_matches_the_oracle():
+    from card_playing_gym_b200.piquet import CardScorer
+
+    data = load_golden("card_scorer")
+    weights = _scorer_weights(data)
+    rng = np.random.default_rng(8)
+    hidden = rng.standard_normal((4096, 256)).astype(np.float32)
+    grid = (rng.standard_normal((4096, 32, 32)) * 0.5).astype(np.float32)
+    logits = CardScorer(weights)(torch.from_numpy(hidden).cuda(), torch.from_numpy(grid).cuda()).cpu().numpy()
+    sample = slice(0, 4096, 29)
+    np.testing.assert_allclose(logits[sample], opiquet.card_scorer(hidden[sample], grid[sample], weights), atol=2e-6,
+                               rtol=0)

@@ -1,0 +1,74 @@
+"""The rummy candidate pointer head (cardgym/games/rummy/model.py:292-357).
+
+CPU: the oracle against the reference's own ``CandidateScorer`` outputs (tests/golden/candidate_scorer.npz,
+a draw call with taken counts and a play call without). GPU: ``cg_candidate_scorer`` against the
+same outputs (40 candidates per decision: more than one warp of lanes), bad ids flagged.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import rummy as orummy
+from tests.conftest import load_golden
+
+
+def _weights(data: dict) -> dict:
+    return {k[2:]: v for k, v in data.items() if k.startswith("w_")}
+
+
+def _inputs(data: dict, head: str):
+    taken = data["taken"].astype(np.float64) if head == "draw" else None
+    return (data["hidden"], data["grid"], data["kind"].astype(np.int64), data["cards"].astype(np.int64),
+            data["target"].astype(np.int64), taken)
+
+
+@pytest.mark.parametrize("head", ("draw", "play"))
+def test_oracle_matches_the_reference_scorer(head):
+    data = load_golden("candidate_scorer")
+    got = orummy.candidate_scorer(*_inputs(data, head), _weights(data))
+    np.testing.assert_allclose(got, data[f"{head}_logits"], atol=1e-6, rtol=0)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("head", ("draw", "play"))
+def test_candidate_scorer_matches_the_reference(head):
+    from card_playing_gym_b200 import _native as nat
+    from card_playing_gym_b200.rummy import CandidateScorer
+
+    data = load_golden("candidate_scorer")
+    scorer = CandidateScorer(_weights(data))
+    hidden, grid, kind, cards, target, taken = _inputs(data, head)
+    cuda = lambda a: None if a is None else torch.from_numpy(a).cuda()  # noqa: E731
+    assert nat.fault_status() == 0
+    logits = scorer(cuda(hidden), cuda(grid), cuda(kind), cuda(data["cards"]), cuda(data["target"]),
+                    None if taken is None else cuda(data["taken"]))
+    np.testing.assert_allclose(logits.cpu().numpy(), data[f"{head}_logits"], atol=3e-6, rtol=0)
+    # bf16 grid: against the oracle on the same rounded grid
+    half = scorer(cuda(hidden), cuda(grid).bfloat16(), cuda(kind), cuda(cards), cuda(target),
+                  None if taken is None else cuda(taken))
+    want = orummy.candidate_scorer(hidden, cuda(grid).bfloat16().float().cpu().numpy(), kind, cards, target, taken,
+                                   _weights(data))
+    np.testing.assert_allclose(half.cpu().numpy(), want, atol=3e-6, rtol=0)
+    assert nat.fault_status() == 0
+
+
+@pytest.mark.gpu
+def test_candidate_scorer_flags_bad_ids():
+    from card_playing_gym_b200 import _native as nat
+    from card_playing_gym_b200.rummy import CandidateScorer
+
+    data = load_golden("candidate_scorer")
+    scorer = CandidateScorer(_weights(data))
+    hidden, grid, kind, cards, target, _ = _inputs(data, "play")
+    cuda = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    for field, value, code in (("cards", 53, 0x220), ("cards", -1, 0x220), ("kind", 7, 0x221)):
+        bad_cards, bad_kind = cards.copy(), kind.copy()
+        if field == "cards":
+            bad_cards[1, 2, 0] = value
+        else:
+            bad_kind[1, 2] = value
+        scorer(cuda(hidden), cuda(grid), cuda(bad_kind), cuda(bad_cards), cuda(target))
+        assert nat.fault_status() == code
