@@ -72,6 +72,8 @@ def parse_args(argv=None):
     parser.add_argument("--ppo-steps", type=int, default=20)
     parser.add_argument("--piquet-steps", type=int, default=20,
                         help="waves of the piquet-scale decode leg (8,192 two-player deals); 0 skips it")
+    parser.add_argument("--pointer-steps", type=int, default=20,
+                        help="waves of the piquet and rummy-style pointer-head legs; 0 skips them")
     return parser.parse_args(argv)
 
 
@@ -307,6 +309,127 @@ def run_piquet_scale(args, device, rank: int, world_size: int) -> dict:
                                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
                                "algorithmic_bytes_per_launch": algorithmic, "mean_launch_ms": mean_ms},
     }
+
+
+def run_pointer_wave(args, device, rank: int, world_size: int, kind: str) -> dict:
+    """A decode wave through the one-hot field lookup, Trunk.condition, the ragged trunk and a
+    pointer head with masked sampling.
+
+    piquet: 8,192 two-player deals (16,384 KV rows, all decoded), lengths U[32, 512], trunk
+      d256/16L/8-2/d_ff 512, piquet field tables (32 fields, 964 rows), one decision per deal
+      scored by CardScorer over its 32 cards.
+    rummy: 8,192 slots, half of them decoded per wave through gathered rows (the continuous
+      collector's form), lengths U[8, 384], trunk d256/8L/8-2/d_ff 768, one decision per three
+      decoded rows scored by CandidateScorer over U[1, 64] candidates (padded to the wave's max).
+    The card-grid features the heads read are synthetic (the card grid is not on this path)."""
+
+    import torch
+    import torch.distributed as dist
+
+    from card_playing_gym_b200 import _native as nat
+    from card_playing_gym_b200.config import PIQUET_SCALE, PlumpModelConfig, synthetic_plump_actor_state
+    from card_playing_gym_b200.piquet import FIELD_ROWS, FIELD_VOCAB, CardScorer, PiquetFieldLookup
+    from card_playing_gym_b200.piquet import forward_ragged as piquet_forward
+    from card_playing_gym_b200.rummy import NO_CARD, CandidateScorer
+    from card_playing_gym_b200.sampling import masked_sample
+    from card_playing_gym_b200.trunk import B200Trunk
+
+    rng = np.random.default_rng(3000 + 7919 * rank + (0 if kind == "piquet" else 1))
+    gen = torch.Generator(device=device).manual_seed(31 + rank)
+    if kind == "piquet":
+        config, slots, decoded, min_len, max_len = PIQUET_SCALE, 16384, 16384, 32, 512
+    else:
+        config = PlumpModelConfig(d_model=256, n_layers=8, n_heads=8, n_kv_heads=2, d_ff=768, per_layer_dim=64)
+        slots, decoded, min_len, max_len = 8192, 4096, 8, 384
+    trunk_cfg = config.trunk()
+    trunk = B200Trunk(trunk_cfg, synthetic_plump_actor_state(config, seed=5), device=device, precision="bf16")
+    d = trunk_cfg.d_model
+    widths = (d, trunk_cfg.ple_width, trunk_cfg.value_width)
+    tables = [torch.randn(FIELD_ROWS, w, device=device, generator=gen) * 0.02 for w in widths]
+    lookup = PiquetFieldLookup(*tables)
+    cache = trunk.new_cache(slots + 1, max_len + 1, torch.float16)
+    for pool in (cache.k_pool, cache.v_pool):
+        for layer in range(pool.shape[0]):
+            pool[layer].normal_(generator=gen)
+    lengths = rng.integers(min_len, max_len + 1, slots)
+    tokens = np.zeros((decoded, 1, 64), dtype=np.int16)
+    for field, vocab in enumerate(FIELD_VOCAB):
+        tokens[:, 0, field] = rng.integers(0, vocab, decoded)
+    rows = np.sort(rng.choice(slots, decoded, replace=False)) if decoded < slots else np.arange(slots)
+    positions = (lengths[rows] - 1).astype(np.int64)
+    dev_tokens = torch.from_numpy(tokens).to(device)
+    dev_rows = torch.from_numpy(rows.astype(np.int64)).to(device)
+    dev_positions = torch.from_numpy(positions).to(device)
+    offsets = torch.zeros(decoded, dtype=torch.int64, device=device)
+    score_state = lambda shapes: {n: rng.standard_normal(s).astype(np.float32) * 0.02 for n, s in shapes.items()}  # noqa: E731
+    if kind == "piquet":
+        decisions, cards = decoded // 2, 32
+        readout = torch.arange(0, decoded, 2, device=device)
+        scorer = CardScorer(score_state({
+            "query.weight": (64, d), "query.bias": (64,), "card.weight": (64, 32), "card_id.weight": (32, 64),
+            "norm.weight": (64,), "norm.bias": (64,), "hidden.weight": (64, 64), "hidden.bias": (64,),
+            "out.weight": (1, 64), "out.bias": (1,)}), device=device)
+        grid = torch.randn(decisions, cards, 32, device=device, generator=gen).to(torch.bfloat16)
+        legal = torch.from_numpy(rng.random((decisions, cards)) < 0.4).to(device)
+        legal[:, 0] = True
+        width = cards
+        head = lambda hidden: scorer(hidden, grid)  # noqa: E731
+    else:
+        decisions = decoded // 3
+        readout = torch.from_numpy(np.sort(rng.choice(decoded, decisions, replace=False))).to(device)
+        counts = rng.integers(1, 65, decisions)
+        width = int(counts.max())
+        scorer = CandidateScorer(score_state({
+            "query.weight": (64, d), "query.bias": (64,), "card.weight": (64, 32), "target.weight": (64, 32),
+            "taken.weight": (64, 32), "card_id.weight": (52, 64), "target_id.weight": (52, 64),
+            "taken_id.weight": (52, 64), "kind.weight": (7, 64), "size.weight": (14, 64), "norm.weight": (64,),
+            "norm.bias": (64,), "hidden.weight": (64, 64), "hidden.bias": (64,), "out.weight": (1, 64),
+            "out.bias": (1,)}), device=device)
+        grid = torch.randn(decisions, 52, 32, device=device, generator=gen).to(torch.bfloat16)
+        cand_kind = torch.from_numpy(rng.integers(0, 7, (decisions, width))).to(device)
+        cand_cards = np.full((decisions, width, 13), NO_CARD, dtype=np.int64)
+        cand_cards[..., :3] = rng.integers(0, 52, (decisions, width, 3))
+        cand_cards[..., 1:3][rng.random((decisions, width)) < 0.7] = NO_CARD
+        cand_target = np.full((decisions, width, 13), NO_CARD, dtype=np.int64)
+        cand_cards, cand_target = torch.from_numpy(cand_cards).to(device), torch.from_numpy(cand_target).to(device)
+        legal = torch.from_numpy(np.arange(width)[None, :] < counts[:, None]).to(device)
+        head = lambda hidden: scorer(hidden, grid, cand_kind, cand_cards, cand_target)  # noqa: E731
+    uniforms = torch.from_numpy(rng.random(decisions)).to(device)
+
+    def step():
+        hidden = piquet_forward(trunk, lookup, dev_tokens, dev_positions, cache, offsets, span=max_len + 1,
+                                rows=dev_rows)
+        logits = head(hidden.index_select(0, readout))
+        return masked_sample(logits, legal, uniforms)
+
+    for _ in range(3):
+        step()
+    if world_size > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    stream = torch.cuda.current_stream(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.pointer_steps):
+        step()
+    end.record(stream)
+    torch.cuda.synchronize(device)
+    ms = start.elapsed_time(end) / args.pointer_steps
+    if world_size > 1:
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    desc = {
+        "piquet": (f"piquet decode wave: {decisions} deals ({decoded} KV rows, 1 token/row), lengths U[{min_len},{max_len}],"
+                   " fp16 KV, one-hot field lookup (32 fields, 964 rows) fused into the trunk d256/16L/8-2/d_ff 512 -> "
+                   "CardScorer over 32 cards -> masked sampling (grid features synthetic)"),
+        "rummy": (f"rummy-style continuous wave: {slots} slots, {decoded} gathered rows decoded (1 token/row), lengths "
+                  f"U[{min_len},{max_len}], fp16 KV, one-hot field lookup fused into the trunk d256/8L/8-2/d_ff 768 -> "
+                  f"CandidateScorer over U[1,64] candidates (padded to {width}) -> masked sampling (grid features "
+                  "synthetic)"),
+    }[kind]
+    return {"workload": desc, "value": world_size * decisions / (ms / 1000.0), "unit": "decisions/s",
+            "rows_per_s": world_size * decoded / (ms / 1000.0), "ms_per_step": ms, "steps": args.pointer_steps}
 
 
 # ---------------------------------------------------------------------------------------------
@@ -569,6 +692,10 @@ def run_b200(args) -> int:
     e2e_value = world_size * games * args.steps / (e2e_ms / 1000.0)
     ppo_line = run_ppo(args, device, rank, world_size) if args.ppo_decisions > 0 else None
     piquet_line = run_piquet_scale(args, device, rank, world_size) if args.piquet_steps > 0 else None
+    pointer_lines = {}
+    if args.pointer_steps > 0:
+        pointer_lines["piquet_pointer"] = run_pointer_wave(args, device, rank, world_size, "piquet")
+        pointer_lines["rummy_style"] = run_pointer_wave(args, device, rank, world_size, "rummy")
 
     if rank == 0:
         head_dim = RL_V6.trunk().head_dim
@@ -628,6 +755,7 @@ def run_b200(args) -> int:
             line["ppo"] = ppo_line
         if piquet_line is not None:
             line["piquet_scale"] = piquet_line
+        line.update(pointer_lines)
         if world_size == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args, args.cpu_seconds)
         print(json.dumps(line), flush=True)

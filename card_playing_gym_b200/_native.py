@@ -100,6 +100,9 @@ _SIGNATURES: dict[str, tuple[type, list]] = {
     "cg_trunk_prepare": (_i32, [ctypes.POINTER(TrunkDims), _p, _p]),
     "cg_plump_embed": (_i32, [ctypes.POINTER(PlumpSchemaC), _p, _i32, _p, _i32, _i64, _p, _p]),
     "cg_onehot_bags": (_i32, [_p, _i32, _i64, _i64, _i32, ctypes.POINTER(_i64), _p, _i32, _i64, _i32, _p, _p]),
+    "cg_bags_forward_ragged": (_i32, [ctypes.POINTER(TrunkDims), _p, _p, _i32, _i64, _i32, ctypes.POINTER(_i64), _p,
+                                      _i64, _p, _i64, _i32, _p, _p, _p, _i32, _p, _p, _i32, _i64, _i32, _i32, _p, _i64,
+                                      _p, _p]),
     "cg_card_scorer": (_i32, [ctypes.POINTER(CardScorerWeights), _p, _i64, _p, _i32, _p, _p]),
     "cg_candidate_scorer": (_i32, [ctypes.POINTER(CandidateScorerWeights), _p, _i64, _i32, _i32, _p, _i32, _p, _p, _p,
                                    _p, _p, _p]),

@@ -15,9 +15,22 @@
 // One warp per token: lanes resolve the token's field ids (one field per lane), drop
 // repeats with __match_any_sync, then stride the row in 16-byte units; the table (a few MB)
 // stays L2-resident, every unit is a coalesced 512-byte warp read per selected row.
-#include "common.cuh"
+#include "lookup_out.cuh"
+#include "trunk.h"
 
 namespace cg {
+
+int forward_ragged_impl(const cg_trunk_dims* dims_p, const void* blob, const float* x_in, const float* ple,
+                        const float* values, int64_t batch, int steps, const int64_t* positions,
+                        const int64_t* readout_offsets, const int64_t* rows, int span, void* k_pool, void* v_pool,
+                        int kv_dtype, int64_t capacity, int max_len, int precision, void* workspace,
+                        int64_t workspace_bytes, float* hidden_out, cudaStream_t s, bool x_in_workspace,
+                        bool lookup_blocked);
+bool tc_layers_available(const cg_trunk_dims& dims);
+unsigned char* step_tc_scratch(const cg_trunk_dims& dims, int64_t batch, int steps, int precision, void* workspace);
+void tc_input_streams(const cg_trunk_dims& dims, int64_t batch, int steps, unsigned char* scratch, float** x_blk,
+                      float** ple_blk, float** val_blk, int64_t* ntiles);
+
 namespace {
 
 constexpr int kBagThreads = 256;
@@ -186,6 +199,48 @@ __global__ void __launch_bounds__(kBagThreads) onehot_bags_scalar_kernel(const _
   }
 }
 
+// fp32 tables into the trunk's tile-blocked input streams (the first dense kernel conditions
+// them), with an optional fp32 addend [n, d] on the x columns (the reference adds the card-grid
+// summary to the field sums before Trunk.condition).
+__global__ void __launch_bounds__(kBagThreads) onehot_bags_blocked_kernel(const __grid_constant__ BagArgs a,
+                                                                           const EmbedOut dest,
+                                                                           const float* __restrict__ x_add) {
+  constexpr int kAhead = 8;
+  __shared__ const unsigned char* rows_s[kBagThreads / 32][32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t token = (static_cast<int64_t>(blockIdx.x) * kBagThreads + threadIdx.x) >> 5;
+  if (token >= a.n) return;
+  int64_t row;
+  const unsigned keep = bag_rows(a, token, lane, row);
+  const int64_t row_bytes = static_cast<int64_t>(a.width) * 4;
+  if ((keep >> lane) & 1u)
+    rows_s[w][__popc(keep & ((1u << lane) - 1u))] = static_cast<const unsigned char*>(a.table) + row * row_bytes;
+  __syncwarp();
+  const int nk = __popc(keep);
+  const int units = a.width / 4;
+  for (int u = lane; u < units; u += 32) {
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int k0 = 0; k0 < nk; k0 += kAhead) {
+      uint4 v[kAhead];
+#pragma unroll
+      for (int i = 0; i < kAhead; ++i)
+        if (k0 + i < nk) v[i] = __ldg(reinterpret_cast<const uint4*>(rows_s[w][k0 + i] + 16 * u));
+#pragma unroll
+      for (int i = 0; i < kAhead; ++i)
+        if (k0 + i < nk) BagUnit<float>::add(v[i], acc);
+    }
+    if (x_add && 4 * u < dest.d) {
+      const float4 e = __ldg(reinterpret_cast<const float4*>(x_add + token * dest.d) + u);
+      acc[0] += e.x;
+      acc[1] += e.y;
+      acc[2] += e.z;
+      acc[3] += e.w;
+    }
+    const LookupColumn col = lookup_column(dest, u);
+    col.base[(token >> 7) * col.tile_stride + (token & 127)] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+  }
+}
+
 template <typename T>
 int launch_bags(const BagArgs& a, cudaStream_t s) {
   const unsigned blocks = static_cast<unsigned>((a.n * 32 + kBagThreads - 1) / kBagThreads);
@@ -230,4 +285,56 @@ extern "C" int cg_onehot_bags(const void* ids, int ids_dtype, int64_t n_tokens, 
   if (table_dtype == CG_F32) return launch_bags<float>(a, s);
   if (table_dtype == CG_BF16) return launch_bags<__nv_bfloat16>(a, s);
   return launch_bags<__half>(a, s);
+}
+
+extern "C" int cg_bags_forward_ragged(const cg_trunk_dims* dims, const void* blob, const void* ids, int ids_dtype,
+                                      int64_t ids_stride, int fields, const int64_t* offsets, const float* table,
+                                      int64_t table_rows, const float* x_add, int64_t batch, int steps,
+                                      const int64_t* positions, const int64_t* readout_offsets, const int64_t* rows,
+                                      int span, void* k_pool, void* v_pool, int kv_dtype, int64_t capacity,
+                                      int max_len, int precision, void* workspace, int64_t workspace_bytes,
+                                      float* hidden_out, void* stream) {
+  using namespace cg;
+  CG_REQUIRE(dims, "cg_bags_forward_ragged: NULL trunk dims");
+  CG_REQUIRE(precision == CG_PREC_BF16 && tc_layers_available(*dims),
+             "cg_bags_forward_ragged: the fused lookup feeds the tensor-core layers (bf16 precision) only");
+  CG_REQUIRE(ids_dtype == CG_I16 || ids_dtype == CG_I32 || ids_dtype == CG_I64, "cg_bags_forward_ragged: bad id dtype");
+  CG_REQUIRE(fields >= 1 && fields <= 32, "cg_bags_forward_ragged: fields must be 1..32 (got %d)", fields);
+  CG_REQUIRE(ids_stride >= fields && table_rows >= 1, "cg_bags_forward_ragged: bad id stride or table");
+  if (batch == 0) return CG_OK;
+  CG_REQUIRE(ids && table && workspace && blob, "cg_bags_forward_ragged: NULL pointer");
+  CG_REQUIRE((reinterpret_cast<uintptr_t>(table) & 15) == 0 && (reinterpret_cast<uintptr_t>(x_add) & 15) == 0,
+             "cg_bags_forward_ragged: table and x_add must be 16-byte aligned");
+  const int64_t need = cg_trunk_step_workspace_bytes(dims, batch, steps, precision);
+  if (need < 0) return set_error(CG_ERR_ARGUMENT, "cg_bags_forward_ragged: bad trunk dims");
+  if (workspace_bytes < need)
+    return set_error(CG_ERR_WORKSPACE, "bags step workspace %lld < %lld bytes", (long long)workspace_bytes,
+                     (long long)need);
+  const cg_trunk_dims& d = *dims;
+  EmbedOut dest{};
+  dest.d = d.d_model;
+  dest.ple_w = d.n_layers * d.per_layer_dim;
+  dest.P = d.per_layer_dim;
+  dest.kvw = d.n_kv_heads * head_dim(d);
+  const int width = dest.d + dest.ple_w + value_layer_count(d) * dest.kvw;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  tc_input_streams(d, batch, steps, step_tc_scratch(d, batch, steps, precision, workspace), &dest.x_blk, &dest.ple_blk,
+                   &dest.val_blk, &dest.ntiles);
+  BagArgs a{};
+  a.ids = ids;
+  a.ids_dtype = ids_dtype;
+  a.n = batch * steps;
+  a.ids_stride = ids_stride;
+  a.fields = fields;
+  for (int f = 0; f < fields; ++f) a.offsets[f] = offsets ? offsets[f] : 0;
+  a.table = table;
+  a.rows = table_rows;
+  a.width = width;
+  const unsigned blocks = static_cast<unsigned>((a.n * 32 + kBagThreads - 1) / kBagThreads);
+  onehot_bags_blocked_kernel<<<blocks, kBagThreads, 0, s>>>(a, dest, x_add);
+  int rc;
+  if ((rc = check_launch("onehot_bags_blocked_kernel"))) return rc;
+  return forward_ragged_impl(dims, blob, nullptr, nullptr, nullptr, batch, steps, positions, readout_offsets, rows,
+                             span, k_pool, v_pool, kv_dtype, capacity, max_len, precision, workspace, workspace_bytes,
+                             hidden_out, s, false, true);
 }

@@ -6,6 +6,7 @@
 // Trunk.forward_ragged). One fused lookup reads a packed [field rows + pattern rows,
 // d | ple | value] table, so all three sums come from one pass over each token, with
 // no boolean-mask nonzero (the reference's host sync, model.py:143).
+#include "lookup_out.cuh"
 #include "trunk.h"
 
 namespace cg {
@@ -126,36 +127,6 @@ struct EmbedIds {
   uint8_t n_main, n_hand;
 };
 
-// Destination of the lookup sums: row-major [n, width], or the trunk's tile-blocked streams
-// (x_blk non-null): columns [0, d) -> x_blk, [d, d + L*P) -> ple_blk (per layer), the rest ->
-// val_blk (per value layer), each [.. tile][width/4][128 rows][4].
-struct EmbedOut {
-  float* rows;
-  float* x_blk;
-  float* ple_blk;
-  float* val_blk;
-  int d, ple_w, P, kvw;
-  int64_t ntiles;
-};
-
-// Blocked destination of float4 column c4 for tile 0, row 0, and the step from one tile to the
-// next: the token-independent part of store_lookup's address, computed once per column.
-struct LookupColumn {
-  float4* base;
-  int64_t tile_stride;
-};
-
-__device__ __forceinline__ LookupColumn lookup_column(const EmbedOut& o, int c4) {
-  int k = 4 * c4;
-  if (k < o.d) return {reinterpret_cast<float4*>(o.x_blk) + static_cast<int64_t>(k / 4) * 128, (o.d / 4) * 128};
-  if ((k -= o.d) < o.ple_w) {
-    const int layer = k / o.P, q = k - layer * o.P;
-    return {reinterpret_cast<float4*>(o.ple_blk) + (layer * o.ntiles * (o.P / 4) + q / 4) * 128, (o.P / 4) * 128};
-  }
-  k -= o.ple_w;
-  const int vl = k / o.kvw, q = k - vl * o.kvw;
-  return {reinterpret_cast<float4*>(o.val_blk) + (vl * o.ntiles * (o.kvw / 4) + q / 4) * 128, (o.kvw / 4) * 128};
-}
 
 
 // Shared memory of a sliced lookup CTA: two table slices, the row ids and the token rows.

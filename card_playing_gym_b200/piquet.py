@@ -136,3 +136,44 @@ class CardScorer:
         nat.call("cg_card_scorer", self.weights, nat.ptr(hidden), count, nat.ptr(grid), nat.DTYPE_CODES[grid.dtype],
                  nat.ptr(logits), nat.stream_handle(hidden.device))
         return logits
+
+
+def forward_ragged(trunk, lookup: PiquetFieldLookup, tokens: torch.Tensor, positions: torch.Tensor, cache,
+                   readout_offsets: torch.Tensor, span: int | None = None, rows: torch.Tensor | None = None,
+                   summary: torch.Tensor | None = None) -> torch.Tensor:
+    """``SequenceModel.forward_ragged`` (cardgym/nn/model.py:76-89) with the piquet field sums:
+    tokens [B, T, 64] -> (field sums + ``summary``, the card-grid summary [B, T, d] if given) ->
+    Trunk.condition -> the ragged trunk decode -> final-normed hidden [B, d] at each readout.
+
+    With a bf16 trunk the lookup writes straight into the first tensor-core layer's inputs
+    (``cg_bags_forward_ragged``); an fp32 trunk runs lookup, condition and decode as three calls.
+    """
+
+    batch, steps, _ = tokens.shape
+    if span is None:
+        span = int(positions.max()) + steps
+    span = min(span, cache.max_len)
+    if trunk.precision != "bf16":
+        fields, ple, values = lookup(tokens)
+        if summary is not None:
+            fields = fields + summary
+        x, ple, values = trunk.condition(fields, ple, values)
+        return trunk.forward_ragged(x, ple, values, cache, positions, readout_offsets, span=span, rows=rows)
+    flat = tokens.reshape(-1, tokens.shape[-1])
+    if flat.dtype not in nat.INDEX_CODES:
+        flat = flat.long()
+    flat = flat.contiguous()
+    table = lookup.table(torch.float32)
+    extra = None if summary is None else summary.reshape(-1, summary.shape[-1]).float().contiguous()
+    need = nat.query("cg_trunk_step_workspace_bytes", trunk.dims, batch, steps, nat.PRECISIONS[trunk.precision])
+    workspace = nat.Workspace.get(trunk.device, need)
+    hidden = torch.empty((batch, trunk.config.d_model), device=trunk.device)
+    offsets = (nat._i64 * NUM_FIELDS)(*lookup.offsets)
+    nat.call("cg_bags_forward_ragged", trunk.dims, nat.ptr(trunk.blob), nat.ptr(flat), nat.INDEX_CODES[flat.dtype],
+             flat.shape[1], NUM_FIELDS, offsets, nat.ptr(table), table.shape[0], nat.ptr(extra), batch, steps,
+             nat.ptr(positions.to(torch.int64).contiguous()), nat.ptr(readout_offsets.to(torch.int64).contiguous()),
+             nat.ptr(None if rows is None else rows.to(torch.int64).contiguous()), int(span), nat.ptr(cache.k_pool),
+             nat.ptr(cache.v_pool), nat.DTYPE_CODES[cache.dtype], cache.capacity, cache.max_len,
+             nat.PRECISIONS[trunk.precision], nat.ptr(workspace), workspace.numel(), nat.ptr(hidden),
+             nat.stream_handle(trunk.device))
+    return hidden

@@ -165,6 +165,19 @@ int cg_onehot_bags(const void* ids, int ids_dtype, int64_t n_tokens, int64_t ids
                    const int64_t* offsets, const void* table, int table_dtype, int64_t rows, int width, void* out,
                    void* stream);
 
+/* The one-hot field lookup fused into the ragged trunk decode (PiquetEmbedding.forward +
+ * SequenceModel.forward_ragged, nn/model.py:76-89; bf16 precision on the tensor-core layers
+ * only): the sums of an fp32 table [table_rows, d + ple + value] (plus x_add fp32 [B*T, d] on
+ * the x columns when non-NULL: the card-grid summary) go straight into the first dense
+ * kernel's inputs, which applies Trunk.condition. ids [B*T rows of ids_stride], as for
+ * cg_onehot_bags; the rest as cg_trunk_forward_ragged, with its step workspace. */
+int cg_bags_forward_ragged(const cg_trunk_dims* dims, const void* blob, const void* ids, int ids_dtype,
+                           int64_t ids_stride, int fields, const int64_t* offsets, const float* table,
+                           int64_t table_rows, const float* x_add, int64_t batch, int steps, const int64_t* positions,
+                           const int64_t* readout_offsets, const int64_t* rows, int span, void* k_pool, void* v_pool,
+                           int kv_dtype, int64_t capacity, int max_len, int precision, void* workspace,
+                           int64_t workspace_bytes, float* hidden_out, void* stream);
+
 /* ---------------------------------------------------------------------------------
  * Card pointer head (cardgym/games/piquet/model.py:348-363 `CardScorer.forward`, the
  * exchange and play heads of PiquetActor.policy_logits 399-411): one logit per card,

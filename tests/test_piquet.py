@@ -182,3 +182,52 @@ def test_card_scorer_at_wave_size_matches_the_oracle():
     sample = slice(0, 4096, 29)
     np.testing.assert_allclose(logits[sample], opiquet.card_scorer(hidden[sample], grid[sample], weights), atol=2e-6,
                                rtol=0)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("precision", ("bf16", "fp32"))
+def test_piquet_decode_with_the_fused_lookup_tracks_the_oracle(precision):
+    """Field sums + a card-grid summary -> Trunk.condition -> ragged decode, against the oracle
+    trunk fed with the oracle's field sums (d 256 piquet trunk, two layers, empty cache, four
+    one-token waves). bf16: the fused lookup writes the first tensor-core layer's inputs."""
+
+    import dataclasses
+
+    from card_playing_gym_b200.config import PIQUET_SCALE, synthetic_plump_actor_state
+    from card_playing_gym_b200.piquet import PiquetFieldLookup, forward_ragged
+    from card_playing_gym_b200.trunk import B200Trunk
+    from oracle.trunk import Cache, Precision, Trunk, TrunkShape, TrunkWeights, value_layers
+
+    config = dataclasses.replace(PIQUET_SCALE, n_layers=2)
+    state = synthetic_plump_actor_state(config, seed=33)
+    tc = config.trunk()
+    trunk = B200Trunk(tc, state, precision=precision)
+    shape = TrunkShape(d_model=tc.d_model, n_layers=tc.n_layers, n_heads=tc.n_heads, n_kv_heads=tc.n_kv_heads,
+                       d_ff=tc.d_ff, per_layer_dim=tc.per_layer_dim,
+                       value_layers=value_layers(tc.n_layers, config.value_embeddings))
+    prec = Precision(gemm="bf16", kv="fp16") if precision == "bf16" else Precision()
+    oracle = Trunk(TrunkWeights.from_state(state, shape), prec)
+    rng = np.random.default_rng(12)
+    batch, waves = 24, 4
+    tokens = np.zeros((batch, waves, 64), dtype=np.int64)
+    for field, vocab in enumerate(opiquet.FIELD_VOCAB):
+        tokens[..., field] = rng.integers(0, vocab, (batch, waves))
+    tables = [(rng.standard_normal((opiquet.ROWS, w)) * 0.02).astype(np.float32)
+              for w in (tc.d_model, tc.ple_width, tc.value_width)]
+    summary = (rng.standard_normal((batch, waves, tc.d_model)) * 0.05).astype(np.float32)
+    lookup = PiquetFieldLookup(*[torch.from_numpy(t).cuda() for t in tables])
+    kv = torch.float16 if precision == "bf16" else torch.float32
+    cache = trunk.new_cache(batch, waves + 1, kv)
+    ocache = Cache(shape.n_layers, batch, shape.n_kv_heads, waves + 1, shape.head_dim, prec)
+    offsets = np.zeros(batch, np.int64)
+    tol = 1e-2 if precision == "bf16" else 5e-5
+    for t in range(waves):
+        positions = np.full(batch, t, np.int64)
+        got = forward_ragged(trunk, lookup, torch.from_numpy(tokens[:, t:t + 1]).cuda(),
+                             torch.from_numpy(positions).cuda(), cache, torch.from_numpy(offsets).cuda(),
+                             summary=torch.from_numpy(summary[:, t:t + 1]).cuda()).cpu().numpy()
+        fields, ple, values = opiquet.field_sums(tokens[:, t:t + 1], tables)
+        x, ple, values = oracle.condition(fields + summary[:, t:t + 1], ple, values)
+        want = oracle.forward_ragged(x, ple, values, ocache, positions, offsets)
+        err = np.abs(got - want).max()
+        assert (err / np.abs(want).max() < tol) if precision == "bf16" else err < tol, (t, err)
