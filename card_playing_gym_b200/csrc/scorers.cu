@@ -43,11 +43,11 @@ __host__ __device__ inline ScorerSmem scorer_smem(int d, int width, int cards) {
   ScorerSmem s{};
   int at = 0;
   s.qT = at, at += d * kScorerDim;           // query weight transposed [d][dim]
-  s.cw = at, at += kScorerDim * width;       // card weight [dim][width]
+  s.cw = at, at += kScorerDim * width;       // card weight transposed [width][dim]
   s.idT = at, at += kScorerDim * 32;         // card ids transposed [dim][32] (cards <= 32, zero-padded)
   s.nw = at, at += kScorerDim;
   s.nb = at, at += kScorerDim;
-  s.hw = at, at += kScorerDim * kScorerDim;  // hidden weight [dim][dim]
+  s.hw = at, at += kScorerDim * kScorerDim;  // hidden weight transposed [in][out]
   s.hb = at, at += kScorerDim;
   s.ow = at, at += kScorerDim;
   s.h = at, at += kScorerWarps * d;          // per-warp hidden row
@@ -65,6 +65,92 @@ __device__ __forceinline__ float scorer_load(const void* p, int dtype, int64_t i
 
 __device__ __forceinline__ float scorer_gelu(float x) { return 0.5f * x * (1.f + erff(x * 0.70710678118654752f)); }
 
+// m[o] += sum_j W[o][j] x[j] (in j order) with W staged transposed, WT[j][o]: each j is 16
+// broadcast float4 reads feeding the 64 independent accumulators.
+template <int kW>
+__device__ __forceinline__ void project_add(const float* WT, const float (&x)[kW], int width, float (&m)[kScorerDim]) {
+#pragma unroll
+  for (int j = 0; j < kW; ++j) {
+    if (j < width) {
+      const float xj = x[j];
+#pragma unroll
+      for (int o = 0; o < kScorerDim; o += 4) {
+        const float4 wv = *reinterpret_cast<const float4*>(WT + j * kScorerDim + o);
+        m[o] = fmaf(wv.x, xj, m[o]);
+        m[o + 1] = fmaf(wv.y, xj, m[o + 1]);
+        m[o + 2] = fmaf(wv.z, xj, m[o + 2]);
+        m[o + 3] = fmaf(wv.w, xj, m[o + 3]);
+      }
+    }
+  }
+}
+
+// LayerNorm over the dim values in place (two passes, fp32, eps 1e-5).
+__device__ __forceinline__ void scorer_layer_norm(float (&m)[kScorerDim], const float* nw, const float* nb) {
+  float mean = 0.f;
+#pragma unroll
+  for (int o = 0; o < kScorerDim; ++o) mean += m[o];
+  mean *= 1.f / kScorerDim;
+  float var = 0.f;
+#pragma unroll
+  for (int o = 0; o < kScorerDim; ++o) {
+    const float t = m[o] - mean;
+    var = fmaf(t, t, var);
+  }
+  const float rstd = rsqrtf(var * (1.f / kScorerDim) + 1e-5f);
+#pragma unroll
+  for (int o = 0; o < kScorerDim; ++o) m[o] = (m[o] - mean) * rstd * nw[o] + nb[o];
+}
+
+// out(GELU(hidden(m))) with the hidden weight staged transposed (hwT[k][o]): sixteen hidden
+// units at a time, each summed over k in order; the output dot in unit order.
+__device__ __forceinline__ float scorer_head(const float (&m)[kScorerDim], const float* hwT, const float* hb,
+                                             const float* ow) {
+  float out = 0.f;
+#pragma unroll 1
+  for (int o0 = 0; o0 < kScorerDim; o0 += 16) {
+    float h[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) h[j] = 0.f;
+#pragma unroll
+    for (int k = 0; k < kScorerDim; ++k) {
+      const float mk = m[k];
+#pragma unroll
+      for (int j = 0; j < 16; j += 4) {
+        const float4 wv = *reinterpret_cast<const float4*>(hwT + k * kScorerDim + o0 + j);
+        h[j] = fmaf(wv.x, mk, h[j]);
+        h[j + 1] = fmaf(wv.y, mk, h[j + 1]);
+        h[j + 2] = fmaf(wv.z, mk, h[j + 2]);
+        h[j + 3] = fmaf(wv.w, mk, h[j + 3]);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) out = fmaf(ow[o0 + j], scorer_gelu(h[j] + hb[o0 + j]), out);
+  }
+  return out;
+}
+
+// The query row of one decision: lanes own outputs lane and lane + 32, four partial sums each.
+__device__ __forceinline__ void scorer_query(const float* qT, const float* hrow, int d, const float* bias, int lane,
+                                             float* qrow) {
+  float a[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+  int k = 0;
+  for (; k + 4 <= d; k += 4) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float hk = hrow[k + u];
+      a[0][u] = fmaf(qT[(k + u) * kScorerDim + lane], hk, a[0][u]);
+      a[1][u] = fmaf(qT[(k + u) * kScorerDim + lane + 32], hk, a[1][u]);
+    }
+  }
+  for (; k < d; ++k) {
+    a[0][0] = fmaf(qT[k * kScorerDim + lane], hrow[k], a[0][0]);
+    a[1][0] = fmaf(qT[k * kScorerDim + lane + 32], hrow[k], a[1][0]);
+  }
+  qrow[lane] = bias[lane] + ((a[0][0] + a[0][1]) + (a[0][2] + a[0][3]));
+  qrow[lane + 32] = bias[lane + 32] + ((a[1][0] + a[1][1]) + (a[1][2] + a[1][3]));
+}
+
 __global__ void __launch_bounds__(kScorerWarps * 32) card_scorer_kernel(const cg_card_scorer_weights w, const float* hidden,
                                                                          int64_t n, const void* grid, int grid_dtype,
                                                                          float* logits) {
@@ -77,7 +163,10 @@ __global__ void __launch_bounds__(kScorerWarps * 32) card_scorer_kernel(const cg
     const int o = i / d, k = i - o * d;
     sc_smem[L.qT + k * kScorerDim + o] = w.query_w[i];
   }
-  for (int i = tid; i < kScorerDim * width; i += blockDim.x) sc_smem[L.cw + i] = w.card_w[i];
+  for (int i = tid; i < kScorerDim * width; i += blockDim.x) {
+    const int o = i / width, j = i - o * width;
+    sc_smem[L.cw + j * kScorerDim + o] = w.card_w[i];  // transposed [width][dim]
+  }
   for (int i = tid; i < kScorerDim * 32; i += blockDim.x) {
     const int o = i / 32, c = i - o * 32;
     sc_smem[L.idT + i] = c < cards ? w.card_id[c * kScorerDim + o] : 0.f;
@@ -88,7 +177,10 @@ __global__ void __launch_bounds__(kScorerWarps * 32) card_scorer_kernel(const cg
     sc_smem[L.hb + i] = w.hidden_b[i];
     sc_smem[L.ow + i] = w.out_w[i];
   }
-  for (int i = tid; i < kScorerDim * kScorerDim; i += blockDim.x) sc_smem[L.hw + i] = w.hidden_w[i];
+  for (int i = tid; i < kScorerDim * kScorerDim; i += blockDim.x) {
+    const int o = i / kScorerDim, k = i - o * kScorerDim;
+    sc_smem[L.hw + k * kScorerDim + o] = w.hidden_w[i];  // transposed [k][o]
+  }
   pdl_wait();
   pdl_trigger();
   __syncthreads();
@@ -98,23 +190,10 @@ __global__ void __launch_bounds__(kScorerWarps * 32) card_scorer_kernel(const cg
 
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * kScorerWarps + warp; i < n;
        i += static_cast<int64_t>(gridDim.x) * kScorerWarps) {
-    // Query row: lanes own outputs lane and lane + 32; sums over k in order.
     __syncwarp();
     for (int k = lane; k < d; k += 32) hrow[k] = hidden[i * d + k];
     __syncwarp();
-    float q0 = w.query_b[lane], q1 = w.query_b[lane + 32];
-    {
-      float a0 = 0.f, a1 = 0.f;
-      for (int k = 0; k < d; ++k) {
-        const float hk = hrow[k];
-        a0 = fmaf(sc_smem[L.qT + k * kScorerDim + lane], hk, a0);
-        a1 = fmaf(sc_smem[L.qT + k * kScorerDim + lane + 32], hk, a1);
-      }
-      q0 += a0;
-      q1 += a1;
-    }
-    qrow[lane] = q0;
-    qrow[lane + 32] = q1;
+    scorer_query(sc_smem + L.qT, hrow, d, w.query_b, lane, qrow);
     __syncwarp();
 
     const bool live = lane < cards;
@@ -126,49 +205,12 @@ __global__ void __launch_bounds__(kScorerWarps * 32) card_scorer_kernel(const cg
     // mixed = query + card(grid) + card_id, the reference's order of the two adds.
     float m[kScorerDim];
 #pragma unroll
-    for (int o = 0; o < kScorerDim; ++o) {
-      float acc = 0.f;
-      const float* row = sc_smem + L.cw + o * width;
+    for (int o = 0; o < kScorerDim; ++o) m[o] = 0.f;
+    project_add(sc_smem + L.cw, g, width, m);
 #pragma unroll
-      for (int k = 0; k < kScorerMaxWidth; ++k)
-        if (k < width) acc = fmaf(row[k], g[k], acc);
-      m[o] = (qrow[o] + acc) + sc_smem[L.idT + o * 32 + c];
-    }
-    // LayerNorm over the card's dim values (two passes, fp32).
-    float mean = 0.f;
-#pragma unroll
-    for (int o = 0; o < kScorerDim; ++o) mean += m[o];
-    mean *= 1.f / kScorerDim;
-    float var = 0.f;
-#pragma unroll
-    for (int o = 0; o < kScorerDim; ++o) {
-      const float t = m[o] - mean;
-      var = fmaf(t, t, var);
-    }
-    const float rstd = rsqrtf(var * (1.f / kScorerDim) + 1e-5f);
-#pragma unroll
-    for (int o = 0; o < kScorerDim; ++o) m[o] = (m[o] - mean) * rstd * sc_smem[L.nw + o] + sc_smem[L.nb + o];
-    // Hidden layer + GELU + output dot, four hidden units at a time.
-    float out = 0.f;
-#pragma unroll 1
-    for (int o = 0; o < kScorerDim; o += 4) {
-      float h[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) h[j] = 0.f;
-#pragma unroll
-      for (int k = 0; k < kScorerDim; k += 4) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float4 wv = *reinterpret_cast<const float4*>(sc_smem + L.hw + (o + j) * kScorerDim + k);
-          h[j] = fmaf(wv.x, m[k], h[j]);
-          h[j] = fmaf(wv.y, m[k + 1], h[j]);
-          h[j] = fmaf(wv.z, m[k + 2], h[j]);
-          h[j] = fmaf(wv.w, m[k + 3], h[j]);
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < 4; ++j) out = fmaf(sc_smem[L.ow + o + j], scorer_gelu(h[j] + sc_smem[L.hb + o + j]), out);
-    }
+    for (int o = 0; o < kScorerDim; ++o) m[o] = (qrow[o] + m[o]) + sc_smem[L.idT + o * 32 + c];
+    scorer_layer_norm(m, sc_smem + L.nw, sc_smem + L.nb);
+    const float out = scorer_head(m, sc_smem + L.hw, sc_smem + L.hb, sc_smem + L.ow);
     if (live) logits[i * cards + lane] = out + out_b;
   }
 }
@@ -188,7 +230,7 @@ __host__ __device__ inline CandSmem cand_smem(const cg_candidate_scorer_weights&
   s.gpad = w.card_width + 1;    // odd row stride of the staged grid rows
   int at = 0;
   s.qT = at, at += w.d_model * kScorerDim;
-  s.w = at, at += 3 * kScorerDim * w.card_width;  // card, target, taken projections [3][dim][width]
+  s.w = at, at += 3 * kScorerDim * w.card_width;  // card, target, taken projections [3][width][dim]
   s.idT = at, at += 3 * kScorerDim * s.cpad;      // card, target, taken ids transposed [3][dim][cards]
   s.kindT = at, at += kScorerDim * w.kinds;
   s.sizeT = at, at += kScorerDim * w.sizes;
@@ -219,8 +261,10 @@ __global__ void __launch_bounds__(kCandWarps * 32) candidate_scorer_kernel(
   const float* projections[3] = {w.card_w, w.target_w, w.taken_w};
   const float* identities[3] = {w.card_id, w.target_id, w.taken_id};
   for (int sl = 0; sl < 3; ++sl) {
-    for (int i = tid; i < kScorerDim * width; i += blockDim.x)
-      cs_smem[L.w + sl * kScorerDim * width + i] = projections[sl][i];
+    for (int i = tid; i < kScorerDim * width; i += blockDim.x) {
+      const int o = i / width, j = i - o * width;
+      cs_smem[L.w + sl * kScorerDim * width + j * kScorerDim + o] = projections[sl][i];  // [width][dim]
+    }
     for (int i = tid; i < kScorerDim * ncards; i += blockDim.x) {
       const int c = i / kScorerDim, o = i - c * kScorerDim;
       cs_smem[L.idT + (sl * kScorerDim + o) * L.cpad + c] = identities[sl][i];
@@ -240,7 +284,10 @@ __global__ void __launch_bounds__(kCandWarps * 32) candidate_scorer_kernel(
     cs_smem[L.hb + i] = w.hidden_b[i];
     cs_smem[L.ow + i] = w.out_w[i];
   }
-  for (int i = tid; i < kScorerDim * kScorerDim; i += blockDim.x) cs_smem[L.hw + i] = w.hidden_w[i];
+  for (int i = tid; i < kScorerDim * kScorerDim; i += blockDim.x) {
+    const int o = i / kScorerDim, k = i - o * kScorerDim;
+    cs_smem[L.hw + k * kScorerDim + o] = w.hidden_w[i];  // transposed [k][o]
+  }
   pdl_wait();
   pdl_trigger();
   __syncthreads();
@@ -259,16 +306,7 @@ __global__ void __launch_bounds__(kCandWarps * 32) candidate_scorer_kernel(
       grid_s[c * L.gpad + j] = scorer_load(grid, grid_dtype, i * ncards * width + x);
     }
     __syncwarp();
-    {
-      float a0 = 0.f, a1 = 0.f;
-      for (int x = 0; x < d; ++x) {
-        const float hx = hrow[x];
-        a0 = fmaf(cs_smem[L.qT + x * kScorerDim + lane], hx, a0);
-        a1 = fmaf(cs_smem[L.qT + x * kScorerDim + lane + 32], hx, a1);
-      }
-      qrow[lane] = w.query_b[lane] + a0;
-      qrow[lane + 32] = w.query_b[lane + 32] + a1;
-    }
+    scorer_query(cs_smem + L.qT, hrow, d, w.query_b, lane, qrow);
     __syncwarp();
 
     for (int c0 = 0; c0 < k_cands; c0 += 32) {
@@ -305,15 +343,9 @@ __global__ void __launch_bounds__(kCandWarps * 32) candidate_scorer_kernel(
 #pragma unroll
           for (int o = 0; o < kScorerDim; ++o) idacc[o] += idT[o * L.cpad + id];
         }
-        const float* W = cs_smem + L.w + sl * kScorerDim * width;
+        project_add(cs_smem + L.w + sl * kScorerDim * width, acc, width, m);
 #pragma unroll
-        for (int o = 0; o < kScorerDim; ++o) {
-          float p = m[o];
-#pragma unroll
-          for (int j = 0; j < kScorerMaxWidth; ++j)
-            if (j < width) p = fmaf(W[o * width + j], acc[j], p);
-          m[o] = p + idacc[o];
-        }
+        for (int o = 0; o < kScorerDim; ++o) m[o] += idacc[o];
       }
       // Slot 2: the taken counts, dense over the card types.
       if (taken) {
@@ -334,15 +366,9 @@ __global__ void __launch_bounds__(kCandWarps * 32) candidate_scorer_kernel(
 #pragma unroll
           for (int o = 0; o < kScorerDim; ++o) idacc[o] = fmaf(t, idT[o * L.cpad + c], idacc[o]);
         }
-        const float* W = cs_smem + L.w + 2 * kScorerDim * width;
+        project_add(cs_smem + L.w + 2 * kScorerDim * width, acc, width, m);
 #pragma unroll
-        for (int o = 0; o < kScorerDim; ++o) {
-          float p = m[o];
-#pragma unroll
-          for (int j = 0; j < kScorerMaxWidth; ++j)
-            if (j < width) p = fmaf(W[o * width + j], acc[j], p);
-          m[o] = p + idacc[o];
-        }
+        for (int o = 0; o < kScorerDim; ++o) m[o] += idacc[o];
       }
       int kd = live ? static_cast<int>(kind[row]) : 0;
       if (kd < 0 || kd >= w.kinds) {
@@ -356,37 +382,8 @@ __global__ void __launch_bounds__(kCandWarps * 32) candidate_scorer_kernel(
 #pragma unroll
       for (int o = 0; o < kScorerDim; ++o)
         m[o] = qrow[o] + ((m[o] + cs_smem[L.kindT + o * w.kinds + kd]) + cs_smem[L.sizeT + o * w.sizes + size]);
-      float mean = 0.f;
-#pragma unroll
-      for (int o = 0; o < kScorerDim; ++o) mean += m[o];
-      mean *= 1.f / kScorerDim;
-      float var = 0.f;
-#pragma unroll
-      for (int o = 0; o < kScorerDim; ++o) {
-        const float t = m[o] - mean;
-        var = fmaf(t, t, var);
-      }
-      const float rstd = rsqrtf(var * (1.f / kScorerDim) + 1e-5f);
-#pragma unroll
-      for (int o = 0; o < kScorerDim; ++o) m[o] = (m[o] - mean) * rstd * cs_smem[L.nw + o] + cs_smem[L.nb + o];
-      float out = 0.f;
-#pragma unroll 1
-      for (int o = 0; o < kScorerDim; o += 4) {
-        float h[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int x = 0; x < kScorerDim; x += 4) {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float4 wv = *reinterpret_cast<const float4*>(cs_smem + L.hw + (o + j) * kScorerDim + x);
-            h[j] = fmaf(wv.x, m[x], h[j]);
-            h[j] = fmaf(wv.y, m[x + 1], h[j]);
-            h[j] = fmaf(wv.z, m[x + 2], h[j]);
-            h[j] = fmaf(wv.w, m[x + 3], h[j]);
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) out = fmaf(cs_smem[L.ow + o + j], scorer_gelu(h[j] + cs_smem[L.hb + o + j]), out);
-      }
+      scorer_layer_norm(m, cs_smem + L.nw, cs_smem + L.nb);
+      const float out = scorer_head(m, cs_smem + L.hw, cs_smem + L.hb, cs_smem + L.ow);
       if (live) logits[row] = out + out_b;
     }
   }
