@@ -148,8 +148,13 @@ class PlumpActor:
         readout_offsets: torch.Tensor,
         span: int | None = None,
         rows: torch.Tensor | None = None,
+        workspace: torch.Tensor | None = None,
     ) -> torch.Tensor:
-        """Append a padded run per cache row 0..B-1 (or ``rows``); hidden at each readout [B, d] (model.py:76-89)."""
+        """Append a padded run per cache row 0..B-1 (or ``rows``); hidden at each readout [B, d] (model.py:76-89).
+
+        ``workspace`` (uint8, at least ``step_workspace_bytes``) pins the step's scratch memory,
+        for callers that capture the step in a CUDA graph; by default a shared buffer is used.
+        """
 
         batch, steps, _ = tokens.shape
         if span is None:
@@ -157,8 +162,11 @@ class PlumpActor:
         span = min(span, cache.max_len)
         tokens = tokens.contiguous()
         precision = nat.PRECISIONS[self.precision]
-        need = nat.query("cg_plump_step_workspace_bytes", self.trunk.dims, batch, steps, precision)
-        workspace = nat.Workspace.get(self.device, need)
+        need = self.step_workspace_bytes(batch, steps)
+        if workspace is None:
+            workspace = nat.Workspace.get(self.device, need)
+        elif workspace.numel() < need:
+            raise ValueError(f"workspace of {workspace.numel()} bytes < {need} needed")
         hidden = torch.empty((batch, self.config.d_model), device=self.device)
         nat.call(
             "cg_plump_forward_ragged", self.trunk.dims, nat.ptr(self.trunk.blob), self.schema, nat.ptr(self.table),
@@ -169,6 +177,9 @@ class PlumpActor:
             nat.ptr(workspace), workspace.numel(), nat.ptr(hidden), nat.stream_handle(self.device),
         )
         return hidden
+
+    def step_workspace_bytes(self, batch: int, steps: int) -> int:
+        return nat.query("cg_plump_step_workspace_bytes", self.trunk.dims, batch, steps, nat.PRECISIONS[self.precision])
 
     def forward_prefill(self, tokens: torch.Tensor, cache: KVCache, rows: torch.Tensor | None) -> torch.Tensor:
         """Encode fresh prefixes [B, T, W] at positions 0..T-1; hidden at the last position (trunk.py:376-389).
