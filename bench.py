@@ -183,7 +183,7 @@ def run_ppo(args, device, rank: int, world_size: int) -> dict:
     players = torch.full((d1 - d0,), PPO_PLAYERS, dtype=torch.int32, device=device)
     gradient = torch.zeros(TRUNK_PARAMS, device=device) if world_size > 1 else None
 
-    def step():
+    def local_step():
         advantages = ppo.segmented_gae(values, seats, starts, returns, 0.95)
         normalize_global_(advantages, weights64)  # batch-global two-pass mean/std, no host read
         leaf = logits.detach().requires_grad_()
@@ -191,9 +191,19 @@ def run_ppo(args, device, rank: int, world_size: int) -> dict:
         pred = prediction.detach().requires_grad_()
         loss, _ = ppo.value_loss(pred, players, targets, weights, 1.0)
         (objective + loss).backward()
+        return leaf.grad, pred.grad
+
+    # One GPU: the whole step replays as one CUDA graph. Several: the step's collectives (the
+    # normalisation's sums and the gradient allreduce) run eagerly with it.
+    graphed = ppo.GraphedStep(local_step) if world_size == 1 else None
+
+    def step():
+        if graphed is not None:
+            return graphed()
+        grads = local_step()
         if gradient is not None:
             dist.all_reduce(gradient)
-        return leaf.grad, pred.grad
+        return grads
 
     for _ in range(3):
         step()
@@ -232,6 +242,7 @@ def run_ppo(args, device, rank: int, world_size: int) -> dict:
                         "allreduce (NCCL) per step"),
         "includes": "GAE, global two-pass mean/std and normalise on the device (no host read), fused PPO "
                     "objective fwd+grad, value loss fwd+grad, autograd backward",
+        "launch": "one CUDA graph replay per step (ppo.GraphedStep)" if world_size == 1 else "eager launches",
     }
 
 

@@ -11,6 +11,7 @@
 namespace cg {
 
 constexpr int kReduceBlocks = 512;  // fixed partial count: the same order on every call
+constexpr int kObjectiveBlocks = 2048;  // the objective's partial count (8 rows in flight per block)
 constexpr int kTerms = 8;
 
 // ---- GAE -----------------------------------------------------------------------------
@@ -65,12 +66,16 @@ __global__ void weighted_sums_kernel(const double* __restrict__ x, const double*
   if (threadIdx.x < 3) partial[blockIdx.x * 3 + threadIdx.x] = s[threadIdx.x][0];
 }
 
-// Sums `count` partial rows of `width` doubles in order into out[width].
+// Sums `count` partial rows of `width` doubles into out[width]: warp k takes column k, lane l
+// the partials l, l + 32, ... in order, then a fixed butterfly; the same order on every call.
 __global__ void sum_partials_kernel(const double* partial, int count, int width, double* out) {
-  for (int k = threadIdx.x; k < width; k += blockDim.x) {
+  const int lane = threadIdx.x & 31;
+  for (int k = threadIdx.x >> 5; k < width; k += blockDim.x >> 5) {
     double total = 0;
-    for (int b = 0; b < count; ++b) total += partial[b * width + k];
-    out[k] = total;
+    for (int b = lane; b < count; b += 32) total += partial[b * width + k];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+    if (lane == 0) out[k] = total;
   }
 }
 
@@ -95,6 +100,8 @@ __global__ void normalize_from_sums_kernel(double* x, int64_t n, const double* _
 // ---- fused PPO objective ---------------------------------------------------------------
 constexpr int kPpoMaxWidth = 256;
 
+// kPer: logits per lane (width <= 32 * kPer).
+template <int kPer>
 __global__ void __launch_bounds__(256) ppo_objective_kernel(
     const float* __restrict__ logits, const float* __restrict__ old_probs, int64_t rows, int width, int64_t stride,
     const int64_t* __restrict__ actions, const float* __restrict__ advantages, const float* __restrict__ weights,
@@ -102,18 +109,40 @@ __global__ void __launch_bounds__(256) ppo_objective_kernel(
   __shared__ double s[8][kTerms];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   double acc[kTerms] = {0, 0, 0, 0, 0, 0, 0, 0};
-  constexpr int kPer = kPpoMaxWidth / 32;
-  for (int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + warp; row < rows; row += static_cast<int64_t>(gridDim.x) * 8) {
-    const float* z = logits + row * stride;
-    const float* old = old_probs + row * stride;
+  const int64_t step = static_cast<int64_t>(gridDim.x) * 8;
+  // The next row's inputs load while this row is computed.
+  float nz[kPer], no[kPer];
+  int64_t na = 0;
+  float nadv = 0.f, nw = 0.f;
+  auto fetch = [&](int64_t r) {
+    if (r >= rows) return;
+    const float* z = logits + r * stride;
+    const float* old = old_probs + r * stride;
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int j = lane + 32 * k;
+      nz[k] = j < width ? z[j] : 0.f;
+      no[k] = j < width ? old[j] : 0.f;
+    }
+    na = actions[r];
+    nadv = advantages[r];
+    nw = weights[r];
+  };
+  fetch(static_cast<int64_t>(blockIdx.x) * 8 + warp);
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + warp; row < rows; row += step) {
     float zl[kPer], ol[kPer];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      zl[k] = nz[k];
+      ol[k] = no[k];
+    }
+    const int64_t a = na;
+    const float adv = nadv, w = nw;
+    fetch(row + step);
     float peak = -INFINITY;
     int count = 0;
 #pragma unroll
     for (int k = 0; k < kPer; ++k) {
-      const int j = lane + 32 * k;
-      zl[k] = j < width ? z[j] : 0.f;
-      ol[k] = j < width ? old[j] : 0.f;
       if (ol[k] > 0.f) {
         peak = fmaxf(peak, zl[k]);
         ++count;
@@ -128,8 +157,6 @@ __global__ void __launch_bounds__(256) ppo_objective_kernel(
       if (ol[k] > 0.f) sum += expf(zl[k] - peak);
     sum = warp_sum(sum);
     const float lse = peak + logf(sum);
-    const int64_t a = actions[row];
-    const float adv = advantages[row], w = weights[row];
     float lp_a = 0.f, old_log_a = 0.f;
     float entropy = 0.f, kl = 0.f;
     float lp[kPer], p[kPer];
@@ -295,7 +322,7 @@ extern "C" int cg_weighted_sums(const double* values, const double* weights, int
   weighted_sums_kernel<<<blocks, 256, 0, s>>>(values, weights, n, shift, nullptr, partial);
   int rc = check_launch("weighted_sums_kernel");
   if (rc) return rc;
-  sum_partials_kernel<<<1, 32, 0, s>>>(partial, blocks, 3, out3);
+  sum_partials_kernel<<<1, 3 * 32, 0, s>>>(partial, blocks, 3, out3);
   return check_launch("sum_partials_kernel");
 }
 
@@ -313,7 +340,7 @@ extern "C" int cg_weighted_sums_shifted(const double* values, const double* weig
   weighted_sums_kernel<<<blocks, 256, 0, s>>>(values, weights, n, 0.0, shift_sums3, partial);
   int rc = check_launch("weighted_sums_kernel");
   if (rc) return rc;
-  sum_partials_kernel<<<1, 32, 0, s>>>(partial, blocks, 3, out3);
+  sum_partials_kernel<<<1, 3 * 32, 0, s>>>(partial, blocks, 3, out3);
   return check_launch("sum_partials_kernel");
 }
 
@@ -337,7 +364,7 @@ extern "C" int cg_normalize(double* values, int64_t n, double mean, double std, 
   return check_launch("normalize_kernel");
 }
 
-extern "C" int64_t cg_ppo_objective_workspace_bytes(int64_t) { return cg::kReduceBlocks * cg::kTerms * sizeof(double); }
+extern "C" int64_t cg_ppo_objective_workspace_bytes(int64_t) { return cg::kObjectiveBlocks * cg::kTerms * sizeof(double); }
 
 extern "C" int cg_ppo_objective(const float* logits, const float* old_probs, int64_t rows, int width, int64_t stride,
                                 const int64_t* actions, const float* advantages, const float* weights, float clip_ratio,
@@ -349,18 +376,24 @@ extern "C" int cg_ppo_objective(const float* logits, const float* old_probs, int
   if (rows == 0) return CG_OK;
   CG_REQUIRE(logits && old_probs && actions && advantages && weights, "cg_ppo_objective: NULL input");
   CG_REQUIRE(!totals || workspace, "cg_ppo_objective: totals need a workspace");
-  const int blocks = reduce_blocks(rows, 8);
+  const int64_t want = (rows + 7) / 8;
+  const int blocks = static_cast<int>(want < kObjectiveBlocks ? want : kObjectiveBlocks);
   if (totals && workspace_bytes < static_cast<int64_t>(blocks) * kTerms * 8)
     return set_error(CG_ERR_WORKSPACE, "cg_ppo_objective: workspace too small");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   double* partial = static_cast<double*>(workspace);
   // Without totals the partials still need a home: the kernel writes them unconditionally.
   if (!partial) return set_error(CG_ERR_WORKSPACE, "cg_ppo_objective: workspace required");
-  ppo_objective_kernel<<<blocks, 256, 0, s>>>(logits, old_probs, rows, width, stride, actions, advantages, weights,
-                                              clip_ratio, alpha, dlogits, row_terms, partial);
+  if (width <= 64)
+    ppo_objective_kernel<2><<<blocks, 256, 0, s>>>(logits, old_probs, rows, width, stride, actions, advantages,
+                                                   weights, clip_ratio, alpha, dlogits, row_terms, partial);
+  else
+    ppo_objective_kernel<kPpoMaxWidth / 32><<<blocks, 256, 0, s>>>(logits, old_probs, rows, width, stride, actions,
+                                                                   advantages, weights, clip_ratio, alpha, dlogits,
+                                                                   row_terms, partial);
   int rc = check_launch("ppo_objective_kernel");
   if (rc || !totals) return rc;
-  sum_partials_kernel<<<1, 32, 0, s>>>(partial, blocks, kTerms, totals);
+  sum_partials_kernel<<<1, kTerms * 32, 0, s>>>(partial, blocks, kTerms, totals);
   return check_launch("sum_partials_kernel");
 }
 
@@ -384,6 +417,6 @@ extern "C" int cg_value_loss(const float* prediction, const float* targets, cons
                                            grad, partial);
   int rc = check_launch("value_loss_kernel");
   if (rc || !totals) return rc;
-  sum_partials_kernel<<<1, 32, 0, s>>>(partial, blocks, 4, totals);
+  sum_partials_kernel<<<1, 4 * 32, 0, s>>>(partial, blocks, 4, totals);
   return check_launch("sum_partials_kernel");
 }

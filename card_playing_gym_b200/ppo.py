@@ -229,3 +229,36 @@ def value_loss(prediction: torch.Tensor, players: torch.Tensor, targets: torch.T
     loss, sum w/n sum raw^2, sum w/n sum target^2, sum w)."""
 
     return _ValueLoss.apply(prediction, targets, players, weights, float(reward_scale))
+
+
+# -- one captured step ------------------------------------------------------------------------
+class GraphedStep:
+    """A fixed-shape step captured once as a CUDA graph and replayed (the update's advantage +
+    loss step is a few dozen short kernels; replayed, it costs its device time, not its launches).
+
+    ``fn`` takes no arguments; the tensors it reads and writes must keep their storage between
+    calls (refill inputs in place). Every call returns what ``fn`` returned on the capture: the
+    same tensors, rewritten by the replay. The first call runs ``fn`` ``warmup`` times on a side
+    stream, so that every kernel and library workspace is configured at its final size before
+    the capture, then captures and replays it. Collectives belong outside the captured step.
+    """
+
+    def __init__(self, fn, warmup: int = 2) -> None:
+        self.fn = fn
+        self.warmup = warmup
+        self.graph: torch.cuda.CUDAGraph | None = None
+        self.outputs = None
+
+    def __call__(self):
+        if self.graph is None:
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                for _ in range(self.warmup):
+                    self.fn()
+            torch.cuda.current_stream().wait_stream(side)
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph):
+                self.outputs = self.fn()
+        self.graph.replay()
+        return self.outputs

@@ -45,3 +45,46 @@ def test_decode_graphs_replay_matches_the_eager_wave():
     assert set(graphs.columns) == {*actor.policy_heads, "values"}
     assert torch.equal(graph_cache.k_pool, eager_cache.k_pool)
     assert torch.equal(graph_cache.v_pool, eager_cache.v_pool)
+
+
+def test_graphed_ppo_step_matches_the_eager_step():
+    """The PPO advantage + loss step replayed as one CUDA graph (ppo.GraphedStep) gives the
+    eager step's gradients bit for bit, replay after replay, as its inputs are refilled."""
+
+    import bench
+    from card_playing_gym_b200 import ppo
+    from card_playing_gym_b200.data_parallel import normalize_global_
+
+    batch = bench.synthetic_ppo_batch(20000, seed=3)
+    cuda = lambda a, dtype=None: torch.as_tensor(np.ascontiguousarray(a)).to(device="cuda", dtype=dtype)  # noqa: E731
+    values = cuda(batch["values"], torch.float64)
+    seats = cuda(batch["seats"], torch.int32)
+    starts = cuda(batch["starts"], torch.int64)
+    returns = cuda(batch["returns"], torch.float64)
+    logits = cuda(batch["logits"])
+    old_probs = cuda(batch["old_probs"])
+    actions = cuda(batch["actions"])
+    weights = cuda(batch["weights"], torch.float32)
+    weights64 = cuda(batch["weights"], torch.float64)
+    prediction = cuda(batch["prediction"])
+    targets = cuda(batch["targets"])
+    players = torch.full((values.shape[0],), 4, dtype=torch.int32, device="cuda")
+
+    def step():
+        advantages = ppo.segmented_gae(values, seats, starts, returns, 0.95)
+        normalize_global_(advantages, weights64)
+        leaf = logits.detach().requires_grad_()
+        objective, _ = ppo.policy_objective(leaf, old_probs, actions, advantages, weights, clip_ratio=0.2, alpha=0.01)
+        pred = prediction.detach().requires_grad_()
+        loss, _ = ppo.value_loss(pred, players, targets, weights, 1.0)
+        (objective + loss).backward()
+        return leaf.grad, pred.grad
+
+    graphed = ppo.GraphedStep(step)
+    for trial in range(3):
+        if trial:
+            logits.add_(0.01)  # new inputs, refilled in place
+            values.mul_(0.9)
+        want = [g.clone() for g in step()]
+        got = graphed()
+        assert all(torch.equal(a, b) for a, b in zip(got, want)), trial
