@@ -237,6 +237,170 @@ __global__ void __launch_bounds__(256) ppo_objective_kernel(
   }
 }
 
+// Rows of at most 64 legal-masked logits (width % 4 == 0, 16-byte aligned rows): eight lanes
+// per row, four rows per warp. Lane l of a row group holds logits 4l..4l+3 and 32+4l..32+4l+3
+// (float4 loads and stores); the row's reductions are three butterfly steps inside the group.
+// The same arithmetic as ppo_objective_kernel; only the order of the per-row sums differs.
+__device__ __forceinline__ float group8_sum(float v) {
+#pragma unroll
+  for (int o = 4; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__global__ void __launch_bounds__(256) ppo_objective_narrow_kernel(
+    const float* __restrict__ logits, const float* __restrict__ old_probs, int64_t rows, int width, int64_t stride,
+    const int64_t* __restrict__ actions, const float* __restrict__ advantages, const float* __restrict__ weights,
+    float clip, float alpha, float* dlogits, float* row_terms, double* partial) {
+  __shared__ double s[8][kTerms];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int grp = lane >> 3, l = lane & 7;
+  double acc[kTerms] = {0, 0, 0, 0, 0, 0, 0, 0};
+  const int64_t step = static_cast<int64_t>(gridDim.x) * 32;
+  float4 nz[2], no[2];
+  int64_t na = 0;
+  float nadv = 0.f, nw = 0.f;
+  auto fetch = [&](int64_t r) {
+    if (r >= rows) return;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int j = 4 * l + 32 * h;
+      nz[h] = j < width ? *reinterpret_cast<const float4*>(logits + r * stride + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+      no[h] = j < width ? *reinterpret_cast<const float4*>(old_probs + r * stride + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    na = actions[r];
+    nadv = advantages[r];
+    nw = weights[r];
+  };
+  // Every group of a warp runs the same iterations, so the shuffles stay converged.
+  const int64_t warp_first = (static_cast<int64_t>(blockIdx.x) * 8 + warp) * 4;
+  fetch(warp_first + grp);
+  for (int64_t base = warp_first; base < rows; base += step) {
+    const int64_t row = base + grp;
+    const bool live = row < rows;
+    float zl[8], ol[8];
+    zl[0] = nz[0].x, zl[1] = nz[0].y, zl[2] = nz[0].z, zl[3] = nz[0].w;
+    zl[4] = nz[1].x, zl[5] = nz[1].y, zl[6] = nz[1].z, zl[7] = nz[1].w;
+    ol[0] = no[0].x, ol[1] = no[0].y, ol[2] = no[0].z, ol[3] = no[0].w;
+    ol[4] = no[1].x, ol[5] = no[1].y, ol[6] = no[1].z, ol[7] = no[1].w;
+    if (!live) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) ol[k] = 0.f;  // nothing legal: the padding row contributes nothing
+    }
+    const int64_t a = na;
+    const float adv = live ? nadv : 0.f, w = live ? nw : 0.f;
+    fetch(row + step);
+    float peak = -INFINITY;
+    float count = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (ol[k] > 0.f) {
+        peak = fmaxf(peak, zl[k]);
+        count += 1.f;
+      }
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) peak = fmaxf(peak, __shfl_xor_sync(0xffffffffu, peak, o));
+    count = group8_sum(count);
+    float sum = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (ol[k] > 0.f) sum += expf(zl[k] - peak);
+    sum = group8_sum(sum);
+    const float lse = peak + logf(sum);
+    float lp_a = 0.f, old_log_a = 0.f, entropy = 0.f, kl = 0.f;
+    float lp[8], p[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int j = 4 * l + 32 * (k >> 2) + (k & 3);
+      const bool legal = ol[k] > 0.f;
+      lp[k] = legal ? zl[k] - lse : 0.f;
+      p[k] = legal ? expf(lp[k]) : 0.f;
+      const float old_log = logf(fmaxf(ol[k], 1e-12f));
+      if (j == a) {
+        lp_a = lp[k];
+        old_log_a = old_log;
+      }
+      if (legal) {
+        entropy -= p[k] * lp[k];
+        kl += ol[k] * (old_log - lp[k]);
+      }
+    }
+    lp_a = group8_sum(lp_a);
+    old_log_a = group8_sum(old_log_a);
+    entropy = group8_sum(entropy);
+    kl = group8_sum(kl);
+    const float ratio = expf(lp_a - old_log_a);
+    const float clipped_ratio = fminf(fmaxf(ratio, 1.f - clip), 1.f + clip);
+    const float unclipped = ratio * adv, clipped = clipped_ratio * adv;
+    const float loss = -fminf(unclipped, clipped);
+    const bool inside = ratio >= 1.f - clip && ratio <= 1.f + clip;
+    const float d_ratio = unclipped < clipped ? -adv : (unclipped > clipped ? (inside ? -adv : 0.f) : -adv);
+    const int icount = static_cast<int>(count);
+    const bool eligible = icount > 1;
+    const float norm_scale = eligible ? 1.f / logf(static_cast<float>(icount < 2 ? 2 : icount)) : 0.f;
+    const float normalized = eligible ? entropy * norm_scale : 0.f;
+    const bool is_clipped = fabsf(ratio - 1.f) > clip;
+    if (dlogits && live) {
+      const float g_action = w * d_ratio * ratio;
+      const float g_entropy = -alpha * w * norm_scale;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int j0 = 4 * l + 32 * h;
+        if (j0 >= width) continue;
+        float g[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int k = 4 * h + e;
+          g[e] = 0.f;
+          if (ol[k] > 0.f) {
+            g[e] = g_action * ((j0 + e == a ? 1.f : 0.f) - p[k]);
+            g[e] += g_entropy * (-p[k] * (lp[k] + entropy));
+          }
+        }
+        *reinterpret_cast<float4*>(dlogits + row * width + j0) = make_float4(g[0], g[1], g[2], g[3]);
+      }
+    }
+    if (row_terms && live && l == 0) {
+      float* t = row_terms + row * kTerms;
+      t[0] = loss;
+      t[1] = kl;
+      t[2] = entropy;
+      t[3] = normalized;
+      t[4] = eligible ? 1.f : 0.f;
+      t[5] = ratio;
+      t[6] = is_clipped ? 1.f : 0.f;
+      t[7] = lp_a;
+    }
+    if (l == 0 && live) {
+      const double wd = w;
+      acc[0] += wd * loss;
+      acc[1] += wd;
+      acc[2] += wd * entropy;
+      acc[3] += wd * (eligible ? 1.0 : 0.0) * normalized;
+      acc[4] += eligible ? wd : 0.0;
+      acc[5] += is_clipped ? wd : 0.0;
+      acc[6] += wd * kl;
+      acc[7] += wd * loss - static_cast<double>(alpha) * wd * (eligible ? 1.0 : 0.0) * normalized;
+    }
+  }
+  // The four group leaders' sums in group order, then the warps in order.
+#pragma unroll
+  for (int k = 0; k < kTerms; ++k) {
+    const double v = acc[k];
+    const double v8 = __shfl_down_sync(0xffffffffu, v, 8);
+    const double v16 = __shfl_down_sync(0xffffffffu, v, 16);
+    const double v24 = __shfl_down_sync(0xffffffffu, v, 24);
+    acc[k] = ((v + v8) + v16) + v24;
+  }
+  if (lane == 0)
+    for (int k = 0; k < kTerms; ++k) s[warp][k] = acc[k];
+  __syncthreads();
+  if (threadIdx.x < kTerms) {
+    double total = 0;
+    for (int w = 0; w < 8; ++w) total += s[w][threadIdx.x];
+    partial[blockIdx.x * kTerms + threadIdx.x] = total;
+  }
+}
+
 // ---- value loss ---------------------------------------------------------------------------
 constexpr int kValueMaxPlayers = 16;
 
@@ -384,7 +548,14 @@ extern "C" int cg_ppo_objective(const float* logits, const float* old_probs, int
   double* partial = static_cast<double*>(workspace);
   // Without totals the partials still need a home: the kernel writes them unconditionally.
   if (!partial) return set_error(CG_ERR_WORKSPACE, "cg_ppo_objective: workspace required");
-  if (width <= 64)
+  const bool narrow = width <= 64 && width % 4 == 0 && stride % 4 == 0 &&
+                      (reinterpret_cast<uintptr_t>(logits) & 15) == 0 &&
+                      (reinterpret_cast<uintptr_t>(old_probs) & 15) == 0 &&
+                      (!dlogits || (reinterpret_cast<uintptr_t>(dlogits) & 15) == 0);
+  if (narrow)
+    ppo_objective_narrow_kernel<<<blocks, 256, 0, s>>>(logits, old_probs, rows, width, stride, actions, advantages,
+                                                       weights, clip_ratio, alpha, dlogits, row_terms, partial);
+  else if (width <= 64)
     ppo_objective_kernel<2><<<blocks, 256, 0, s>>>(logits, old_probs, rows, width, stride, actions, advantages,
                                                    weights, clip_ratio, alpha, dlogits, row_terms, partial);
   else
