@@ -72,6 +72,8 @@ def parse_args(argv=None):
     parser.add_argument("--ppo-steps", type=int, default=20)
     parser.add_argument("--piquet-steps", type=int, default=20,
                         help="waves of the piquet-scale decode leg (8,192 two-player deals); 0 skips it")
+    parser.add_argument("--t2-steps", type=int, default=20,
+                        help="waves of the rl-v6 T = 2 leg (two tokens appended per row); 0 skips it")
     parser.add_argument("--pointer-steps", type=int, default=20,
                         help="waves of the piquet and rummy-style pointer-head legs; 0 skips them")
     return parser.parse_args(argv)
@@ -320,6 +322,51 @@ def run_piquet_scale(args, device, rank: int, world_size: int) -> dict:
                                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
                                "algorithmic_bytes_per_launch": algorithmic, "mean_launch_ms": mean_ms},
     }
+
+
+def run_two_token_wave(args, device, rank: int, world_size: int, actor, cache, wave: dict, span: int) -> dict:
+    """The rl-v6 wave with T = 2 tokens appended per row (both readouts' rows decide on the
+    second), the same games, cache and heads as the headline wave."""
+
+    import torch
+    import torch.distributed as dist
+
+    rows = wave["tokens"].shape[0]
+    tokens = np.repeat(wave["tokens"], 2, axis=1)
+    tokens[:, 1, 1:16] = np.roll(tokens[:, 1, 1:16], 1, axis=0)  # a different second token
+    positions = np.maximum(wave["positions"] - 1, 0)
+    dev = {k: torch.from_numpy(v).to(device) for k, v in wave.items()}
+    dev_tokens = torch.from_numpy(tokens).to(device)
+    dev_positions = torch.from_numpy(positions).to(device)
+    offsets = torch.ones(rows, dtype=torch.int64, device=device)
+
+    def step():
+        hidden = actor.forward_ragged(dev_tokens, dev_positions, cache, offsets, span=span)
+        return actor.decide(hidden, dev["heads"], dev["legal"], dev["uniforms"], dev["readout_rows"], logits=False,
+                            values=True)
+
+    for _ in range(3):
+        step()
+    if world_size > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    stream = torch.cuda.current_stream(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.t2_steps):
+        step()
+    end.record(stream)
+    torch.cuda.synchronize(device)
+    ms = start.elapsed_time(end) / args.t2_steps
+    if world_size > 1:
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    games = wave["heads"].shape[0]
+    return {"workload": f"rl-v6 decode wave with T = 2 tokens per row: {games} games ({rows} rows), same lengths, "
+                        "fp16 KV, readout at the second token",
+            "value": world_size * games / (ms / 1000.0), "unit": "decisions/s",
+            "tokens_per_s": world_size * 2 * rows / (ms / 1000.0), "ms_per_step": ms, "steps": args.t2_steps}
 
 
 def run_pointer_wave(args, device, rank: int, world_size: int, kind: str) -> dict:
@@ -704,6 +751,8 @@ def run_b200(args) -> int:
     ppo_line = run_ppo(args, device, rank, world_size) if args.ppo_decisions > 0 else None
     piquet_line = run_piquet_scale(args, device, rank, world_size) if args.piquet_steps > 0 else None
     pointer_lines = {}
+    if args.t2_steps > 0:
+        pointer_lines["rlv6_t2"] = run_two_token_wave(args, device, rank, world_size, actor, cache, wave, span)
     if args.pointer_steps > 0:
         pointer_lines["piquet_pointer"] = run_pointer_wave(args, device, rank, world_size, "piquet")
         pointer_lines["rummy_style"] = run_pointer_wave(args, device, rank, world_size, "rummy")
