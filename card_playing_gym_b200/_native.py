@@ -79,6 +79,15 @@ class CandidateScorerWeights(ctypes.Structure):
         "size_emb", "norm_w", "norm_b", "hidden_w", "hidden_b", "out_w", "out_b")]
 
 
+class CardGridWeights(ctypes.Structure):
+    _fields_ = [
+        ("width", ctypes.c_int32), ("hidden", ctypes.c_int32), ("kernel", ctypes.c_int32), ("blocks", ctypes.c_int32),
+        ("codes", ctypes.c_int32), ("code_emb", ctypes.c_void_p), ("rank_emb", ctypes.c_void_p),
+    ] + [(name, ctypes.c_void_p * 4) for name in ("norm_w", "conv_w", "conv_b", "across_w", "out_w", "out_b")] + [
+        ("final_norm", ctypes.c_void_p),
+    ]
+
+
 _SIGNATURES: dict[str, tuple[type, list]] = {
     "cg_last_error": (ctypes.c_char_p, []),
     "cg_version": (_i32, []),
@@ -103,6 +112,7 @@ _SIGNATURES: dict[str, tuple[type, list]] = {
     "cg_bags_forward_ragged": (_i32, [ctypes.POINTER(TrunkDims), _p, _p, _i32, _i64, _i32, ctypes.POINTER(_i64), _p,
                                       _i64, _p, _i64, _i32, _p, _p, _p, _i32, _p, _p, _i32, _i64, _i32, _i32, _p, _i64,
                                       _p, _p]),
+    "cg_card_grid": (_i32, [ctypes.POINTER(CardGridWeights), _p, _i32, _i64, _i64, _p, _p]),
     "cg_card_scorer": (_i32, [ctypes.POINTER(CardScorerWeights), _p, _i64, _p, _i32, _p, _p]),
     "cg_candidate_scorer": (_i32, [ctypes.POINTER(CandidateScorerWeights), _p, _i64, _i32, _i32, _p, _i32, _p, _p, _p,
                                    _p, _p, _p]),

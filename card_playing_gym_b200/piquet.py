@@ -7,6 +7,10 @@ the autocast dtype (fp32 accumulation, each sum rounded once) or the tables' own
 product is a gather-sum of each distinct selected row (``cg_onehot_bags``). The card-grid
 summary that ``PiquetEmbedding.forward`` adds to the first sum stays with the caller.
 
+``CardGrid`` mirrors cardgym/games/piquet/model.py:180-240 (``cards`` and ``forward``): the
+per-card features of a token's 32 card codes (``cg_card_grid``, in the reference's bf16
+autocast form) and their summary projection (a plain GEMM, left to torch).
+
 ``CardScorer`` mirrors cardgym/games/piquet/model.py:348-363: one logit per card from the
 readout state and the card's grid features (``cg_card_scorer``), as PiquetActor.policy_logits
 (399-411) calls it for the exchange and play heads.
@@ -177,3 +181,59 @@ def forward_ragged(trunk, lookup: PiquetFieldLookup, tokens: torch.Tensor, posit
              nat.PRECISIONS[trunk.precision], nat.ptr(workspace), workspace.numel(), nat.ptr(hidden),
              nat.stream_handle(trunk.device))
     return hidden
+
+
+class CardGrid:
+    """``CardGrid``: card codes [..., 32] -> (cards fp32 [..., 32, width], summary [..., d]).
+
+    Built from the reference module's parameters (``prefix + "code.weight"`` etc., as in a
+    PiquetActor ``state_dict`` with prefix ``"embedding.grid."``). ``cards`` is computed as the
+    reference computes it under bf16 autocast (its rollout precision); ``forward`` adds the
+    summary projection with torch, honouring the caller's autocast state like the reference.
+    """
+
+    def __init__(self, state: dict, prefix: str = "", device: torch.device | str = "cuda", blocks: int | None = None):
+        get = lambda name: torch.as_tensor(state[prefix + name]).detach().to(device=device, dtype=torch.float32).contiguous()  # noqa: E731
+        if blocks is None:
+            blocks = 0
+            while f"{prefix}blocks.{blocks}.norm.weight" in state:
+                blocks += 1
+        self.params = {"code": get("code.weight"), "rank": get("rank.weight"), "norm": get("norm.weight")}
+        self.summary = get("summary.weight") if prefix + "summary.weight" in state else None
+        names = ("norm.weight", "along_rank.weight", "along_rank.bias", "across_suits.weight", "out.weight", "out.bias")
+        self.blocks = [{n: get(f"blocks.{b}.{n}") for n in names} for b in range(blocks)]
+        width = self.params["code"].shape[1]
+        hidden, _, taps = self.blocks[0]["along_rank.weight"].shape if blocks else (64, width, 3)
+        w = nat.CardGridWeights()
+        w.width, w.hidden, w.kernel, w.blocks, w.codes = width, hidden, taps, blocks, self.params["code"].shape[0]
+        w.code_emb, w.rank_emb, w.final_norm = (nat.ptr(self.params[k]) for k in ("code", "rank", "norm"))
+        for b, blk in enumerate(self.blocks):
+            w.norm_w[b] = nat.ptr(blk["norm.weight"])
+            w.conv_w[b] = nat.ptr(blk["along_rank.weight"])
+            w.conv_b[b] = nat.ptr(blk["along_rank.bias"])
+            w.across_w[b] = nat.ptr(blk["across_suits.weight"])
+            w.out_w[b] = nat.ptr(blk["out.weight"])
+            w.out_b[b] = nat.ptr(blk["out.bias"])
+        self.weights = w
+        self.width = width
+
+    def cards(self, codes: torch.Tensor) -> torch.Tensor:
+        """Per-card features [..., 32, width] of card codes [..., 32] (any view of token rows)."""
+
+        lead = codes.shape[:-1]
+        flat = codes.reshape(-1, codes.shape[-1])
+        if flat.dtype not in nat.INDEX_CODES:
+            flat = flat.long()
+        if flat.stride(-1) != 1:
+            flat = flat.contiguous()
+        count = flat.shape[0]
+        out = torch.empty((count, 32, self.width), dtype=torch.float32, device=flat.device)
+        nat.call("cg_card_grid", self.weights, nat.ptr(flat), nat.INDEX_CODES[flat.dtype], count, flat.stride(0),
+                 nat.ptr(out), nat.stream_handle(flat.device))
+        return out.view(*lead, 32, self.width)
+
+    def __call__(self, codes: torch.Tensor):
+        cards = self.cards(codes)
+        if self.summary is None:
+            return cards, None
+        return cards, torch.nn.functional.linear(cards.flatten(-2), self.summary)

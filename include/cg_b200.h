@@ -179,6 +179,32 @@ int cg_bags_forward_ragged(const cg_trunk_dims* dims, const void* blob, const vo
                            int64_t workspace_bytes, float* hidden_out, void* stream);
 
 /* ---------------------------------------------------------------------------------
+ * Piquet card grid (cardgym/games/piquet/model.py:180-240 `CardGrid.cards`, with
+ * GridBlock 129-177 and GridNorm 118-126): a token's 32 card codes (card = suit * 8 + rank)
+ * -> per-card features fp32 [n, 32, width] after `blocks` residual grid blocks and the final
+ * RMSNorm, computed as the reference computes it under bf16 autocast (bf16 GEMM operands,
+ * fp32 accumulation, every Linear/matmul output, their sum and the GELU rounded to bf16; the
+ * residual grid and the norms in fp32). width 32, hidden 64, 3 rank taps, blocks <= 4,
+ * code vocabulary <= 16. codes: n rows of codes_stride ids (CG_I16/I32/I64), the 32 card
+ * codes first (tokens + CARD_START). A code outside the vocabulary sets the fault word 0x230.
+ * The summary projection (a plain [32 * width -> d] Linear) stays with the caller's GEMM.
+ * ------------------------------------------------------------------------------- */
+typedef struct {
+  int32_t width, hidden, kernel, blocks, codes;
+  const float* code_emb;     /* [codes, width] */
+  const float* rank_emb;     /* [8, width] */
+  const float* norm_w[4];    /* per block: GridNorm gain [width] */
+  const float* conv_w[4];    /* along_rank Conv1d weight [hidden, width, 3] */
+  const float* conv_b[4];    /* [hidden] */
+  const float* across_w[4];  /* across_suits [hidden, width] */
+  const float* out_w[4];     /* [width, hidden] */
+  const float* out_b[4];     /* [width] */
+  const float* final_norm;   /* [width] */
+} cg_card_grid_weights;
+int cg_card_grid(const cg_card_grid_weights* weights, const void* codes, int codes_dtype, int64_t n,
+                 int64_t codes_stride, float* cards, void* stream);
+
+/* ---------------------------------------------------------------------------------
  * Card pointer head (cardgym/games/piquet/model.py:348-363 `CardScorer.forward`, the
  * exchange and play heads of PiquetActor.policy_logits 399-411): one logit per card,
  *   out(GELU(hidden(LayerNorm(query(h)[:, None] + card(grid) + card_id)))).

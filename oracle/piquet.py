@@ -3,7 +3,8 @@
 Restates cardgym/games/piquet/model.py: ``_onehot_bags`` 255-264 (every table's field sums
 as one GEMM of one-hot token rows against the tables side by side, in the autocast dtype
 or the tables' own) and the field part of ``PiquetEmbedding.forward`` 323-345 (ids =
-tokens[..., :NUM_FIELDS] + the per-field row offsets); ``CardScorer.forward`` 348-363. The field vocabularies restate
+tokens[..., :NUM_FIELDS] + the per-field row offsets); ``CardScorer.forward`` 348-363;
+``CardGrid`` 180-240 with ``GridBlock`` 129-177 and ``GridNorm`` 118-126. The field vocabularies restate
 cardgym/games/piquet/tokens.py:108-128 independently of the product's copy.
 """
 
@@ -59,3 +60,52 @@ def card_scorer(hidden: np.ndarray, grid: np.ndarray, w: dict) -> np.ndarray:
     normed = layer_norm(mixed, w["norm.weight"].astype(np.float64), w["norm.bias"].astype(np.float64))
     hid = gelu(normed @ w["hidden.weight"].T.astype(np.float64) + w["hidden.bias"])
     return (hid @ w["out.weight"].T.astype(np.float64) + w["out.bias"])[..., 0]
+
+
+NUM_SUITS, NUM_RANKS = 4, 8
+CARD_RANKS = np.arange(NUM_SUITS * NUM_RANKS) % NUM_RANKS  # card = suit * 8 + rank (piquet/cards.py)
+
+
+def grid_norm(x: np.ndarray, weight: np.ndarray, eps: float = 1e-5) -> np.ndarray:
+    """GridNorm: RMSNorm over the card width with a gain (fp32 statistics in the reference)."""
+
+    return x / np.sqrt((x * x).mean(axis=-1, keepdims=True) + eps) * weight
+
+
+def card_grid(codes: np.ndarray, w: dict, blocks: int = 2, kernel: int = 3, storage: str = "fp32"):
+    """``CardGrid.forward``: card codes [N, 32] -> (cards [N, 32, width], summary [N, d]).
+
+    ``storage="bf16"`` rounds where the reference's bf16 autocast does: every Linear / matmul
+    output (the rank convolution with its bias, the suit mean, the across-suit projection,
+    the output layer with its bias), their sum and the GELU; the residual grid, the norms and
+    the final features stay fp32. The summary projection is left to the caller's GEMM."""
+
+    f = lambda name: w[name].astype(np.float64)  # noqa: E731
+    rnd = (lambda x: round_to(x, "bf16")) if storage == "bf16" else (lambda x: x)  # noqa: E731
+    count = codes.shape[0]
+    grid = f("code.weight")[codes.astype(np.int64)] + f("rank.weight")[CARD_RANKS]
+    width = grid.shape[-1]
+    grid = grid.reshape(count, NUM_SUITS, NUM_RANKS, width)
+    half = kernel // 2
+    for b in range(blocks):
+        p = f"blocks.{b}."
+        rows = rnd(grid_norm(grid, f(p + "norm.weight")))  # autocast casts the GEMM input
+        conv = rnd(f(p + "along_rank.weight"))  # [hidden, width, kernel]
+        hidden = conv.shape[0]
+        along = np.zeros((count, NUM_SUITS, NUM_RANKS, hidden))
+        for tap in range(kernel):
+            for o in range(NUM_RANKS):
+                i = o + tap - half
+                if 0 <= i < NUM_RANKS:
+                    along[:, :, o, :] += rows[:, :, i, :] @ conv[:, :, tap].T
+        along = rnd(along + rnd(f(p + "along_rank.bias")))
+        pooled = rnd(rows.mean(axis=1))  # [N, ranks, width]
+        across = rnd(pooled @ rnd(f(p + "across_suits.weight")).T)  # [N, ranks, hidden]
+        mixed = rnd(along + across[:, None])
+        out = rnd(rnd(gelu(mixed)) @ rnd(f(p + "out.weight")).T + rnd(f(p + "out.bias")))
+        grid = grid + out
+    cards = grid_norm(grid, f("norm.weight")).reshape(count, NUM_SUITS * NUM_RANKS, width)
+    if "summary.weight" not in w:
+        return cards, None
+    summary = cards.reshape(count, -1) @ f("summary.weight").T
+    return cards, summary

@@ -22,6 +22,7 @@ Fixtures:
   piquet_bags.npz     the piquet field lookup (``_onehot_bags``) in fp32, bf16 and fp16
   card_scorer.npz     the piquet card pointer head (``CardScorer``) in fp32 and bf16 autocast
   candidate_scorer.npz the rummy candidate pointer head (``CandidateScorer``), draw and play calls
+  card_grid.npz       the piquet card grid (``CardGrid``) in fp32 and bf16 autocast
 
 ``python tests/golden/make_golden.py piquet_bags`` regenerates one fixture.
 """
@@ -411,6 +412,34 @@ def make_candidate_scorer() -> None:
                         **out, **state)
 
 
+def make_card_grid() -> None:
+    """``CardGrid.forward`` (piquet card grid: two grid blocks, final norm, summary) in fp32
+    and under bf16 autocast, on random card codes."""
+
+    from cardgym.games.piquet.model import CardGrid, PiquetModelConfig
+
+    torch.manual_seed(71)
+    grid = CardGrid(PiquetModelConfig())
+    with torch.no_grad():  # exercise the gains and biases the init leaves at 1 / 0
+        for block in grid.blocks:
+            block.norm.weight.uniform_(0.5, 1.5)
+            block.along_rank.bias.normal_(0.0, 0.05)
+            block.out.bias.normal_(0.0, 0.05)
+        grid.norm.weight.uniform_(0.5, 1.5)
+    grid.eval()
+    codes = torch.from_numpy(np.random.default_rng(72).integers(0, 12, (40, 32)))
+    with torch.no_grad():
+        cards, summary = grid(codes)
+        with torch.autocast("cpu", dtype=torch.bfloat16):
+            cards16, summary16 = grid(codes)
+    # The summary is one plain projection of the flattened cards (a library GEMM here): the
+    # fixture keeps the cards, not the 1 MB summary weight.
+    del summary, summary16
+    state = {f"w_{k}": v.numpy() for k, v in grid.state_dict().items() if not k.startswith("summary")}
+    np.savez_compressed(HERE / "card_grid.npz", codes=codes.numpy().astype(np.int8), cards=cards.numpy(),
+                        cards_bf16=cards16.float().numpy(), **state)
+
+
 def main() -> None:
     only = set(sys.argv[1:])
     if only:
@@ -431,6 +460,7 @@ def main() -> None:
     make_piquet_bags()
     make_card_scorer()
     make_candidate_scorer()
+    make_card_grid()
     for path in sorted(HERE.glob("*.npz")):
         print(f"{path.name}: {path.stat().st_size / 1024:.0f} KiB")
 

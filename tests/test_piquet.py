@@ -231,3 +231,59 @@ def test_piquet_decode_with_the_fused_lookup_tracks_the_oracle(precision):
         want = oracle.forward_ragged(x, ple, values, ocache, positions, offsets)
         err = np.abs(got - want).max()
         assert (err / np.abs(want).max() < tol) if precision == "bf16" else err < tol, (t, err)
+
+
+def _grid_weights(data: dict) -> dict:
+    return {k[2:]: v for k, v in data.items() if k.startswith("w_")}
+
+
+def test_card_grid_oracle_matches_the_reference():
+    data = load_golden("card_grid")
+    cards, _ = opiquet.card_grid(data["codes"], _grid_weights(data))
+    np.testing.assert_allclose(cards, data["cards"], atol=1e-5, rtol=0)
+    # The bf16-autocast form: the oracle rounds where the reference does.
+    cards16, _ = opiquet.card_grid(data["codes"], _grid_weights(data), storage="bf16")
+    assert np.abs(cards16 - data["cards_bf16"]).max() < 2e-3 < np.abs(data["cards_bf16"] - data["cards"]).max()
+
+
+@pytest.mark.gpu
+def test_card_grid_matches_the_reference_autocast_form():
+    from card_playing_gym_b200 import _native as nat
+    from card_playing_gym_b200.piquet import CardGrid
+
+    data = load_golden("card_grid")
+    grid = CardGrid(_grid_weights(data))
+    assert nat.fault_status() == 0
+    # The codes as a slice of token rows (stride 64), the collector's int16 storage.
+    tokens = np.zeros((data["codes"].shape[0], 64), dtype=np.int16)
+    tokens[:, 32:] = data["codes"]
+    cards = grid.cards(torch.from_numpy(tokens).cuda()[:, 32:]).cpu().numpy()
+    want16, fp32 = data["cards_bf16"], data["cards"]
+    # bf16 rounding points as the reference's autocast: no farther from its autocast result
+    # than that result is from fp32 (an intermediate that rounds the other way at a bf16 tie
+    # moves a few features by one bf16 step), and on average far closer.
+    assert np.abs(cards - want16).max() <= np.abs(want16 - fp32).max()
+    assert np.abs(cards - want16).mean() < 0.1 * np.abs(want16 - fp32).mean()
+    assert np.abs(cards - fp32).max() <= 1.5 * np.abs(want16 - fp32).max()
+    assert nat.fault_status() == 0
+    # Out-of-vocabulary codes are flagged.
+    bad = tokens.copy()
+    bad[3, 40] = 12
+    grid.cards(torch.from_numpy(bad).cuda()[:, 32:])
+    assert nat.fault_status() == 0x230
+
+
+@pytest.mark.gpu
+def test_card_grid_at_wave_size_matches_the_oracle():
+    from card_playing_gym_b200.piquet import CardGrid
+
+    data = load_golden("card_grid")
+    weights = _grid_weights(data)
+    codes = np.random.default_rng(4).integers(0, 12, (4096, 32))
+    cards = CardGrid(weights)(torch.from_numpy(codes).cuda())[0].cpu().numpy()
+    sample = slice(0, 4096, 41)
+    want, _ = opiquet.card_grid(codes[sample], weights, storage="bf16")
+    diff = np.abs(cards[sample] - want)
+    # Identical roundings but for the rare intermediate at a bf16 tie (fp32 sums here, exact
+    # ones in the oracle), which moves a token's features by about one bf16 step.
+    assert (diff > 1e-5).mean() < 0.02 and diff.mean() < 1e-4 and diff.max() < 0.04
