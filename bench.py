@@ -386,7 +386,7 @@ def run_pointer_wave(args, device, rank: int, world_size: int, kind: str) -> dic
 
     from card_playing_gym_b200 import _native as nat
     from card_playing_gym_b200.config import PIQUET_SCALE, PlumpModelConfig, synthetic_plump_actor_state
-    from card_playing_gym_b200.piquet import FIELD_ROWS, FIELD_VOCAB, CardScorer, PiquetFieldLookup
+    from card_playing_gym_b200.piquet import FIELD_ROWS, FIELD_VOCAB, CardGrid, CardScorer, PiquetFieldLookup
     from card_playing_gym_b200.piquet import forward_ragged as piquet_forward
     from card_playing_gym_b200.rummy import NO_CARD, CandidateScorer
     from card_playing_gym_b200.sampling import masked_sample
@@ -413,6 +413,7 @@ def run_pointer_wave(args, device, rank: int, world_size: int, kind: str) -> dic
     tokens = np.zeros((decoded, 1, 64), dtype=np.int16)
     for field, vocab in enumerate(FIELD_VOCAB):
         tokens[:, 0, field] = rng.integers(0, vocab, decoded)
+    tokens[:, 0, 32:] = rng.integers(0, 12, (decoded, 32))  # card codes (the piquet card grid's input)
     rows = np.sort(rng.choice(slots, decoded, replace=False)) if decoded < slots else np.arange(slots)
     positions = (lengths[rows] - 1).astype(np.int64)
     dev_tokens = torch.from_numpy(tokens).to(device)
@@ -427,11 +428,21 @@ def run_pointer_wave(args, device, rank: int, world_size: int, kind: str) -> dic
             "query.weight": (64, d), "query.bias": (64,), "card.weight": (64, 32), "card_id.weight": (32, 64),
             "norm.weight": (64,), "norm.bias": (64,), "hidden.weight": (64, 64), "hidden.bias": (64,),
             "out.weight": (1, 64), "out.bias": (1,)}), device=device)
-        grid = torch.randn(decisions, cards, 32, device=device, generator=gen).to(torch.bfloat16)
+        grid_shapes = {"code.weight": (12, 32), "rank.weight": (8, 32), "norm.weight": (32,),
+                       "summary.weight": (d, 32 * 32)}
+        for b in range(2):
+            grid_shapes.update({f"blocks.{b}.norm.weight": (32,), f"blocks.{b}.along_rank.weight": (64, 32, 3),
+                                f"blocks.{b}.along_rank.bias": (64,), f"blocks.{b}.across_suits.weight": (64, 32),
+                                f"blocks.{b}.out.weight": (32, 64), f"blocks.{b}.out.bias": (32,)})
+        grid_state = score_state(grid_shapes)
+        for name in ("norm.weight", "blocks.0.norm.weight", "blocks.1.norm.weight"):
+            grid_state[name] = np.ones_like(grid_state[name])
+        card_grid = CardGrid(grid_state, device=device)
         legal = torch.from_numpy(rng.random((decisions, cards)) < 0.4).to(device)
         legal[:, 0] = True
         width = cards
-        head = lambda hidden: scorer(hidden, grid)  # noqa: E731
+        card_features = {}
+        head = lambda hidden: scorer(hidden, card_features["cards"].index_select(0, readout))  # noqa: E731
     else:
         decisions = decoded // 3
         readout = torch.from_numpy(np.sort(rng.choice(decoded, decisions, replace=False))).to(device)
@@ -455,8 +466,13 @@ def run_pointer_wave(args, device, rank: int, world_size: int, kind: str) -> dic
     uniforms = torch.from_numpy(rng.random(decisions)).to(device)
 
     def step():
+        summary = None
+        if kind == "piquet":  # PiquetEmbedding: the card grid's features and summary of every token
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                cards_all, summary = card_grid(dev_tokens[:, :, 32:])
+            card_features["cards"] = cards_all[:, -1]
         hidden = piquet_forward(trunk, lookup, dev_tokens, dev_positions, cache, offsets, span=max_len + 1,
-                                rows=dev_rows)
+                                rows=dev_rows, summary=summary)
         logits = head(hidden.index_select(0, readout))
         return masked_sample(logits, legal, uniforms)
 
@@ -479,8 +495,8 @@ def run_pointer_wave(args, device, rank: int, world_size: int, kind: str) -> dic
         ms = float(t.item())
     desc = {
         "piquet": (f"piquet decode wave: {decisions} deals ({decoded} KV rows, 1 token/row), lengths U[{min_len},{max_len}],"
-                   " fp16 KV, one-hot field lookup (32 fields, 964 rows) fused into the trunk d256/16L/8-2/d_ff 512 -> "
-                   "CardScorer over 32 cards -> masked sampling (grid features synthetic)"),
+                   " fp16 KV, card grid (2 blocks) + summary, one-hot field lookup (32 fields, 964 rows) fused into the "
+                   "trunk d256/16L/8-2/d_ff 512 -> CardScorer over the readout's 32 card features -> masked sampling"),
         "rummy": (f"rummy-style continuous wave: {slots} slots, {decoded} gathered rows decoded (1 token/row), lengths "
                   f"U[{min_len},{max_len}], fp16 KV, one-hot field lookup fused into the trunk d256/8L/8-2/d_ff 768 -> "
                   f"CandidateScorer over U[1,64] candidates (padded to {width}) -> masked sampling (grid features "
