@@ -82,7 +82,8 @@ class CandidateScorerWeights(ctypes.Structure):
 class CardGridWeights(ctypes.Structure):
     _fields_ = [
         ("width", ctypes.c_int32), ("hidden", ctypes.c_int32), ("kernel", ctypes.c_int32), ("blocks", ctypes.c_int32),
-        ("codes", ctypes.c_int32), ("code_emb", ctypes.c_void_p), ("rank_emb", ctypes.c_void_p),
+        ("codes", ctypes.c_int32), ("ranks", ctypes.c_int32), ("circular", ctypes.c_int32),
+        ("code_emb", ctypes.c_void_p), ("rank_emb", ctypes.c_void_p),
     ] + [(name, ctypes.c_void_p * 4) for name in ("norm_w", "conv_w", "conv_b", "across_w", "out_w", "out_b")] + [
         ("final_norm", ctypes.c_void_p),
     ]

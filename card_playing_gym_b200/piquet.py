@@ -186,13 +186,17 @@ def forward_ragged(trunk, lookup: PiquetFieldLookup, tokens: torch.Tensor, posit
 class CardGrid:
     """``CardGrid``: card codes [..., 32] -> (cards fp32 [..., 32, width], summary [..., d]).
 
+    Rummy's ledger grid (cardgym/games/rummy/model.py:166-230: 52 codes, 13 ranks, a circular
+    5-tap convolution) is the same class built from that module's parameters.
+
     Built from the reference module's parameters (``prefix + "code.weight"`` etc., as in a
     PiquetActor ``state_dict`` with prefix ``"embedding.grid."``). ``cards`` is computed as the
     reference computes it under bf16 autocast (its rollout precision); ``forward`` adds the
     summary projection with torch, honouring the caller's autocast state like the reference.
     """
 
-    def __init__(self, state: dict, prefix: str = "", device: torch.device | str = "cuda", blocks: int | None = None):
+    def __init__(self, state: dict, prefix: str = "", device: torch.device | str = "cuda", blocks: int | None = None,
+                 circular: bool | None = None):
         get = lambda name: torch.as_tensor(state[prefix + name]).detach().to(device=device, dtype=torch.float32).contiguous()  # noqa: E731
         if blocks is None:
             blocks = 0
@@ -204,8 +208,12 @@ class CardGrid:
         self.blocks = [{n: get(f"blocks.{b}.{n}") for n in names} for b in range(blocks)]
         width = self.params["code"].shape[1]
         hidden, _, taps = self.blocks[0]["along_rank.weight"].shape if blocks else (64, width, 3)
+        ranks = self.params["rank"].shape[0]
         w = nat.CardGridWeights()
         w.width, w.hidden, w.kernel, w.blocks, w.codes = width, hidden, taps, blocks, self.params["code"].shape[0]
+        # Piquet's 8-rank grid pads with zeros; rummy's 13-rank ledger grid wraps around.
+        w.ranks, w.circular = ranks, int(ranks == 13 if circular is None else circular)
+        self.cards_per_token = 4 * ranks
         w.code_emb, w.rank_emb, w.final_norm = (nat.ptr(self.params[k]) for k in ("code", "rank", "norm"))
         for b, blk in enumerate(self.blocks):
             w.norm_w[b] = nat.ptr(blk["norm.weight"])
@@ -218,7 +226,7 @@ class CardGrid:
         self.width = width
 
     def cards(self, codes: torch.Tensor) -> torch.Tensor:
-        """Per-card features [..., 32, width] of card codes [..., 32] (any view of token rows)."""
+        """Per-card features [..., cards, width] of card codes [..., cards] (any view of token rows)."""
 
         lead = codes.shape[:-1]
         flat = codes.reshape(-1, codes.shape[-1])
@@ -227,10 +235,11 @@ class CardGrid:
         if flat.stride(-1) != 1:
             flat = flat.contiguous()
         count = flat.shape[0]
-        out = torch.empty((count, 32, self.width), dtype=torch.float32, device=flat.device)
+        cards = self.cards_per_token
+        out = torch.empty((count, cards, self.width), dtype=torch.float32, device=flat.device)
         nat.call("cg_card_grid", self.weights, nat.ptr(flat), nat.INDEX_CODES[flat.dtype], count, flat.stride(0),
                  nat.ptr(out), nat.stream_handle(flat.device))
-        return out.view(*lead, 32, self.width)
+        return out.view(*lead, cards, self.width)
 
     def __call__(self, codes: torch.Tensor):
         cards = self.cards(codes)

@@ -179,20 +179,22 @@ int cg_bags_forward_ragged(const cg_trunk_dims* dims, const void* blob, const vo
                            int64_t workspace_bytes, float* hidden_out, void* stream);
 
 /* ---------------------------------------------------------------------------------
- * Piquet card grid (cardgym/games/piquet/model.py:180-240 `CardGrid.cards`, with
- * GridBlock 129-177 and GridNorm 118-126): a token's 32 card codes (card = suit * 8 + rank)
- * -> per-card features fp32 [n, 32, width] after `blocks` residual grid blocks and the final
+ * Card grid (cardgym/games/piquet/model.py:180-240 `CardGrid.cards`, with GridBlock
+ * 129-177 and GridNorm 118-126; rummy's ledger grid, cardgym/games/rummy/model.py:112-225):
+ * a token's 4 * ranks card codes (card = suit * ranks + rank) -> per-card features fp32
+ * [n, 4 * ranks, width] after `blocks` residual grid blocks and the final
  * RMSNorm, computed as the reference computes it under bf16 autocast (bf16 GEMM operands,
  * fp32 accumulation, every Linear/matmul output, their sum and the GELU rounded to bf16; the
- * residual grid and the norms in fp32). width 32, hidden 64, 3 rank taps, blocks <= 4,
- * code vocabulary <= 16. codes: n rows of codes_stride ids (CG_I16/I32/I64), the 32 card
- * codes first (tokens + CARD_START). A code outside the vocabulary sets the fault word 0x230.
+ * residual grid and the norms in fp32). width 32, hidden 64, blocks <= 4. codes: n rows of
+ * codes_stride ids (CG_I16/I32/I64), the card codes first (tokens + CARD_START). A code
+ * outside the vocabulary sets the fault word 0x230.
  * The summary projection (a plain [32 * width -> d] Linear) stays with the caller's GEMM.
  * ------------------------------------------------------------------------------- */
 typedef struct {
   int32_t width, hidden, kernel, blocks, codes;
+  int32_t ranks, circular;   /* 8 ranks, 3 zero-padded taps (piquet) or 13 ranks, 5 circular taps (rummy) */
   const float* code_emb;     /* [codes, width] */
-  const float* rank_emb;     /* [8, width] */
+  const float* rank_emb;     /* [ranks, width] */
   const float* norm_w[4];    /* per block: GridNorm gain [width] */
   const float* conv_w[4];    /* along_rank Conv1d weight [hidden, width, 3] */
   const float* conv_b[4];    /* [hidden] */

@@ -72,31 +72,38 @@ def grid_norm(x: np.ndarray, weight: np.ndarray, eps: float = 1e-5) -> np.ndarra
     return x / np.sqrt((x * x).mean(axis=-1, keepdims=True) + eps) * weight
 
 
-def card_grid(codes: np.ndarray, w: dict, blocks: int = 2, kernel: int = 3, storage: str = "fp32"):
+def card_grid(codes: np.ndarray, w: dict, blocks: int = 2, kernel: int = 3, storage: str = "fp32",
+              ranks: int = NUM_RANKS, circular: bool = False):
     """``CardGrid.forward``: card codes [N, 32] -> (cards [N, 32, width], summary [N, d]).
 
     ``storage="bf16"`` rounds where the reference's bf16 autocast does: every Linear / matmul
     output (the rank convolution with its bias, the suit mean, the across-suit projection,
     the output layer with its bias), their sum and the GELU; the residual grid, the norms and
-    the final features stay fp32. The summary projection is left to the caller's GEMM."""
+    the final features stay fp32. The summary projection is left to the caller's GEMM.
+
+    ``ranks=13, kernel=5, circular=True`` is rummy's ledger grid (cardgym/games/rummy/model.py:
+    112-225): 52 cards, a circular convolution along the ranks."""
 
     f = lambda name: w[name].astype(np.float64)  # noqa: E731
     rnd = (lambda x: round_to(x, "bf16")) if storage == "bf16" else (lambda x: x)  # noqa: E731
     count = codes.shape[0]
-    grid = f("code.weight")[codes.astype(np.int64)] + f("rank.weight")[CARD_RANKS]
+    card_ranks = np.arange(NUM_SUITS * ranks) % ranks
+    grid = f("code.weight")[codes.astype(np.int64)] + f("rank.weight")[card_ranks]
     width = grid.shape[-1]
-    grid = grid.reshape(count, NUM_SUITS, NUM_RANKS, width)
+    grid = grid.reshape(count, NUM_SUITS, ranks, width)
     half = kernel // 2
     for b in range(blocks):
         p = f"blocks.{b}."
         rows = rnd(grid_norm(grid, f(p + "norm.weight")))  # autocast casts the GEMM input
         conv = rnd(f(p + "along_rank.weight"))  # [hidden, width, kernel]
         hidden = conv.shape[0]
-        along = np.zeros((count, NUM_SUITS, NUM_RANKS, hidden))
+        along = np.zeros((count, NUM_SUITS, ranks, hidden))
         for tap in range(kernel):
-            for o in range(NUM_RANKS):
+            for o in range(ranks):
                 i = o + tap - half
-                if 0 <= i < NUM_RANKS:
+                if circular:
+                    i %= ranks
+                if 0 <= i < ranks:
                     along[:, :, o, :] += rows[:, :, i, :] @ conv[:, :, tap].T
         along = rnd(along + rnd(f(p + "along_rank.bias")))
         pooled = rnd(rows.mean(axis=1))  # [N, ranks, width]
@@ -104,7 +111,7 @@ def card_grid(codes: np.ndarray, w: dict, blocks: int = 2, kernel: int = 3, stor
         mixed = rnd(along + across[:, None])
         out = rnd(rnd(gelu(mixed)) @ rnd(f(p + "out.weight")).T + rnd(f(p + "out.bias")))
         grid = grid + out
-    cards = grid_norm(grid, f("norm.weight")).reshape(count, NUM_SUITS * NUM_RANKS, width)
+    cards = grid_norm(grid, f("norm.weight")).reshape(count, NUM_SUITS * ranks, width)
     if "summary.weight" not in w:
         return cards, None
     summary = cards.reshape(count, -1) @ f("summary.weight").T

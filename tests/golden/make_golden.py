@@ -23,6 +23,7 @@ Fixtures:
   card_scorer.npz     the piquet card pointer head (``CardScorer``) in fp32 and bf16 autocast
   candidate_scorer.npz the rummy candidate pointer head (``CandidateScorer``), draw and play calls
   card_grid.npz       the piquet card grid (``CardGrid``) in fp32 and bf16 autocast
+  ledger_grid.npz     rummy's ledger grid (52 cards, circular 5-tap convolution), same forms
 
 ``python tests/golden/make_golden.py piquet_bags`` regenerates one fixture.
 """
@@ -440,6 +441,32 @@ def make_card_grid() -> None:
                         cards_bf16=cards16.float().numpy(), **state)
 
 
+def make_ledger_grid() -> None:
+    """Rummy's ledger grid (``CardGrid`` of cardgym/games/rummy/model.py: 52 cards, 13 ranks,
+    a 5-tap circular convolution) in fp32 and under bf16 autocast."""
+
+    from cardgym.games.rummy.model import CardGrid, RummyModelConfig
+    from cardgym.games.rummy.tokens import CARD_VOCAB
+
+    torch.manual_seed(81)
+    grid = CardGrid(RummyModelConfig())
+    with torch.no_grad():
+        for block in grid.blocks:
+            block.norm.weight.uniform_(0.5, 1.5)
+            block.along_rank.bias.normal_(0.0, 0.05)
+            block.out.bias.normal_(0.0, 0.05)
+        grid.norm.weight.uniform_(0.5, 1.5)
+    grid.eval()
+    codes = torch.from_numpy(np.random.default_rng(82).integers(0, CARD_VOCAB, (24, 52)))
+    with torch.no_grad():
+        cards = grid.cards(codes)
+        with torch.autocast("cpu", dtype=torch.bfloat16):
+            cards16 = grid.cards(codes)
+    state = {f"w_{k}": v.numpy() for k, v in grid.state_dict().items() if not k.startswith("summary")}
+    np.savez_compressed(HERE / "ledger_grid.npz", codes=codes.numpy().astype(np.int16), cards=cards.numpy(),
+                        cards_bf16=cards16.float().numpy(), **state)
+
+
 def main() -> None:
     only = set(sys.argv[1:])
     if only:
@@ -461,6 +488,7 @@ def main() -> None:
     make_card_scorer()
     make_candidate_scorer()
     make_card_grid()
+    make_ledger_grid()
     for path in sorted(HERE.glob("*.npz")):
         print(f"{path.name}: {path.stat().st_size / 1024:.0f} KiB")
 

@@ -72,3 +72,41 @@ def test_candidate_scorer_flags_bad_ids():
             bad_kind[1, 2] = value
         scorer(cuda(hidden), cuda(grid), cuda(bad_kind), cuda(bad_cards), cuda(target))
         assert nat.fault_status() == code
+
+
+def _ledger_weights(data: dict) -> dict:
+    return {k[2:]: v for k, v in data.items() if k.startswith("w_")}
+
+
+def test_ledger_grid_oracle_matches_the_reference():
+    from oracle import piquet as opiquet
+
+    data = load_golden("ledger_grid")
+    cards, _ = opiquet.card_grid(data["codes"], _ledger_weights(data), kernel=5, ranks=13, circular=True)
+    np.testing.assert_allclose(cards, data["cards"], atol=1e-5, rtol=0)
+
+
+@pytest.mark.gpu
+def test_ledger_grid_matches_the_reference_autocast_form():
+    """Rummy's ledger grid (52 cards, circular 5-tap convolution) through cg_card_grid: as close to
+    the reference's bf16-autocast result as one bf16 step of a rare tie-rounded intermediate."""
+
+    from card_playing_gym_b200 import _native as nat
+    from card_playing_gym_b200.piquet import CardGrid
+    from oracle import piquet as opiquet
+
+    data = load_golden("ledger_grid")
+    weights = _ledger_weights(data)
+    grid = CardGrid(weights)
+    assert nat.fault_status() == 0
+    tokens = np.zeros((data["codes"].shape[0], 78), dtype=np.int16)
+    tokens[:, 26:] = data["codes"]  # the ledger codes sit after rummy's 26 token fields
+    cards = grid.cards(torch.from_numpy(tokens).cuda()[:, 26:]).cpu().numpy()
+    want16, fp32 = data["cards_bf16"], data["cards"]
+    assert cards.shape == fp32.shape
+    assert np.abs(cards - want16).max() <= np.abs(want16 - fp32).max()
+    assert np.abs(cards - want16).mean() < 0.1 * np.abs(want16 - fp32).mean()
+    oracle16, _ = opiquet.card_grid(data["codes"], weights, kernel=5, ranks=13, circular=True, storage="bf16")
+    diff = np.abs(cards - oracle16)
+    assert (diff > 1e-5).mean() < 0.02 and diff.mean() < 1e-4
+    assert nat.fault_status() == 0
