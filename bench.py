@@ -454,7 +454,18 @@ def run_pointer_wave(args, device, rank: int, world_size: int, kind: str) -> dic
             "taken_id.weight": (52, 64), "kind.weight": (7, 64), "size.weight": (14, 64), "norm.weight": (64,),
             "norm.bias": (64,), "hidden.weight": (64, 64), "hidden.bias": (64,), "out.weight": (1, 64),
             "out.bias": (1,)}), device=device)
-        grid = torch.randn(decisions, 52, 32, device=device, generator=gen).to(torch.bfloat16)
+        ledger_shapes = {"code.weight": (570, 32), "rank.weight": (13, 32), "norm.weight": (32,),
+                         "summary.weight": (d, 52 * 32)}
+        for b in range(2):
+            ledger_shapes.update({f"blocks.{b}.norm.weight": (32,), f"blocks.{b}.along_rank.weight": (64, 32, 5),
+                                  f"blocks.{b}.along_rank.bias": (64,), f"blocks.{b}.across_suits.weight": (64, 32),
+                                  f"blocks.{b}.out.weight": (32, 64), f"blocks.{b}.out.bias": (32,)})
+        ledger_state = score_state(ledger_shapes)
+        for name in ("norm.weight", "blocks.0.norm.weight", "blocks.1.norm.weight"):
+            ledger_state[name] = np.ones_like(ledger_state[name])
+        card_grid = CardGrid(ledger_state, device=device)
+        ledger = torch.from_numpy(rng.integers(0, 570, (decoded, 1, 52)).astype(np.int16)).to(device)
+        card_features = {}
         cand_kind = torch.from_numpy(rng.integers(0, 7, (decisions, width))).to(device)
         cand_cards = np.full((decisions, width, 13), NO_CARD, dtype=np.int64)
         cand_cards[..., :3] = rng.integers(0, 52, (decisions, width, 3))
@@ -462,15 +473,16 @@ def run_pointer_wave(args, device, rank: int, world_size: int, kind: str) -> dic
         cand_target = np.full((decisions, width, 13), NO_CARD, dtype=np.int64)
         cand_cards, cand_target = torch.from_numpy(cand_cards).to(device), torch.from_numpy(cand_target).to(device)
         legal = torch.from_numpy(np.arange(width)[None, :] < counts[:, None]).to(device)
-        head = lambda hidden: scorer(hidden, grid, cand_kind, cand_cards, cand_target)  # noqa: E731
+        head = lambda hidden: scorer(hidden, card_features["cards"].index_select(0, readout), cand_kind,  # noqa: E731
+                                     cand_cards, cand_target)
     uniforms = torch.from_numpy(rng.random(decisions)).to(device)
 
     def step():
-        summary = None
-        if kind == "piquet":  # PiquetEmbedding: the card grid's features and summary of every token
-            with torch.autocast("cuda", dtype=torch.bfloat16):
-                cards_all, summary = card_grid(dev_tokens[:, :, 32:])
-            card_features["cards"] = cards_all[:, -1]
+        # The embedder's card grid (piquet) or ledger grid (rummy): every token's card features
+        # and their summary, added to the field sums.
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            cards_all, summary = card_grid(dev_tokens[:, :, 32:] if kind == "piquet" else ledger)
+        card_features["cards"] = cards_all[:, -1]
         hidden = piquet_forward(trunk, lookup, dev_tokens, dev_positions, cache, offsets, span=max_len + 1,
                                 rows=dev_rows, summary=summary)
         logits = head(hidden.index_select(0, readout))
@@ -498,9 +510,9 @@ def run_pointer_wave(args, device, rank: int, world_size: int, kind: str) -> dic
                    " fp16 KV, card grid (2 blocks) + summary, one-hot field lookup (32 fields, 964 rows) fused into the "
                    "trunk d256/16L/8-2/d_ff 512 -> CardScorer over the readout's 32 card features -> masked sampling"),
         "rummy": (f"rummy-style continuous wave: {slots} slots, {decoded} gathered rows decoded (1 token/row), lengths "
-                  f"U[{min_len},{max_len}], fp16 KV, one-hot field lookup fused into the trunk d256/8L/8-2/d_ff 768 -> "
-                  f"CandidateScorer over U[1,64] candidates (padded to {width}) -> masked sampling (grid features "
-                  "synthetic)"),
+                  f"U[{min_len},{max_len}], fp16 KV, ledger grid (52 cards, 2 blocks) + summary, one-hot field lookup "
+                  f"(piquet's tables standing in for rummy's fields) fused into the trunk d256/8L/8-2/d_ff 768 -> "
+                  f"CandidateScorer over U[1,64] candidates (padded to {width}) -> masked sampling"),
     }[kind]
     return {"workload": desc, "value": world_size * decisions / (ms / 1000.0), "unit": "decisions/s",
             "rows_per_s": world_size * decoded / (ms / 1000.0), "ms_per_step": ms, "steps": args.pointer_steps}
