@@ -379,7 +379,9 @@ def run_pointer_wave(args, device, rank: int, world_size: int, kind: str) -> dic
     rummy: 8,192 slots, half of them decoded per wave through gathered rows (the continuous
       collector's form), lengths U[8, 384], trunk d256/8L/8-2/d_ff 768, one decision per three
       decoded rows scored by CandidateScorer over U[1, 64] candidates (padded to the wave's max).
-    The card-grid features the heads read are synthetic (the card grid is not on this path)."""
+    Each wave runs the embedder's grid over the decoded tokens first (piquet's card grid over the
+    tokens' card codes, rummy's ledger grid over a 52-card ledger) and fuses its summary into the
+    trunk's input; the heads read the readout token's grid cards."""
 
     import torch
     import torch.distributed as dist

@@ -1,0 +1,510 @@
+"""Continuous self-play collector: a fixed pool of games in flight, refilled as games end.
+
+Reference: cardgym/rl/continuous.py:55-408 (``Lane``, ``split_lanes``, ``ContinuousCollector``)
+and the helpers it takes from cardgym/rl/selfplay.py (``restart_contexts`` 172-190,
+``sample_decisions`` 532-567, ``_round_up`` 204-205). The host side keeps the reference's
+protocol: games implement ``SelfPlayGame`` (``prefix_tokens``, ``decision``, ``step``,
+``done``, ``returns``, ``context_starts``, a per-game ``rng``), each game owns one cache row
+per seat, a wave decodes only the rows that received tokens (gathered by index, padded to a
+multiple of ``ROW_BUCKET`` with entries that write a scratch row past every game's rows), and
+``cohorts = 2`` lets the host step one group of games while the device decodes the other's.
+
+What runs where. One wave is, on the device and in stream order: the host-packed inputs
+uploaded from pinned memory, one ``DecodeGraphs`` replay (field lookup, the ragged trunk
+decode into the KV pool, every head's logits and the per-seat values), a gather of the
+readout rows, legal-masked softmax and inverse-CDF sampling for each head group
+(``sampling.masked_sample``) and the copy of only the readouts' probabilities, actions and
+values back to pinned host memory, closed by one event. The host never sees logits.
+
+Uniforms. ``sample_decisions`` draws one ``game.rng.random()`` per decision after the wave's
+logits arrive. Here it is drawn when the wave is launched, which is after the game's
+``decision()`` and before its next ``step()`` exactly as there; every game owns its ``rng``
+(cardgym/games/*/selfplay.py seed ``^ 0x5EED``) and nothing else draws from it in between,
+so each game sees the same sequence of uniforms.
+"""
+
+from __future__ import annotations
+
+import random
+import time
+from collections import deque
+from collections.abc import Callable
+from dataclasses import dataclass, field, replace
+
+import numpy as np
+import torch
+
+ROW_BUCKET = 64
+SPAN_BUCKET = 32
+
+
+def round_up(value: int, multiple: int) -> int:
+    return -(-value // multiple) * multiple
+
+
+@dataclass
+class Decision:
+    """What the acting seat must choose now (selfplay.py:51-59)."""
+
+    seat: int
+    head: str
+    legal: np.ndarray  # bool [actions]; actions index the head's output
+    features: dict[str, np.ndarray] | None = None
+
+
+@dataclass
+class DecisionRecord:
+    """One sampled decision (selfplay.py:113-124)."""
+
+    seat: int
+    head: str
+    position: int  # readout index in the seat's own stream
+    action: int
+    probs: np.ndarray  # masked behaviour policy, float32 [actions]
+    features: dict[str, np.ndarray] | None = None
+    version: int = 0
+    value: np.ndarray | None = None
+
+
+@dataclass
+class Trajectory:
+    game: object
+    streams: list[np.ndarray]  # per absolute seat, [length, width]
+    decisions: list[DecisionRecord]
+    returns: np.ndarray
+
+
+@dataclass
+class CollectionStats:
+    """The reference's counters (selfplay.py:134-150)."""
+
+    games: int = 0
+    decisions: int = 0
+    waves: int = 0
+    forward_rows: int = 0
+    padded_rows: int = 0
+    peak_rows: int = 0
+    compactions: int = 0
+    collect_sec: float = 0.0
+    forward_sec: float = 0.0  # host time preparing and launching device work
+    wait_sec: float = 0.0  # host time blocked on the device
+    sample_sec: float = 0.0
+    step_sec: float = 0.0
+    in_flight: int = 0
+    policy_lag: float = 0.0
+
+
+@dataclass(frozen=True)
+class Lane:
+    """One kind of game kept running (continuous.py:55-70).
+
+    ``deal(rng)`` returns a fresh game, or None once a finite source is spent. With
+    ``quota = None`` the lane runs until its source is spent and every game has ended;
+    otherwise each collection returns exactly ``quota`` finished games from it.
+    """
+
+    name: str
+    players: int  # cache rows per game
+    in_flight: int
+    quota: int | None
+    deal: Callable[[random.Random], object | None] = field(compare=False)
+
+
+def split_lanes(lanes: list[Lane], index: int, count: int) -> list[Lane]:
+    """Worker ``index`` of ``count``'s share of each lane's quota and games in flight
+    (continuous.py:73-89); shares differ by at most one game, empty shares are left out."""
+
+    shares = []
+    for lane in lanes:
+        if lane.quota is None:
+            raise ValueError("Only lanes with a quota can be split between workers.")
+        quota = lane.quota // count + (index < lane.quota % count)
+        in_flight = lane.in_flight // count + (index < lane.in_flight % count)
+        if quota > 0:
+            shares.append(replace(lane, quota=quota, in_flight=max(1, in_flight)))
+    return shares
+
+
+@dataclass
+class LiveGame:
+    """A game in flight (selfplay.py:153-169)."""
+
+    game: object
+    base: int  # first cache row
+    lengths: np.ndarray  # per observer cached tokens
+    blocks: list[list[np.ndarray]]  # per observer recorded blocks
+    decisions: list[DecisionRecord] = field(default_factory=list)
+    pending: Decision | None = None
+    readout: np.ndarray | None = None  # the pending actor's last token
+    offsets: np.ndarray | None = None  # per observer, stream tokens before its current context
+
+    def __post_init__(self) -> None:
+        if self.offsets is None:
+            self.offsets = np.zeros_like(self.lengths)
+
+
+def restart_contexts(state: LiveGame, blocks: list[np.ndarray]) -> list[np.ndarray]:
+    """Apply the game's context restarts after a step; returns the blocks to decode
+    (selfplay.py:172-190). A restarted observer's cached length drops to zero: the new
+    context is written from position 0 and causal attention never reaches the stale keys."""
+
+    starts = state.game.context_starts()
+    if starts is None:
+        return blocks
+    decoded = list(blocks)
+    for seat, start in enumerate(starts):
+        if start is None:
+            continue
+        state.offsets[seat] += state.lengths[seat] + start
+        state.lengths[seat] = 0
+        decoded[seat] = blocks[seat][start:]
+    return decoded
+
+
+@dataclass
+class PackedWave:
+    tokens: np.ndarray  # int64 [rows, run, width]
+    positions: np.ndarray  # int64 [rows]
+    offsets: np.ndarray  # int64 [rows], each row's last real token
+    cache_rows: np.ndarray  # int64 [rows]
+    span: int
+    count: int  # real entries; the rest write the scratch row
+
+
+def pack_wave(entries: list[tuple[int, int, np.ndarray]], scratch: int, row_bucket: int = ROW_BUCKET,
+              span_bucket: int = SPAN_BUCKET) -> PackedWave:
+    """Pack (cache row, position, token block) entries into one wave (continuous.py:316-331).
+
+    Rows are padded to a multiple of ``row_bucket`` with zero tokens at position 0 of the
+    scratch row; a block shorter than the wave's run repeats its last token; the span is the
+    furthest position written, rounded up to ``span_bucket``. One gather over the
+    concatenated blocks replaces the reference's per-entry copy loop.
+    """
+
+    count = len(entries)
+    lengths = np.fromiter((len(block) for _, _, block in entries), dtype=np.int64, count=count)
+    if count == 0 or lengths.min() < 1:
+        raise ValueError("every entry needs at least one token")
+    run = int(lengths.max())
+    rows = round_up(count, row_bucket)
+    width = entries[0][2].shape[1]
+    flat = np.concatenate([block for _, _, block in entries], axis=0).astype(np.int64, copy=False)
+    starts = np.cumsum(lengths) - lengths
+    gather = starts[:, None] + np.minimum(np.arange(run)[None, :], lengths[:, None] - 1)
+    tokens = np.zeros((rows, run, width), dtype=np.int64)
+    tokens[:count] = flat[gather]
+    cache_rows = np.full(rows, scratch, dtype=np.int64)
+    cache_rows[:count] = np.fromiter((row for row, _, _ in entries), dtype=np.int64, count=count)
+    positions = np.zeros(rows, dtype=np.int64)
+    positions[:count] = np.fromiter((position for _, position, _ in entries), dtype=np.int64, count=count)
+    offsets = np.zeros(rows, dtype=np.int64)
+    offsets[:count] = lengths - 1
+    span = round_up(int(positions.max()) + run, span_bucket)
+    return PackedWave(tokens, positions, offsets, cache_rows, span, count)
+
+
+@dataclass
+class _Readout:
+    """One head group's sampled decisions on their way to the host."""
+
+    states: list[LiveGame]
+    probs: torch.Tensor  # pinned fp32 [n, head width]
+    actions: torch.Tensor  # pinned int64 [n]
+    values: torch.Tensor | None  # pinned fp32 [n, seats]
+
+
+@dataclass
+class _Wave:
+    readouts: list[_Readout] = field(default_factory=list)
+    fence: torch.cuda.Event | None = None
+
+
+def _pinned(array: np.ndarray, device: torch.device) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(array)).pin_memory().to(device, non_blocking=True)
+
+
+class DeviceWaves:
+    """A wave's device half: graph replay, readout gather, masked sampling, readout copy-back.
+
+    ``launch`` enqueues everything on the current stream and returns at once; ``receive``
+    waits on the wave's event and hands every state its sampled decision.
+    """
+
+    def __init__(self, model, cache, *, values: bool) -> None:
+        from .graphs import DecodeGraphs
+
+        self.graphs = DecodeGraphs(model, cache, values=values)
+        self.values = values
+        self.device = cache.device
+
+    def launch(self, wave: PackedWave, readouts: list[tuple[int, LiveGame, float]]) -> _Wave:
+        from .sampling import masked_sample
+
+        output = self.graphs.run(wave.tokens, wave.positions, wave.offsets, wave.cache_rows, wave.span)
+        columns = self.graphs.columns
+        groups: dict[str, list[tuple[int, LiveGame, float]]] = {}
+        for entry in readouts:
+            groups.setdefault(entry[1].pending.head, []).append(entry)
+        result = _Wave()
+        for head, group in groups.items():
+            head_columns = columns[head]
+            width = head_columns.stop - head_columns.start
+            legal = np.zeros((len(group), width), dtype=np.uint8)
+            for row, (_, state, _) in enumerate(group):
+                mask = state.pending.legal
+                if mask.shape[0] > width:
+                    raise ValueError(f"head {head!r} has {width} actions, a decision offers {mask.shape[0]}")
+                legal[row, : mask.shape[0]] = mask
+            index = _pinned(np.fromiter((entry for entry, _, _ in group), dtype=np.int64, count=len(group)),
+                            self.device)
+            uniforms = _pinned(np.fromiter((u for _, _, u in group), dtype=np.float64, count=len(group)),
+                               self.device)
+            selected = output.index_select(0, index)
+            probs, actions = masked_sample(selected[:, head_columns], _pinned(legal, self.device), uniforms)
+            values = selected[:, columns["values"]].to("cpu", non_blocking=True) if self.values else None
+            result.readouts.append(_Readout([state for _, state, _ in group], probs.to("cpu", non_blocking=True),
+                                            actions.to("cpu", non_blocking=True), values))
+        result.fence = torch.cuda.Event()
+        result.fence.record()
+        return result
+
+    @staticmethod
+    def wait(wave: _Wave) -> None:
+        if wave.fence is not None:
+            wave.fence.synchronize()
+
+
+class ContinuousCollector:
+    """Keeps every lane's ``in_flight`` games running; ``collect`` returns each lane's quota
+    of finished games (continuous.py:115-408). Games still running carry over, with their
+    cache rows, into the next call. ``policy_lag`` in the stats reports how many versions old
+    the returned decisions are."""
+
+    ROW_BUCKET = ROW_BUCKET
+    SPAN_BUCKET = SPAN_BUCKET
+
+    def __init__(self, model, *, device: torch.device | str = "cuda", precision: str | None = None,
+                 kv_dtype: str | torch.dtype = "fp16", max_length: int, cohorts: int = 1,
+                 record_values: bool = False, waves_factory=None) -> None:
+        if precision is not None and precision != getattr(model, "precision", precision):
+            raise ValueError(f"the model runs in {model.precision}, not {precision}")
+        self.model = model
+        self.device = torch.device(device)
+        self.record_values = record_values
+        dtypes = {"fp16": torch.float16, "bf16": torch.bfloat16, "fp32": torch.float32}
+        self.kv_dtype = dtypes[kv_dtype] if isinstance(kv_dtype, str) else kv_dtype
+        self.cohorts = max(1, cohorts)
+        # One spare position past the longest stream absorbs ragged padding.
+        self.cache_length = max_length + 1
+        self.stats = CollectionStats()
+        self._waves_factory = waves_factory or (lambda cache: DeviceWaves(model, cache, values=record_values))
+        self.reset()
+
+    def reset(self) -> None:
+        """Drop every game in flight, every banked result and the cache."""
+
+        self._layout: tuple | None = None
+        self._slots: list[_Slot] = []
+        self._finished: dict[str, deque[Trajectory]] = {}
+        self._cache = None
+        self._device_waves = None
+        self._scratch = 0
+        self._waves = [_Wave() for _ in range(self.cohorts)]
+        self._width: int | None = None
+
+    def release(self) -> None:
+        """Nothing to free between updates: the pool holds the games in flight."""
+
+    @property
+    def in_flight(self) -> int:
+        return sum(slot.state is not None for slot in self._slots)
+
+    @torch.no_grad()
+    def collect(self, lanes: list[Lane], rng: random.Random, *, version: int = 0) -> list[Trajectory]:
+        started = time.perf_counter()
+        self.stats = CollectionStats()
+        self._configure(lanes)
+        for slot in self._slots:
+            if slot.state is None:
+                self._deal(slot, lanes, rng)
+        pending = [False] * self.cohorts
+        while True:
+            for cohort in range(self.cohorts):
+                if pending[cohort]:
+                    self._receive(cohort)
+                    self._act(cohort, lanes, rng, version)
+                    pending[cohort] = False
+                if not self._satisfied(lanes) and self.in_flight:
+                    pending[cohort] = self._launch(cohort)
+            if not any(pending):
+                break
+        results: list[Trajectory] = []
+        for lane in lanes:
+            bank = self._finished[lane.name]
+            count = len(bank) if lane.quota is None else min(lane.quota, len(bank))
+            results.extend(bank.popleft() for _ in range(count))
+        versions = [record.version for trajectory in results for record in trajectory.decisions]
+        self.stats.games = len(results)
+        self.stats.in_flight = self.in_flight
+        self.stats.policy_lag = float(version - np.mean(versions)) if versions else 0.0
+        self.stats.collect_sec = time.perf_counter() - started
+        return results
+
+    # ------------------------------------------------------------------
+
+    def _configure(self, lanes: list[Lane]) -> None:
+        layout = tuple((lane.name, lane.players, lane.in_flight) for lane in lanes)
+        if layout == self._layout:
+            return
+        self.reset()
+        self._layout = layout
+        row = 0
+        for index, lane in enumerate(lanes):
+            self._finished[lane.name] = deque()
+            for _ in range(lane.in_flight):
+                self._slots.append(_Slot(lane=index, base=row, cohort=len(self._slots) % self.cohorts))
+                row += lane.players
+        self._scratch = row
+        self._cache = self.model.new_cache(row + 1, self.cache_length, self.kv_dtype)
+        self._device_waves = self._waves_factory(self._cache)
+
+    def _satisfied(self, lanes: list[Lane]) -> bool:
+        for index, lane in enumerate(lanes):
+            if lane.quota is None:
+                if any(slot.state is not None for slot in self._slots if slot.lane == index):
+                    return False
+            elif len(self._finished[lane.name]) < lane.quota:
+                return False
+        return True
+
+    def _deal(self, slot: _Slot, lanes: list[Lane], rng: random.Random) -> None:
+        """Fill an empty slot; games that end before any decision finish at once. A lane
+        whose finished games already cover its quota deals nothing (continuous.py:224-255)."""
+
+        lane = lanes[slot.lane]
+        if lane.quota is not None and len(self._finished[lane.name]) >= lane.quota:
+            return
+        while True:
+            game = lane.deal(rng)
+            if game is None:
+                return
+            state = LiveGame(game=game, base=slot.base, lengths=np.zeros(game.num_players, dtype=np.int64),
+                             blocks=[[] for _ in range(game.num_players)])
+            queued = self._record(state, game.prefix_tokens())
+            if game.done():
+                self._finished[lane.name].append(self._finish(state))
+                continue
+            slot.state = state
+            slot.queued = queued
+            self._expect_readout(state, queued)
+            return
+
+    def _record(self, state: LiveGame, blocks: list[np.ndarray], restart: bool = False) -> list[tuple[int, np.ndarray]]:
+        """Record every observer's new tokens; returns those to decode (after any restart)."""
+
+        for seat, block in enumerate(blocks):
+            if len(block):
+                state.blocks[seat].append(block)
+                self._width = block.shape[1]
+        decoded = restart_contexts(state, blocks) if restart else blocks
+        return [(seat, block) for seat, block in enumerate(decoded) if len(block)]
+
+    @staticmethod
+    def _expect_readout(state: LiveGame, queued: list[tuple[int, np.ndarray]]) -> None:
+        state.pending = state.game.decision()
+        seat = state.pending.seat
+        blocks = [block for queued_seat, block in queued if queued_seat == seat]
+        if not blocks:
+            raise AssertionError("The next actor's stream received no readout token.")
+        state.readout = blocks[-1][-1]
+
+    def _finish(self, state: LiveGame) -> Trajectory:
+        width = self._width or 0
+        streams = [np.concatenate(blocks, axis=0) if blocks else np.zeros((0, width), dtype=np.int16)
+                   for blocks in state.blocks]
+        return Trajectory(game=state.game, streams=streams, decisions=state.decisions,
+                          returns=np.asarray(state.game.returns(), dtype=np.float64))
+
+    def _launch(self, cohort: int) -> bool:
+        """Decode the cohort's queued blocks and sample its pending decisions on the device
+        (continuous.py:299-353). Returns whether anything was launched."""
+
+        started = time.perf_counter()
+        entries: list[tuple[int, int, np.ndarray]] = []  # (row, position, block)
+        readouts: list[tuple[int, LiveGame, float]] = []  # (entry, state, uniform)
+        for slot in self._slots:
+            state = slot.state
+            if state is None or slot.cohort != cohort:
+                continue
+            actor = state.pending.seat
+            for seat, block in slot.queued:
+                if seat == actor:
+                    readouts.append((len(entries), state, state.game.rng.random()))
+                entries.append((slot.base + seat, int(state.lengths[seat]), block))
+                state.lengths[seat] += len(block)
+            if int(state.lengths.max()) >= self.cache_length:
+                raise RuntimeError("A stream outgrew the model's maximum sequence length.")
+            slot.queued = []
+        if not entries:
+            return False
+        wave = pack_wave(entries, self._scratch, self.ROW_BUCKET, self.SPAN_BUCKET)
+        self._waves[cohort] = self._device_waves.launch(wave, readouts)
+        rows, run = wave.tokens.shape[:2]
+        self.stats.waves += 1
+        self.stats.forward_rows += rows * run
+        self.stats.padded_rows += rows * run - sum(len(block) for _, _, block in entries)
+        self.stats.peak_rows = max(self.stats.peak_rows, len(entries))
+        self.stats.forward_sec += time.perf_counter() - started
+        return True
+
+    def _receive(self, cohort: int) -> None:
+        started = time.perf_counter()
+        self._device_waves.wait(self._waves[cohort])
+        self.stats.wait_sec += time.perf_counter() - started
+
+    def _act(self, cohort: int, lanes: list[Lane], rng: random.Random, version: int) -> None:
+        """Record the cohort's sampled decisions and step their games; retire and replace
+        finished games (continuous.py:383-408, selfplay.py:532-567)."""
+
+        t0 = time.perf_counter()
+        wave = self._waves[cohort]
+        self._waves[cohort] = _Wave()
+        for readout in wave.readouts:
+            probs = readout.probs.numpy()
+            actions = readout.actions.numpy()
+            values = None if readout.values is None else readout.values.numpy()
+            for row, state in enumerate(readout.states):
+                decision = state.pending
+                count = decision.legal.shape[0]
+                state.decisions.append(DecisionRecord(
+                    seat=decision.seat, head=decision.head,
+                    position=int(state.offsets[decision.seat] + state.lengths[decision.seat]) - 1,
+                    action=int(actions[row]), probs=probs[row, :count].astype(np.float32),
+                    features=decision.features, version=version,
+                    value=None if values is None else values[row].copy()))
+                state.pending = None
+                self.stats.decisions += 1
+        t1 = time.perf_counter()
+        for slot in self._slots:
+            state = slot.state
+            if state is None or slot.cohort != cohort:
+                continue
+            queued = self._record(state, state.game.step(state.decisions[-1].action), restart=True)
+            if state.game.done():
+                self._finished[lanes[slot.lane].name].append(self._finish(state))
+                slot.state = None
+                self._deal(slot, lanes, rng)
+            else:
+                slot.queued = queued
+                self._expect_readout(state, queued)
+        self.stats.sample_sec += t1 - t0
+        self.stats.step_sec += time.perf_counter() - t1
+
+
+@dataclass
+class _Slot:
+    lane: int
+    base: int  # first cache row
+    cohort: int = 0
+    state: LiveGame | None = None
+    queued: list[tuple[int, np.ndarray]] = field(default_factory=list)  # (seat, block) not yet decoded
