@@ -76,6 +76,9 @@ def parse_args(argv=None):
                         help="waves of the rl-v6 T = 2 leg (two tokens appended per row); 0 skips it")
     parser.add_argument("--pointer-steps", type=int, default=20,
                         help="waves of the piquet and rummy-style pointer-head legs; 0 skips them")
+    parser.add_argument("--prefill-steps", type=int, default=10,
+                        help="prefills of the rl-v6 new-game leg (every row's prefix from position 0); 0 skips it")
+    parser.add_argument("--prefill-tokens", type=int, default=16, help="prefix tokens per row in the prefill leg")
     return parser.parse_args(argv)
 
 
@@ -367,6 +370,78 @@ def run_two_token_wave(args, device, rank: int, world_size: int, actor, cache, w
                         "fp16 KV, readout at the second token",
             "value": world_size * games / (ms / 1000.0), "unit": "decisions/s",
             "tokens_per_s": world_size * 2 * rows / (ms / 1000.0), "ms_per_step": ms, "steps": args.t2_steps}
+
+
+def dense_flops(trunk, row_tokens: int) -> int:
+    """FLOPs of every projection of one pass over ``row_tokens`` row-tokens: the first
+    launch's PLE context and QKV GEMMs, then per layer out, up, down and the next layer's QKV."""
+
+    d, f, qkv = trunk.d_model, trunk.d_ff, (trunk.n_heads + 2 * trunk.n_kv_heads) * trunk.head_dim
+    ple_w = trunk.n_layers * trunk.per_layer_dim
+    layer_flops = 2 * (d * d + 2 * d * f + d * qkv)
+    return row_tokens * 2 * (ple_w * d + qkv * d) + row_tokens * (trunk.n_layers - 1) * layer_flops \
+        + row_tokens * (layer_flops - 2 * d * qkv)
+
+
+def run_prefill(args, device, rank: int, world_size: int, actor, cache) -> dict:
+    """New games: every row of the rl-v6 pool encodes a fresh prefix of ``--prefill-tokens``
+    tokens from position 0 (``forward_prefill``, trunk.py:376-389) and each game's first
+    decision is read at its actor's prefix end. The dense layers run over rows x T row-tokens."""
+
+    import torch
+    import torch.distributed as dist
+
+    from card_playing_gym_b200 import _native as nat
+    from card_playing_gym_b200.config import RL_V6
+
+    steps_t = args.prefill_tokens
+    parts = [synthetic_wave(args.games, args.min_len, args.max_len, seed=5000 + 31 * t + 7919 * rank)
+             for t in range(steps_t)]
+    first = parts[0]
+    tokens = torch.from_numpy(np.concatenate([p["tokens"] for p in parts], axis=1)).to(device)
+    dev = {k: torch.from_numpy(first[k]).to(device) for k in ("heads", "legal", "uniforms", "readout_rows")}
+    rows = tokens.shape[0]
+
+    def step():
+        hidden = actor.forward_prefill(tokens, cache, rows=None)
+        return actor.decide(hidden, dev["heads"], dev["legal"], dev["uniforms"], dev["readout_rows"], logits=False,
+                            values=True)
+
+    for _ in range(3):
+        step()
+    if world_size > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    stream = torch.cuda.current_stream(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.prefill_steps):
+        step()
+    end.record(stream)
+    torch.cuda.synchronize(device)
+    ms = start.elapsed_time(end) / args.prefill_steps
+    nat.dense_profiling(True, capacity=args.prefill_steps * (RL_V6.n_layers + 1) + 16)
+    for _ in range(args.prefill_steps):
+        step()
+    torch.cuda.synchronize(device)
+    dense_ms = nat.dense_timings()
+    nat.dense_profiling(False)
+    if world_size > 1:
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    trunk = RL_V6.trunk()
+    flops = dense_flops(trunk, rows * steps_t)
+    dense_pass_ms = statistics.fmean(dense_ms) * (trunk.n_layers + 1) if dense_ms else float("nan")
+    tflops = flops / (dense_pass_ms / 1000.0) / 1e12
+    tpeak, tpeak_kind = measured_peak("bf16_tflops_sustained")
+    return {"workload": (f"rl-v6 prefill: {rows} rows x {steps_t} prefix tokens from position 0, fp16 KV, "
+                         "field lookup + trunk + heads at each game's actor"),
+            "tokens_per_s": world_size * rows * steps_t / (ms / 1000.0), "ms_per_step": ms, "steps": args.prefill_steps,
+            "dense_layers": {"achieved": tflops, "unit": "TFLOP/s", "peak": tpeak, "frac": tflops / tpeak,
+                             "peak_source": f"{tpeak_kind} (MEASURED_PEAKS.json bf16_tflops_sustained)",
+                             "mean_launch_ms": statistics.fmean(dense_ms) if dense_ms else None,
+                             "flops_per_pass": flops}}
 
 
 def run_pointer_wave(args, device, rank: int, world_size: int, kind: str) -> dict:
@@ -786,6 +861,8 @@ def run_b200(args) -> int:
     if args.pointer_steps > 0:
         pointer_lines["piquet_pointer"] = run_pointer_wave(args, device, rank, world_size, "piquet")
         pointer_lines["rummy_style"] = run_pointer_wave(args, device, rank, world_size, "rummy")
+    if args.prefill_steps > 0:  # last: it overwrites the first positions of every cache row
+        pointer_lines["rlv6_prefill"] = run_prefill(args, device, rank, world_size, actor, cache)
 
     if rank == 0:
         head_dim = RL_V6.trunk().head_dim
@@ -824,11 +901,7 @@ def run_b200(args) -> int:
         # Dense layers (tcgen05): the projections' FLOPs per wave over the summed dense-launch
         # time per wave, against the measured sustained bf16 GEMM rate (timed inside a long step).
         trunk = RL_V6.trunk()
-        d, f, qkv = trunk.d_model, trunk.d_ff, (trunk.n_heads + 2 * trunk.n_kv_heads) * trunk.head_dim
-        ple_w = trunk.n_layers * trunk.per_layer_dim
-        layer_flops = 2 * (d * d + 2 * d * f + d * qkv)
-        wave_flops = rows * 2 * (ple_w * d + qkv * d) + rows * (trunk.n_layers - 1) * layer_flops \
-            + rows * (layer_flops - 2 * d * qkv)
+        wave_flops = dense_flops(trunk, rows)
         launches_per_wave = trunk.n_layers + 1
         dense_wave_ms = statistics.fmean(dense_ms) * launches_per_wave if dense_ms else float("nan")
         tflops = wave_flops / (dense_wave_ms / 1000.0) / 1e12

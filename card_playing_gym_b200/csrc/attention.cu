@@ -6,8 +6,11 @@
 // a KV head is g * T + t (trunk.py:243-254).
 //
 // Two kernels:
-//  * attn_tc: fp16/bf16 caches, head_dim in {16, 24, 32, 40, 48, 64}, G*T <= 16. One
-//    warp per (row, KV head) unit, persistent over units. Each warp streams its units'
+//  * attn_tc: fp16/bf16 caches, head_dim in {16, 24, 32, 40, 48, 64}, G <= 16. One
+//    warp per unit, persistent over units. A unit is a (row, KV head) pair and a block of
+//    its steps: all T of them when G*T <= 16 (the decode case: one m16 tile of queries),
+//    else floor(16 / G) steps per block (a prefill of T = 16 at G = 5: six blocks of three
+//    steps, the same keys read from L2 by each). Each warp streams its units'
 //    keys in chunks of 32 through a four-stage shared-memory ring filled with 16-byte
 //    cp.async copies (zero-filled past the row's length, L2 evict-first; a unit's query
 //    rows travel with its first chunk), computes Q K^T
@@ -224,12 +227,15 @@ struct TcShape {
   static constexpr int kWarpBytes = kStages * kStageElems * static_cast<int>(sizeof(KV));
 };
 
-// Rows with no visible key get a zero output.
-__device__ void zero_unit(const AttnParams& p, int64_t b, int kvh, int M, int lane) {
+// Steps per unit: every step when the G*T query rows fit one m16 tile, else the most that do.
+__host__ __device__ inline int step_block(int group, int steps) { return group * steps <= 16 ? steps : 16 / group; }
+
+// Rows with no visible key get a zero output: the unit's steps t0 .. t0 + tb - 1.
+__device__ void zero_unit(const AttnParams& p, int64_t b, int kvh, int t0, int tb, int lane) {
   const int D = p.head_dim;
-  for (int i = lane; i < M * D; i += 32) {
+  for (int i = lane; i < p.group * tb * D; i += 32) {
     const int m = i / D, d = i % D;
-    const int h = kvh * p.group + m / p.steps, t = m % p.steps;
+    const int h = kvh * p.group + m / tb, t = t0 + m % tb;
     const int64_t off = p.out_blocked ? blocked_offset(b * p.steps + t, h * D + d, p.blocked_width)
                                       : b * p.o_sb + h * p.o_sh + t * p.o_st + d;
     store_from_float(p.out, off, p.out_dtype, 0.f);
@@ -242,7 +248,8 @@ struct TcUnit {
   int b;     // batch index
   int kvh;   // KV head
   int keys;  // keys visible to the unit's last query (> 0)
-  int len;   // min(lengths[b], span): keys visible to its first step
+  int len;   // min(lengths[b] + t0, span): keys visible to its first step
+  int t0;    // its first step
 };
 
 constexpr int kRing = 8;  // units claimed ahead by the issue cursor, per warp
@@ -266,8 +273,10 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
   pdl_wait();  // q, K and V come from the kernel before
   pdl_trigger();
 
-  const int units = static_cast<int>(p.batch * p.kv_heads);  // < 2^31: checked by the host
-  const int M = p.group * p.steps;
+  const int sblk = step_block(p.group, p.steps);
+  const int nblk = (p.steps + sblk - 1) / sblk;
+  const int units = static_cast<int>(p.batch * p.kv_heads * nblk);  // < 2^31: checked by the host
+  const int M = p.group * sblk;  // query rows of a unit's tile (a short last block uses fewer)
   const float scale_log2 = p.scale * 1.4426950408889634f;
   const KV* kc = static_cast<const KV*>(p.k);
   const KV* vc = static_cast<const KV*>(p.v);
@@ -292,18 +301,23 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
         static_next += stride;
       }
       if (x >= units) return false;
-      const int b = x / p.kv_heads, kvh = x - b * p.kv_heads;
-      const int64_t len = p.lengths[b];
-      const int64_t last = len + p.steps - 1;
+      // Consecutive units are the step blocks of one (row, KV head): their keys stay in L2.
+      const int per_row = p.kv_heads * nblk;
+      const int b = x / per_row, rest = x - b * per_row;
+      const int kvh = rest / nblk, t0 = (rest - kvh * nblk) * sblk;
+      const int tb = min(sblk, p.steps - t0);
+      const int64_t len = p.lengths[b] + t0;
+      const int64_t last = len + tb - 1;
       const int keys = static_cast<int>(last < p.span ? last : p.span);
       if (keys <= 0) {
-        zero_unit(p, b, kvh, M, lane);
+        zero_unit(p, b, kvh, t0, tb, lane);
         continue;
       }
       u.b = b;
       u.kvh = kvh;
       u.keys = keys;
       u.len = static_cast<int>(len < p.span ? len : p.span);
+      u.t0 = t0;
       return true;
     }
   };
@@ -313,26 +327,28 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
   constexpr int kQPieces = Shape::kQRows * Shape::kPieces;
   constexpr int kQIters = (kQPieces + 31) / 32;
   int q_off[kQIters];
+  int q_t[kQIters];  // the piece's step within the unit's block
   bool q_ok[kQIters];
 #pragma unroll
   for (int it = 0; it < kQIters; ++it) {
     const int i = lane + 32 * it;
     const int m = i / Shape::kPieces, piece = i - m * Shape::kPieces;
     q_ok[it] = i < kQPieces && m < M;
-    q_off[it] = q_ok[it] ? static_cast<int>((m / p.steps) * p.q_sh + (m % p.steps) * p.q_st) + piece * 8 : 0;
+    q_t[it] = q_ok[it] ? m % sblk : 0;
+    q_off[it] = q_ok[it] ? static_cast<int>((m / sblk) * p.q_sh + (m % sblk) * p.q_st) + piece * 8 : 0;
   }
   int row_h[2], row_t[2], row_tlim[2];  // rows gid and gid + 8: head within the group, step, step for the limit
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
     const int m = gid + 8 * r;
-    row_h[r] = m < M ? m / p.steps : 0;
-    row_t[r] = m < M ? m % p.steps : 0;
-    row_tlim[r] = m < M ? row_t[r] : p.steps - 1;  // padding rows attend to every visible key: finite, never stored
+    row_h[r] = m < M ? m / sblk : 0;
+    row_t[r] = m < M ? m % sblk : 0;
+    row_tlim[r] = m < M ? row_t[r] : sblk - 1;  // padding rows attend to every visible key: finite, never stored
   }
 
   // Issue cursor.
   bool issue_live = true;
-  TcUnit iu{0, 0, 0, 0};
+  TcUnit iu{0, 0, 0, 0, 0};
   int issue_chunk_no = 0;
   int64_t issue_kv = 0;  // element offset of the unit's (row, KV head) block in the pool
   auto issue_next_unit = [&]() {
@@ -342,7 +358,8 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
       const int64_t row = p.rows ? p.rows[iu.b] : iu.b;
       issue_kv = row * p.kv_row + iu.kvh * p.kv_head;
     }
-    if (lane == 0) ring[wib][head % kRing] = issue_live ? make_int4(iu.b, iu.kvh, iu.keys, iu.len)
+    // KV head and first step share one slot: kv_heads < 2^16 and steps < 2^15 (checked by the host).
+    if (lane == 0) ring[wib][head % kRing] = issue_live ? make_int4(iu.b, iu.kvh | (iu.t0 << 16), iu.keys, iu.len)
                                                         : make_int4(0, 0, 0, -1);
     ++head;
   };
@@ -378,10 +395,14 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
       }
       if (issue_chunk_no == 0) {
         uint4* qdst = reinterpret_cast<uint4*>(sbase + 2 * Shape::kChunkElems) + lane;
-        const KV* qunit = qg + iu.b * p.q_sb + static_cast<int64_t>(iu.kvh) * p.group * p.q_sh;
+        const KV* qunit = qg + iu.b * p.q_sb + static_cast<int64_t>(iu.kvh) * p.group * p.q_sh +
+                          static_cast<int64_t>(iu.t0) * p.q_st;
 #pragma unroll
-        for (int it = 0; it < kQIters; ++it)
-          if (lane + 32 * it < kQPieces) cp_async16(qdst + 32 * it, qunit + q_off[it], q_ok[it], policy);
+        for (int it = 0; it < kQIters; ++it) {
+          // Rows past the last step (a short last block) are zero-filled like the tile's padding.
+          const bool ok = q_ok[it] && iu.t0 + q_t[it] < p.steps;
+          if (lane + 32 * it < kQPieces) cp_async16(qdst + 32 * it, qunit + (ok ? q_off[it] : 0), ok, policy);
+        }
       }
     }
     cp_async_commit();  // one group per chunk slot, empty or not: keeps the group count in step
@@ -407,7 +428,8 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
     const int4 r = ring[wib][tail % kRing];
     ++tail;
     u.b = r.x;
-    u.kvh = r.y;
+    u.kvh = r.y & 0xffff;
+    u.t0 = r.y >> 16;
     u.keys = r.z;
     u.len = r.w;
     return r.w >= 0;
@@ -601,9 +623,9 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_tc_kernel(AttnParams p) {
 #pragma unroll
       for (int r = 0; r < kRows; ++r) {
         const int m = gid + 8 * r;
-        if (m < M) {
+        if (m < M && cu.t0 + row_t[r] < p.steps) {
           const float inv = 1.f / lrow[r];
-          const int h = cu.kvh * p.group + row_h[r], t = row_t[r];
+          const int h = cu.kvh * p.group + row_h[r], t = cu.t0 + row_t[r];
 #pragma unroll
           for (int j = 0; j < Shape::kDTiles; ++j) {
             const int d = j * 8 + 2 * tid4;
@@ -645,7 +667,8 @@ int launch_tc(const AttnParams& p, cudaStream_t stream) {
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occupancy, kernel, kTcWarps * 32, smem);
     if (occupancy < 1) occupancy = 1;
   }
-  const int64_t units = p.batch * p.kv_heads;
+  const int sblk = step_block(p.group, p.steps);
+  const int64_t units = p.batch * p.kv_heads * ((p.steps + sblk - 1) / sblk);
   int64_t blocks = static_cast<int64_t>(sm_count()) * occupancy;
   const int64_t needed = (units + kTcWarps - 1) / kTcWarps;
   if (blocks > needed) blocks = needed;
@@ -656,7 +679,7 @@ int launch_tc(const AttnParams& p, cudaStream_t stream) {
 
 template <typename KV, int D>
 int dispatch_layout(const AttnParams& p, cudaStream_t stream) {
-  const bool half = p.group * p.steps <= 8;
+  const bool half = p.group * step_block(p.group, p.steps) <= 8;
   if (p.out_blocked) return half ? launch_tc<KV, D, true, true>(p, stream) : launch_tc<KV, D, false, true>(p, stream);
   return half ? launch_tc<KV, D, true, false>(p, stream) : launch_tc<KV, D, false, false>(p, stream);
 }
@@ -676,7 +699,7 @@ int dispatch_tc(const AttnParams& p, cudaStream_t stream) {
 
 bool tc_eligible(const AttnParams& p) {
   if (p.kv_dtype == CG_F32) return false;
-  if (p.group * p.steps > 16) return false;
+  if (p.group > 16 || p.kv_heads >= (1 << 16) || p.steps >= (1 << 15)) return false;
   const int d = p.head_dim;
   if (!(d == 16 || d == 24 || d == 32 || d == 40 || d == 48 || d == 64)) return false;
   // q (and the non-blocked output) in the cache dtype; q rows are copied in 16-byte pieces,
@@ -684,7 +707,8 @@ bool tc_eligible(const AttnParams& p) {
   if (p.q_dtype != p.kv_dtype) return false;
   if (!p.out_blocked && p.out_dtype != p.kv_dtype) return false;
   if ((p.q_sb | p.q_sh | p.q_st) & 7) return false;
-  if (p.batch * p.kv_heads >= (1LL << 31)) return false;
+  const int sblk = step_block(p.group, p.steps);
+  if (p.batch * p.kv_heads * ((p.steps + sblk - 1) / sblk) >= (1LL << 31)) return false;
   if (!p.out_blocked && ((p.o_sb | p.o_sh | p.o_st) & 1)) return false;
   // 16-byte copies: contiguous key rows, aligned row/head strides and bases.
   if (p.kv_pos != d) return false;

@@ -27,7 +27,7 @@ def scaled_error(actual: np.ndarray, expected: np.ndarray) -> float:
 
 @pytest.mark.parametrize("kv", ["fp32", "fp16", "bf16"])
 @pytest.mark.parametrize("heads,kv_heads,dim", [(10, 2, 24), (8, 2, 32), (5, 1, 40), (8, 4, 64)])
-@pytest.mark.parametrize("steps", [1, 3])
+@pytest.mark.parametrize("steps", [1, 3, 7, 16])  # 7, 16: G*T > 16 splits a row's steps into blocks
 def test_decode_attention_matches_the_oracle(kv, heads, kv_heads, dim, steps):
     rng = np.random.default_rng(heads * 100 + dim + steps)
     batch, capacity, max_len = 37, 48, 300
