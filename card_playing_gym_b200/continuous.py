@@ -25,6 +25,7 @@ so each game sees the same sequence of uniforms.
 
 from __future__ import annotations
 
+import gc
 import random
 import time
 from collections import deque
@@ -131,16 +132,16 @@ class LiveGame:
 
     game: object
     base: int  # first cache row
-    lengths: np.ndarray  # per observer cached tokens
+    lengths: list[int]  # per observer cached tokens (Python ints: the collector's inner loops index them)
     blocks: list[list[np.ndarray]]  # per observer recorded blocks
     decisions: list[DecisionRecord] = field(default_factory=list)
     pending: Decision | None = None
     readout: np.ndarray | None = None  # the pending actor's last token
-    offsets: np.ndarray | None = None  # per observer, stream tokens before its current context
+    offsets: list[int] | None = None  # per observer, stream tokens before its current context
 
     def __post_init__(self) -> None:
         if self.offsets is None:
-            self.offsets = np.zeros_like(self.lengths)
+            self.offsets = [0] * len(self.lengths)
 
 
 def restart_contexts(state: LiveGame, blocks: list[np.ndarray]) -> list[np.ndarray]:
@@ -169,6 +170,7 @@ class PackedWave:
     cache_rows: np.ndarray  # int64 [rows]
     span: int
     count: int  # real entries; the rest write the scratch row
+    real_tokens: int = 0  # tokens of the real entries (the rest of rows x run is padding)
 
 
 def pack_wave(entries: list[tuple[int, int, np.ndarray]], scratch: int, row_bucket: int = ROW_BUCKET,
@@ -181,26 +183,36 @@ def pack_wave(entries: list[tuple[int, int, np.ndarray]], scratch: int, row_buck
     concatenated blocks replaces the reference's per-entry copy loop.
     """
 
-    count = len(entries)
-    lengths = np.fromiter((len(block) for _, _, block in entries), dtype=np.int64, count=count)
+    return pack_columns([row for row, _, _ in entries], [position for _, position, _ in entries],
+                        [block for _, _, block in entries], scratch, row_bucket, span_bucket)
+
+
+def pack_columns(cache_rows: list[int], positions: list[int], blocks: list[np.ndarray], scratch: int,
+                 row_bucket: int = ROW_BUCKET, span_bucket: int = SPAN_BUCKET) -> PackedWave:
+    """``pack_wave`` over the entries' three columns, as the collector gathers them."""
+
+    count = len(blocks)
+    lengths = np.fromiter(map(len, blocks), dtype=np.int64, count=count)
     if count == 0 or lengths.min() < 1:
         raise ValueError("every entry needs at least one token")
     run = int(lengths.max())
     rows = round_up(count, row_bucket)
-    width = entries[0][2].shape[1]
-    flat = np.concatenate([block for _, _, block in entries], axis=0).astype(np.int64, copy=False)
-    starts = np.cumsum(lengths) - lengths
-    gather = starts[:, None] + np.minimum(np.arange(run)[None, :], lengths[:, None] - 1)
+    width = blocks[0].shape[1]
+    flat = np.concatenate(blocks, axis=0)
     tokens = np.zeros((rows, run, width), dtype=np.int64)
-    tokens[:count] = flat[gather]
-    cache_rows = np.full(rows, scratch, dtype=np.int64)
-    cache_rows[:count] = np.fromiter((row for row, _, _ in entries), dtype=np.int64, count=count)
-    positions = np.zeros(rows, dtype=np.int64)
-    positions[:count] = np.fromiter((position for _, position, _ in entries), dtype=np.int64, count=count)
+    if run == 1:
+        tokens[:count, 0] = flat
+    else:
+        starts = np.cumsum(lengths) - lengths
+        tokens[:count] = flat[starts[:, None] + np.minimum(np.arange(run)[None, :], lengths[:, None] - 1)]
+    packed_rows = np.full(rows, scratch, dtype=np.int64)
+    packed_rows[:count] = cache_rows
+    packed_positions = np.zeros(rows, dtype=np.int64)
+    packed_positions[:count] = positions
     offsets = np.zeros(rows, dtype=np.int64)
     offsets[:count] = lengths - 1
-    span = round_up(int(positions.max()) + run, span_bucket)
-    return PackedWave(tokens, positions, offsets, cache_rows, span, count)
+    span = round_up(int(packed_positions.max()) + run, span_bucket)
+    return PackedWave(tokens, packed_positions, offsets, packed_rows, span, count, int(lengths.sum()))
 
 
 @dataclass
@@ -249,12 +261,16 @@ class DeviceWaves:
         for head, group in groups.items():
             head_columns = columns[head]
             width = head_columns.stop - head_columns.start
-            legal = np.zeros((len(group), width), dtype=np.uint8)
-            for row, (_, state, _) in enumerate(group):
-                mask = state.pending.legal
-                if mask.shape[0] > width:
-                    raise ValueError(f"head {head!r} has {width} actions, a decision offers {mask.shape[0]}")
-                legal[row, : mask.shape[0]] = mask
+            masks = [state.pending.legal for _, state, _ in group]
+            sizes = set(map(len, masks))
+            if max(sizes) > width:
+                raise ValueError(f"head {head!r} has {width} actions, a decision offers {max(sizes)}")
+            if sizes == {width}:
+                legal = np.stack(masks).astype(np.uint8, copy=False)
+            else:
+                legal = np.zeros((len(group), width), dtype=np.uint8)
+                for row, mask in enumerate(masks):
+                    legal[row, : mask.shape[0]] = mask
             index = _pinned(np.fromiter((entry for entry, _, _ in group), dtype=np.int64, count=len(group)),
                             self.device)
             uniforms = _pinned(np.fromiter((u for _, _, u in group), dtype=np.float64, count=len(group)),
@@ -324,20 +340,29 @@ class ContinuousCollector:
         started = time.perf_counter()
         self.stats = CollectionStats()
         self._configure(lanes)
-        for slot in self._slots:
-            if slot.state is None:
-                self._deal(slot, lanes, rng)
-        pending = [False] * self.cohorts
-        while True:
-            for cohort in range(self.cohorts):
-                if pending[cohort]:
-                    self._receive(cohort)
-                    self._act(cohort, lanes, rng, version)
-                    pending[cohort] = False
-                if not self._satisfied(lanes) and self.in_flight:
-                    pending[cohort] = self._launch(cohort)
-            if not any(pending):
-                break
+        # Every wave allocates a few objects per decision (records, entries, blocks) and almost
+        # none form cycles; at the default young-generation threshold the cyclic collector runs
+        # every few hundred decisions and rescans the games in flight, about a third of the
+        # collector's host time. It runs less often for the collection's duration.
+        thresholds = gc.get_threshold()
+        gc.set_threshold(max(thresholds[0], 100_000), *thresholds[1:])
+        try:
+            for slot in self._slots:
+                if slot.state is None:
+                    self._deal(slot, lanes, rng)
+            pending = [False] * self.cohorts
+            while True:
+                for cohort in range(self.cohorts):
+                    if pending[cohort]:
+                        self._receive(cohort)
+                        self._act(cohort, lanes, rng, version)
+                        pending[cohort] = False
+                    if not self._satisfied(lanes) and self.in_flight:
+                        pending[cohort] = self._launch(cohort)
+                if not any(pending):
+                    break
+        finally:
+            gc.set_threshold(*thresholds)
         results: list[Trajectory] = []
         for lane in lanes:
             bank = self._finished[lane.name]
@@ -388,7 +413,7 @@ class ContinuousCollector:
             game = lane.deal(rng)
             if game is None:
                 return
-            state = LiveGame(game=game, base=slot.base, lengths=np.zeros(game.num_players, dtype=np.int64),
+            state = LiveGame(game=game, base=slot.base, lengths=[0] * game.num_players,
                              blocks=[[] for _ in range(game.num_players)])
             queued = self._record(state, game.prefix_tokens())
             if game.done():
@@ -402,12 +427,18 @@ class ContinuousCollector:
     def _record(self, state: LiveGame, blocks: list[np.ndarray], restart: bool = False) -> list[tuple[int, np.ndarray]]:
         """Record every observer's new tokens; returns those to decode (after any restart)."""
 
+        queued = []
         for seat, block in enumerate(blocks):
             if len(block):
                 state.blocks[seat].append(block)
-                self._width = block.shape[1]
-        decoded = restart_contexts(state, blocks) if restart else blocks
-        return [(seat, block) for seat, block in enumerate(decoded) if len(block)]
+                queued.append((seat, block))
+        if queued:
+            self._width = queued[-1][1].shape[1]
+        if restart:
+            decoded = restart_contexts(state, blocks)
+            if decoded is not blocks:
+                return [(seat, block) for seat, block in enumerate(decoded) if len(block)]
+        return queued
 
     @staticmethod
     def _expect_readout(state: LiveGame, queued: list[tuple[int, np.ndarray]]) -> None:
@@ -430,30 +461,38 @@ class ContinuousCollector:
         (continuous.py:299-353). Returns whether anything was launched."""
 
         started = time.perf_counter()
-        entries: list[tuple[int, int, np.ndarray]] = []  # (row, position, block)
+        cache_rows: list[int] = []  # the entries, as three columns: cache row, position, block
+        positions: list[int] = []
+        blocks: list[np.ndarray] = []
         readouts: list[tuple[int, LiveGame, float]] = []  # (entry, state, uniform)
+        limit = self.cache_length
         for slot in self._slots:
             state = slot.state
             if state is None or slot.cohort != cohort:
                 continue
             actor = state.pending.seat
+            lengths = state.lengths
             for seat, block in slot.queued:
                 if seat == actor:
-                    readouts.append((len(entries), state, state.game.rng.random()))
-                entries.append((slot.base + seat, int(state.lengths[seat]), block))
-                state.lengths[seat] += len(block)
-            if int(state.lengths.max()) >= self.cache_length:
-                raise RuntimeError("A stream outgrew the model's maximum sequence length.")
+                    readouts.append((len(blocks), state, state.game.rng.random()))
+                length = lengths[seat]
+                cache_rows.append(slot.base + seat)
+                positions.append(length)
+                blocks.append(block)
+                length += len(block)
+                lengths[seat] = length
+                if length >= limit:
+                    raise RuntimeError("A stream outgrew the model's maximum sequence length.")
             slot.queued = []
-        if not entries:
+        if not blocks:
             return False
-        wave = pack_wave(entries, self._scratch, self.ROW_BUCKET, self.SPAN_BUCKET)
+        wave = pack_columns(cache_rows, positions, blocks, self._scratch, self.ROW_BUCKET, self.SPAN_BUCKET)
         self._waves[cohort] = self._device_waves.launch(wave, readouts)
         rows, run = wave.tokens.shape[:2]
         self.stats.waves += 1
         self.stats.forward_rows += rows * run
-        self.stats.padded_rows += rows * run - sum(len(block) for _, _, block in entries)
-        self.stats.peak_rows = max(self.stats.peak_rows, len(entries))
+        self.stats.padded_rows += rows * run - wave.real_tokens
+        self.stats.peak_rows = max(self.stats.peak_rows, wave.count)
         self.stats.forward_sec += time.perf_counter() - started
         return True
 
@@ -478,7 +517,7 @@ class ContinuousCollector:
                 count = decision.legal.shape[0]
                 state.decisions.append(DecisionRecord(
                     seat=decision.seat, head=decision.head,
-                    position=int(state.offsets[decision.seat] + state.lengths[decision.seat]) - 1,
+                    position=state.offsets[decision.seat] + state.lengths[decision.seat] - 1,
                     action=int(actions[row]), probs=probs[row, :count].astype(np.float32),
                     features=decision.features, version=version,
                     value=None if values is None else values[row].copy()))

@@ -194,11 +194,11 @@ def test_restart_contexts_drops_cached_lengths():
         def context_starts(self):
             return [None, 1]
 
-    state = cont.LiveGame(game=Game(), base=0, lengths=np.array([5, 7]), blocks=[[], []])
+    state = cont.LiveGame(game=Game(), base=0, lengths=[5, 7], blocks=[[], []])
     blocks = [np.zeros((2, 3)), np.arange(9).reshape(3, 3)]
     decoded = cont.restart_contexts(state, blocks)
     assert decoded[0] is blocks[0] and np.array_equal(decoded[1], blocks[1][1:])
-    assert state.lengths.tolist() == [5, 0] and state.offsets.tolist() == [0, 8]
+    assert state.lengths == [5, 0] and state.offsets == [0, 8]
 
 
 @pytest.mark.parametrize("cohorts", (1, 2))
