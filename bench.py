@@ -862,7 +862,8 @@ def run_b200(args) -> int:
         pointer_lines["piquet_pointer"] = run_pointer_wave(args, device, rank, world_size, "piquet")
         pointer_lines["rummy_style"] = run_pointer_wave(args, device, rank, world_size, "rummy")
     if args.prefill_steps > 0:  # last: it overwrites the first positions of every cache row
-        pointer_lines["rlv6_prefill"] = run_prefill(args, device, rank, world_size, actor, cache)
+        with torch.cuda.nvtx.range("rlv6_prefill"):  # lets a profiler select this leg's launches
+            pointer_lines["rlv6_prefill"] = run_prefill(args, device, rank, world_size, actor, cache)
 
     if rank == 0:
         head_dim = RL_V6.trunk().head_dim
