@@ -63,9 +63,10 @@ int cg_dense_timings(float* ms_out, int max_count);
  *   q [B, H, T, D] contiguous, k/v [R, KVH, L, D] (stride over D == 1), rows [B],
  *   lengths [B] (key length including the row's first new token), span, scale;
  *   query t of row b sees keys < min(lengths[b] + t, span).
- * Beyond the reference: any D that is a multiple of 8 up to 128, H/KVH groups
- * with G*T up to 64, spans up to L, and fp32 / fp16 / bf16 caches. q and out may
- * use their own dtypes; out has q's [B, H, T, D] layout.
+ * Beyond the reference: any D that is a multiple of 8 up to 128, any H/KVH group
+ * and step count T (fp16/bf16 caches with G <= 16 run on the tensor cores, a row's
+ * steps in blocks of floor(16 / G) when G*T > 16), spans up to L, and fp32 / fp16 /
+ * bf16 caches. q and out may use their own dtypes; out has q's [B, H, T, D] layout.
  * ------------------------------------------------------------------------------- */
 int cg_decode_attention(const void* q, int q_dtype, const void* k_cache, const void* v_cache, int kv_dtype,
                         int64_t kv_stride_row, int64_t kv_stride_head, int64_t kv_stride_pos,
