@@ -851,8 +851,49 @@ def run_b200(args) -> int:
         e2e_step()
     end.record(stream)
     barrier()
+    e2e_eager_ms = max_over_ranks(start.elapsed_time(end))
+
+    # The same step captured once as a CUDA graph, copies included: the host writes the next
+    # wave's inputs into the pinned buffers and replays (as DecodeGraphs does for the
+    # collector), so no launch waits on the host after each wave's synchronize.
+    static_in = {k: torch.empty(v.shape, dtype=v.dtype, device=device) for k, v in host.items()}
+    graph_workspace = torch.empty(actor.step_workspace_bytes(rows, 1), dtype=torch.uint8, device=device)
+
+    def e2e_body():
+        for k, v in host.items():
+            static_in[k].copy_(v, non_blocking=True)
+        hidden = actor.forward_ragged(static_in["tokens"], static_in["positions"], cache, static_in["offsets"],
+                                      span=span, workspace=graph_workspace)
+        _, probs, actions, _ = actor.decide(hidden, static_in["heads"], static_in["legal"], static_in["uniforms"],
+                                            static_in["readout_rows"], logits=False, values=False)
+        out_actions.copy_(actions, non_blocking=True)
+        out_probs.copy_(probs, non_blocking=True)
+
+    side = torch.cuda.Stream(device)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        e2e_body()
+    stream.wait_stream(side)
+    e2e_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(e2e_graph):
+        e2e_body()
+
+    def e2e_graph_step():
+        e2e_graph.replay()
+        stream.synchronize()
+
+    for _ in range(max(2, args.warmup // 2)):
+        e2e_graph_step()
+    barrier()
+    start.record(stream)
+    for _ in range(args.steps):
+        e2e_graph_step()
+    end.record(stream)
+    barrier()
     e2e_ms = max_over_ranks(start.elapsed_time(end))
+    del e2e_graph
     e2e_value = world_size * games * args.steps / (e2e_ms / 1000.0)
+    e2e_eager_value = world_size * games * args.steps / (e2e_eager_ms / 1000.0)
     ppo_line = run_ppo(args, device, rank, world_size) if args.ppo_decisions > 0 else None
     piquet_line = run_piquet_scale(args, device, rank, world_size) if args.piquet_steps > 0 else None
     pointer_lines = {}
@@ -886,7 +927,9 @@ def run_b200(args) -> int:
                 "decisions_per_step_per_gpu": games, "l2": "inputs larger than L2 (KV read ~6.9 GB per wave per GPU)",
                 "parallelism": f"independent self-play games on each of {world_size} GPU(s), no collective",
             },
-            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "launch": "one CUDA graph replay per step (pinned inputs in, wave, actions + probabilities out)",
+                    "eager_value": e2e_eager_value},
             "roofline": {
                 "kernel": "decode attention (attn_tc_kernel)", "bound": "hbm", "achieved": achieved, "peak": peak,
                 "unit": "GB/s", "frac": achieved / peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
