@@ -5,7 +5,8 @@ per row, token width, attention span) the whole wave — the field lookup and ra
 decode into the KV cache, every policy head's logits at each row's readout and, with
 ``values``, the per-seat values — is captured once and replayed with one launch. The output
 is one fp32 [rows, columns] device tensor (``columns`` names each head's slice), valid until
-the next ``run``.
+the next ``run``. A model with ``pop_context`` (piquet's card grid) hands each head the
+context of its row's readout token, as graphs.py:88-95 does.
 
 The step's scratch memory belongs to this object: captured graphs hold its address, so when
 a larger shape needs more, the buffer is replaced and every earlier graph is dropped (and
@@ -49,7 +50,12 @@ class DecodeGraphs:
         positions, offsets, cache_rows = inputs[cells:].view(3, rows)
         hidden = self.model.forward_ragged(tokens, positions, self.cache, offsets, span=span, rows=cache_rows,
                                            workspace=self._workspace)
-        outputs = [self.model.policy_logits(hidden, head) for head in self.heads]
+        # Pointer heads (piquet's card scorers) read the readout token's grid cards.
+        pop = getattr(self.model, "pop_context", None)
+        context = pop() if pop is not None else None
+        if context is not None:
+            context = context[torch.arange(rows, device=inputs.device), offsets]
+        outputs = [self.model.policy_logits(hidden, head, None, None, context) for head in self.heads]
         if self.values:
             outputs.append(self.model.player_values(hidden))
         if not self.columns:

@@ -14,13 +14,20 @@ autocast form) and their summary projection (a plain GEMM, left to torch).
 ``CardScorer`` mirrors cardgym/games/piquet/model.py:348-363: one logit per card from the
 readout state and the card's grid features (``cg_card_scorer``), as PiquetActor.policy_logits
 (399-411) calls it for the exchange and play heads.
+
+``PiquetActor`` puts them together as the reference's rollout model (model.py:365-411).
 """
 
 from __future__ import annotations
 
+from dataclasses import dataclass
+
 import torch
 
 from . import _native as nat
+from .config import TrunkConfig
+from .kv_cache import KVCache
+from .trunk import B200Trunk
 
 NUM_FIELDS = 32
 CARD_START = NUM_FIELDS
@@ -144,13 +151,14 @@ class CardScorer:
 
 def forward_ragged(trunk, lookup: PiquetFieldLookup, tokens: torch.Tensor, positions: torch.Tensor, cache,
                    readout_offsets: torch.Tensor, span: int | None = None, rows: torch.Tensor | None = None,
-                   summary: torch.Tensor | None = None) -> torch.Tensor:
+                   summary: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
     """``SequenceModel.forward_ragged`` (cardgym/nn/model.py:76-89) with the piquet field sums:
     tokens [B, T, 64] -> (field sums + ``summary``, the card-grid summary [B, T, d] if given) ->
     Trunk.condition -> the ragged trunk decode -> final-normed hidden [B, d] at each readout.
 
     With a bf16 trunk the lookup writes straight into the first tensor-core layer's inputs
     (``cg_bags_forward_ragged``); an fp32 trunk runs lookup, condition and decode as three calls.
+    ``workspace`` as in ``B200Trunk.forward_ragged``.
     """
 
     batch, steps, _ = tokens.shape
@@ -162,15 +170,15 @@ def forward_ragged(trunk, lookup: PiquetFieldLookup, tokens: torch.Tensor, posit
         if summary is not None:
             fields = fields + summary
         x, ple, values = trunk.condition(fields, ple, values)
-        return trunk.forward_ragged(x, ple, values, cache, positions, readout_offsets, span=span, rows=rows)
+        return trunk.forward_ragged(x, ple, values, cache, positions, readout_offsets, span=span, rows=rows,
+                                    workspace=workspace)
     flat = tokens.reshape(-1, tokens.shape[-1])
     if flat.dtype not in nat.INDEX_CODES:
         flat = flat.long()
     flat = flat.contiguous()
     table = lookup.table(torch.float32)
     extra = None if summary is None else summary.reshape(-1, summary.shape[-1]).float().contiguous()
-    need = nat.query("cg_trunk_step_workspace_bytes", trunk.dims, batch, steps, nat.PRECISIONS[trunk.precision])
-    workspace = nat.Workspace.get(trunk.device, need)
+    workspace = trunk.workspace(batch, steps, workspace)
     hidden = torch.empty((batch, trunk.config.d_model), device=trunk.device)
     offsets = (nat._i64 * NUM_FIELDS)(*lookup.offsets)
     nat.call("cg_bags_forward_ragged", trunk.dims, nat.ptr(trunk.blob), nat.ptr(flat), nat.INDEX_CODES[flat.dtype],
@@ -246,3 +254,139 @@ class CardGrid:
         if self.summary is None:
             return cards, None
         return cards, torch.nn.functional.linear(cards.flatten(-2), self.summary)
+
+
+HEADS = ("exchange", "declare", "play")  # cardgym/games/piquet/engine.py:56
+PLAYERS = 2
+
+
+@dataclass(frozen=True)
+class PiquetModelConfig:
+    """The reference's piquet ``[model]`` section (cardgym/games/piquet/model.py:79-108): the
+    16-layer actor by default."""
+
+    d_model: int = 256
+    n_layers: int = 16
+    n_heads: int = 8
+    n_kv_heads: int = 2
+    d_ff: int = 512
+    per_layer_dim: int = 64
+    value_embeddings: str = "alternating"
+    card_width: int = 32
+    card_hidden: int = 64
+    card_layers: int = 2
+    card_kernel: int = 3
+    score_dim: int = 64
+
+    def trunk(self) -> TrunkConfig:
+        return TrunkConfig(d_model=self.d_model, n_layers=self.n_layers, n_heads=self.n_heads,
+                           n_kv_heads=self.n_kv_heads, d_ff=self.d_ff, per_layer_dim=self.per_layer_dim,
+                           value_embeddings=self.value_embeddings, input_norm=True)
+
+
+class PiquetActor:
+    """The rollout side of ``PiquetActor`` (cardgym/games/piquet/model.py:365-411) over its
+    ``state_dict`` names: ``forward_ragged`` runs the card grid over every appended token, adds
+    its summary to the one-hot field sums, and decodes them through the trunk (fused into the
+    first tensor-core layer with a bf16 trunk); ``pop_context`` hands back the grid cards of
+    those tokens, which ``policy_logits`` scores for the exchange and play heads
+    (``CardScorer``; the exchange head appends the stop logit) while the declare head and the
+    player values are plain projections of the readout state.
+
+    ``precision = "bf16"`` is the reference's rollout form (bf16 autocast): the card grid in its
+    autocast rounding (always: ``CardGrid.cards``), the summary projection under bf16 autocast,
+    bf16 trunk GEMM operands. The scorers, the declare and stop heads and the value MLP run in
+    fp32 in both precisions (the reference runs those few small projections in bf16 under
+    autocast). The heads read only the readout state and its grid cards, so a wave can be
+    captured by ``graphs.DecodeGraphs``.
+    """
+
+    policy_heads = HEADS
+
+    def __init__(self, config: PiquetModelConfig, state: dict, device: torch.device | str = "cuda",
+                 precision: str = "bf16") -> None:
+        self.config = config
+        self.device = torch.device(device)
+        self.precision = precision
+        self.trunk = B200Trunk(config.trunk(), state, self.device, precision)
+
+        def get(name: str) -> torch.Tensor | None:
+            if name not in state:
+                return None
+            return torch.as_tensor(state[name]).detach().to(device=self.device, dtype=torch.float32).contiguous()
+
+        self.lookup = PiquetFieldLookup(get("embedding.fields.weight"), get("embedding.ple_fields.weight"),
+                                        get("embedding.value_fields.weight"))
+        self.grid = CardGrid(state, "embedding.grid.", self.device, blocks=config.card_layers, circular=False)
+        self.exchange_scorer = CardScorer(state, "exchange_scorer.", self.device)
+        self.play_scorer = CardScorer(state, "play_scorer.", self.device)
+        self.linear = {name: (get(f"{name}.weight"), get(f"{name}.bias"))
+                       for name in ("stop_head", "declare_head", "value_head.0", "value_head.2")}
+        self.kept: torch.Tensor | None = None
+
+    @property
+    def trunk_config(self) -> TrunkConfig:
+        return self.trunk.config
+
+    def new_cache(self, capacity: int, max_len: int, dtype: torch.dtype = torch.float16) -> KVCache:
+        return self.trunk.new_cache(capacity, max_len, dtype)
+
+    def step_workspace_bytes(self, batch: int, steps: int) -> int:
+        return self.trunk.step_workspace_bytes(batch, steps)
+
+    def _grid(self, tokens: torch.Tensor):
+        codes = tokens[..., CARD_START:]
+        if self.precision == "bf16":
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                return self.grid(codes)
+        return self.grid(codes)
+
+    def forward_ragged(self, tokens: torch.Tensor, positions: torch.Tensor, cache: KVCache,
+                       readout_offsets: torch.Tensor, span: int | None = None, rows: torch.Tensor | None = None,
+                       workspace: torch.Tensor | None = None) -> torch.Tensor:
+        """Append a padded run per cache row 0..B-1 (or ``rows``); hidden at each readout [B, d]
+        (cardgym/nn/model.py:76-89). Keeps the appended tokens' grid cards for ``pop_context``."""
+
+        cards, summary = self._grid(tokens)
+        self.kept = cards
+        return forward_ragged(self.trunk, self.lookup, tokens, positions, cache, readout_offsets, span=span,
+                              rows=rows, summary=summary, workspace=workspace)
+
+    def forward_prefill(self, tokens: torch.Tensor, cache: KVCache, rows: torch.Tensor | None) -> torch.Tensor:
+        """Fresh prefixes [B, T, 64] at positions 0..T-1; hidden at the last position."""
+
+        batch, steps, _ = tokens.shape
+        positions = torch.zeros(batch, dtype=torch.int64, device=self.device)
+        offsets = torch.full((batch,), steps - 1, dtype=torch.int64, device=self.device)
+        return self.forward_ragged(tokens, positions, cache, offsets, span=steps, rows=rows)
+
+    def pop_context(self) -> torch.Tensor | None:
+        """The grid cards [B, T, 32, card_width] of the last forward's tokens (model.py:389-391)."""
+
+        cards, self.kept = self.kept, None
+        return cards
+
+    def _project(self, name: str, x: torch.Tensor) -> torch.Tensor:
+        weight, bias = self.linear[name]
+        return torch.nn.functional.linear(x.float(), weight, bias)
+
+    def policy_logits(self, hidden: torch.Tensor, head: str, features=None, tokens=None, context=None) -> torch.Tensor:
+        """fp32 logits of ``head`` at each readout (model.py:393-406)."""
+
+        if head == "declare":
+            return self._project("declare_head", hidden)
+        if head not in ("exchange", "play"):
+            raise ValueError(f"Unknown piquet policy head {head!r}.")
+        if context is None:
+            if tokens is None:
+                raise ValueError("Card heads need the readout tokens or their grid features.")
+            context = self.grid.cards(tokens[..., CARD_START:])
+        if head == "play":
+            return self.play_scorer(hidden, context)
+        return torch.cat([self.exchange_scorer(hidden, context), self._project("stop_head", hidden)], dim=-1)
+
+    def player_values(self, hidden: torch.Tensor) -> torch.Tensor:
+        """value_head: Linear -> exact GELU -> Linear, fp32 [N, 2] (cardgym/nn/model.py:12-17)."""
+
+        inner = torch.nn.functional.gelu(self._project("value_head.0", hidden))
+        return self._project("value_head.2", inner)

@@ -142,16 +142,20 @@ class B200Trunk:
         readout_offsets: torch.Tensor,
         span: int | None = None,
         rows: torch.Tensor | None = None,
+        workspace: torch.Tensor | None = None,
     ) -> torch.Tensor:
-        """Append a padded run of tokens per row; final-norm hidden at each readout [B, d] (trunk.py:391-429)."""
+        """Append a padded run of tokens per row; final-norm hidden at each readout [B, d] (trunk.py:391-429).
+
+        ``workspace`` (uint8, at least ``step_workspace_bytes``) pins the step's scratch memory,
+        for callers that capture the step in a CUDA graph; by default a shared buffer is used.
+        """
 
         batch, steps, _ = x.shape
         if span is None:
             span = int(positions.max()) + steps
         span = min(span, cache.max_len)
         x = x.float().contiguous()
-        need = nat.query("cg_trunk_step_workspace_bytes", self.dims, batch, steps, nat.PRECISIONS[self.precision])
-        workspace = nat.Workspace.get(self.device, need)
+        workspace = self.workspace(batch, steps, workspace)
         hidden = torch.empty((batch, self.config.d_model), device=self.device)
         nat.call(
             "cg_trunk_forward_ragged", self.dims, nat.ptr(self.blob), nat.ptr(x),
@@ -164,6 +168,19 @@ class B200Trunk:
             nat.stream_handle(self.device),
         )
         return hidden
+
+    def step_workspace_bytes(self, batch: int, steps: int) -> int:
+        return nat.query("cg_trunk_step_workspace_bytes", self.dims, batch, steps, nat.PRECISIONS[self.precision])
+
+    def workspace(self, batch: int, steps: int, given: torch.Tensor | None = None) -> torch.Tensor:
+        """The caller's scratch buffer (checked for size) or the shared one."""
+
+        need = self.step_workspace_bytes(batch, steps)
+        if given is None:
+            return nat.Workspace.get(self.device, need)
+        if given.numel() < need:
+            raise ValueError(f"workspace of {given.numel()} bytes < {need} needed")
+        return given
 
     @property
     def scale(self) -> float:

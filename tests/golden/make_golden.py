@@ -24,6 +24,7 @@ Fixtures:
   candidate_scorer.npz the rummy candidate pointer head (``CandidateScorer``), draw and play calls
   card_grid.npz       the piquet card grid (``CardGrid``) in fp32 and bf16 autocast
   ledger_grid.npz     rummy's ledger grid (52 cards, circular 5-tap convolution), same forms
+  piquet_actor.npz    the piquet actor (lookup + card grid + trunk + heads) at a small trunk, fp32
 
 ``python tests/golden/make_golden.py piquet_bags`` regenerates one fixture.
 """
@@ -467,6 +468,46 @@ def make_ledger_grid() -> None:
                         cards_bf16=cards16.float().numpy(), **state)
 
 
+PIQUET_ACTOR_CONFIG = dict(d_model=32, n_layers=2, n_heads=4, n_kv_heads=2, d_ff=64, per_layer_dim=8)
+
+
+def make_piquet_actor() -> None:
+    """The reference ``PiquetActor`` (cardgym/games/piquet/model.py:365-411) at a small trunk:
+    the full causal forward of random piquet token rows (32 field ids + 32 card codes), the
+    hidden state at one readout per row, every head's logits there with the readout's grid
+    cards as context, and the player values; fp32. The parameters the reference initialises
+    to zero (conditioning tables, biases) are drawn small so that every term carries signal."""
+
+    from cardgym.games.piquet.model import FIELD_VOCAB, PiquetActor, PiquetModelConfig
+
+    torch.manual_seed(91)
+    model = PiquetActor(PiquetModelConfig(**PIQUET_ACTOR_CONFIG))
+    with torch.no_grad():
+        for param in model.parameters():
+            if not param.any():
+                param.normal_(0.0, 0.02)
+    model.eval()
+    rng = np.random.default_rng(92)
+    batch, steps = 6, 12
+    fields = np.stack([rng.integers(0, vocab, (batch, steps)) for vocab in FIELD_VOCAB], axis=-1)
+    cards = rng.integers(0, 12, (batch, steps, 32))
+    tokens = torch.from_numpy(np.concatenate([fields, cards], axis=-1).astype(np.int64))
+    readouts = rng.integers(0, steps, batch)
+    rows = torch.arange(batch)
+    with torch.no_grad():
+        hidden = model.forward_hidden(tokens)[rows, readouts]
+        context = model.pop_context()[rows, readouts]
+        logits = {f"logits_{head}": model.policy_logits(hidden, head, None, None, context).numpy()
+                  for head in model.policy_heads}
+        values = model.player_values(hidden).numpy()
+    state = {f"w_{k}": v.numpy() for k, v in model.state_dict().items()}
+    np.savez_compressed(HERE / "piquet_actor.npz", tokens=tokens.numpy().astype(np.int16), readouts=readouts,
+                        hidden=hidden.numpy(), values=values, heads=np.array(model.policy_heads),
+                        config_keys=np.array(list(PIQUET_ACTOR_CONFIG)),
+                        config_values=np.array([PIQUET_ACTOR_CONFIG[k] for k in PIQUET_ACTOR_CONFIG]),
+                        **logits, **state)
+
+
 def main() -> None:
     only = set(sys.argv[1:])
     if only:
@@ -489,6 +530,7 @@ def main() -> None:
     make_candidate_scorer()
     make_card_grid()
     make_ledger_grid()
+    make_piquet_actor()
     for path in sorted(HERE.glob("*.npz")):
         print(f"{path.name}: {path.stat().st_size / 1024:.0f} KiB")
 

@@ -287,3 +287,76 @@ def test_card_grid_at_wave_size_matches_the_oracle():
     # Identical roundings but for the rare intermediate at a bf16 tie (fp32 sums here, exact
     # ones in the oracle), which moves a token's features by about one bf16 step.
     assert (diff > 1e-5).mean() < 0.02 and diff.mean() < 1e-4 and diff.max() < 0.04
+
+
+def _piquet_actor(precision: str):
+    from card_playing_gym_b200.piquet import PiquetActor, PiquetModelConfig
+
+    data = load_golden("piquet_actor")
+    config = PiquetModelConfig(**{str(k): int(v) for k, v in zip(data["config_keys"], data["config_values"])})
+    state = {k[2:]: v for k, v in data.items() if k.startswith("w_")}
+    return data, PiquetActor(config, state, precision=precision)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("precision,kv,tol", [("fp32", torch.float32, 2e-2), ("bf16", torch.float16, 5e-2)])
+def test_piquet_actor_matches_the_reference_actor(precision, kv, tol):
+    """``PiquetActor`` against the reference's own (cardgym/games/piquet/model.py:365-411, fp32):
+    hidden state at each row's readout after a 12-token prefill, every head's logits with the
+    readout's grid cards as context, the player values. The tolerance (max |error| / max |value|)
+    covers the grid cards, which are always in the reference's bf16-autocast rounding here,
+    and in bf16 mode the trunk's bf16 GEMM operands and fp16 KV."""
+
+    data, actor = _piquet_actor(precision)
+    tokens = torch.from_numpy(data["tokens"].astype(np.int64)).cuda()
+    batch, steps, _ = tokens.shape
+    readouts = torch.from_numpy(data["readouts"]).cuda()
+    cache = actor.new_cache(batch, steps + 1, kv)
+    hidden = actor.forward_ragged(tokens, torch.zeros(batch, dtype=torch.int64, device="cuda"), cache, readouts,
+                                  span=steps)
+    context = actor.pop_context()[torch.arange(batch, device="cuda"), readouts]
+    assert actor.pop_context() is None
+
+    def scaled(got, want):
+        return float(np.abs(got - want).max() / np.abs(want).max())
+
+    assert scaled(hidden.cpu().numpy(), data["hidden"]) < tol
+    for head in actor.policy_heads:
+        logits = actor.policy_logits(hidden, head, None, None, context).cpu().numpy()
+        assert logits.shape == data[f"logits_{head}"].shape
+        assert scaled(logits, data[f"logits_{head}"]) < tol, head
+    assert scaled(actor.player_values(hidden).cpu().numpy(), data["values"]) < tol
+    with pytest.raises(ValueError):
+        actor.policy_logits(hidden, "bid")
+
+
+@pytest.mark.gpu
+def test_piquet_actor_decode_graphs_match_the_eager_wave():
+    """A piquet wave captured by ``DecodeGraphs`` (card grid, fused lookup + trunk, the card
+    scorers fed the readout's grid cards) replays the eager calls bit for bit."""
+
+    from card_playing_gym_b200.graphs import DecodeGraphs
+
+    data, actor = _piquet_actor("bf16")
+    streams = data["tokens"].astype(np.int64)
+    batch = streams.shape[0]
+    graph_cache = actor.new_cache(batch + 1, 16, torch.float16)
+    eager_cache = actor.new_cache(batch + 1, 16, torch.float16)
+    graphs = DecodeGraphs(actor, graph_cache, values=True)
+    cache_rows = np.arange(1, batch + 1, dtype=np.int64)
+    position = 0
+    for run in (4, 1, 1, 2):
+        tokens = streams[:, position:position + run]
+        positions = np.full(batch, position, np.int64)
+        offsets = np.full(batch, run - 1, np.int64)
+        got = graphs.run(tokens, positions, offsets, cache_rows, span=16).clone()
+        cuda = lambda a: torch.from_numpy(a).cuda()  # noqa: E731
+        hidden = actor.forward_ragged(cuda(tokens), cuda(positions), eager_cache, cuda(offsets), span=16,
+                                      rows=cuda(cache_rows))
+        context = actor.pop_context()[torch.arange(batch, device="cuda"), cuda(offsets)]
+        want = torch.cat([actor.policy_logits(hidden, head, None, None, context) for head in actor.policy_heads]
+                         + [actor.player_values(hidden)], dim=-1)
+        assert torch.equal(got, want), (run, position)
+        position += run
+    assert graphs.columns["exchange"] == slice(0, 33) and graphs.columns["values"] == slice(67, 69)
+    assert torch.equal(graph_cache.k_pool, eager_cache.k_pool)
