@@ -302,6 +302,8 @@ class PiquetActor:
     """
 
     policy_heads = HEADS
+    # Every head reads only the readout state and its grid cards (model.py:367-370).
+    graphable_heads = True
 
     def __init__(self, config: PiquetModelConfig, state: dict, device: torch.device | str = "cuda",
                  precision: str = "bf16") -> None:
