@@ -37,24 +37,29 @@ class ScriptedGame:
     stream's length, which is what an eager recomputation needs.
     """
 
+    players = 4
+
     def __init__(self, seed: int, pool: np.ndarray, *, restart: int | None = None, max_steps: int = 7):
         self.seed = seed
         self.rng = random.Random(seed ^ 0x5EED)
         self._script = random.Random(seed)
-        self.num_players = 4
+        self.num_players = self.players
         self.pool = pool
         self.steps_left = self._script.randint(0, max_steps)
         self.turn = 0
         self.restart = restart
-        self.streams = [[] for _ in range(4)]
-        self.context_base = [0, 0, 0, 0]
+        self.streams = [[] for _ in range(self.players)]
+        self.context_base = [0] * self.players
         self._starts = None
         self.log = []  # (seat, head, legal, context base, stream length)
         self.actions = []
 
+    def head(self) -> tuple[str, int]:
+        return ("bid", BID) if self.turn < 4 else ("play", PLAY)
+
     def _blocks(self, low: int, high: int):
         blocks = []
-        for seat in range(4):
+        for seat in range(self.players):
             count = self._script.randint(low, high)
             rows = [self._script.randrange(len(self.pool)) for _ in range(count)]
             block = self.pool[rows].astype(np.int16)
@@ -66,9 +71,8 @@ class ScriptedGame:
         return self._blocks(1, 3)
 
     def decision(self):
-        seat = self.turn % 4
-        head = "bid" if self.turn < 4 else "play"
-        width = BID if head == "bid" else PLAY
+        seat = self.turn % self.players
+        head, width = self.head()
         legal = np.array([self._script.random() < 0.5 for _ in range(width)])
         legal[self._script.randrange(width)] = True
         self.log.append((seat, head, legal, self.context_base[seat], len(self.streams[seat])))
@@ -84,8 +88,8 @@ class ScriptedGame:
         blocks = self._blocks(1, 2)
         self._starts = None
         if self.restart is not None and self.turn == self.restart and not self.done():
-            starts = [None] * 4
-            for restarted in (0, 2):
+            starts = [None] * self.players
+            for restarted in range(0, self.players, 2):
                 starts[restarted] = len(blocks[restarted]) - 1
                 self.context_base[restarted] = before[restarted] + starts[restarted]
             self._starts = starts
@@ -95,11 +99,21 @@ class ScriptedGame:
         return self.steps_left <= 0
 
     def returns(self):
-        score = np.array([self._script.uniform(-1, 1) for _ in range(4)])
+        score = np.array([self._script.uniform(-1, 1) for _ in range(self.players)])
         return score - score.mean()
 
     def context_starts(self):
         return self._starts
+
+
+class ScriptedPiquet(ScriptedGame):
+    """The same script with two seats, piquet tokens and piquet's heads: exchange (32 cards +
+    stop), declare (2), play (32 cards)."""
+
+    players = 2
+
+    def head(self) -> tuple[str, int]:
+        return (("exchange", 33), ("declare", 2), ("play", 32))[min(self.turn // 2, 2)]
 
 
 def _pool() -> np.ndarray:
@@ -287,3 +301,42 @@ def test_collector_decisions_match_an_eager_prefill():
             checked += 1
     assert checked > 100
     assert collector.stats.waves > 0 and collector.stats.peak_rows > 0
+
+
+@pytest.mark.gpu
+def test_collector_runs_piquet_pointer_heads():
+    """The collector over a piquet actor: the card scorers read each readout token's grid cards
+    through ``pop_context`` inside the graphed wave; every recorded decision against an eager
+    prefill of its context with the same context cards (fp32)."""
+
+    from card_playing_gym_b200.piquet import PiquetActor, PiquetModelConfig
+
+    data = load_golden("piquet_actor")
+    config = PiquetModelConfig(**{str(k): int(v) for k, v in zip(data["config_keys"], data["config_values"])})
+    actor = PiquetActor(config, {k[2:]: v for k, v in data.items() if k.startswith("w_")}, precision="fp32")
+    pool = data["tokens"].reshape(-1, data["tokens"].shape[-1]).astype(np.int64)
+
+    def deal(rng):
+        seed = rng.randrange(1 << 30)
+        return ScriptedPiquet(seed, pool, restart=3 if seed % 2 else None)
+
+    lanes = [cont.Lane("piquet", 2, 20, 30, deal=deal)]
+    collector = cont.ContinuousCollector(actor, max_length=48, cohorts=2, kv_dtype="fp32", record_values=True)
+    results = collector.collect(lanes, random.Random(11))
+    assert len(results) == 30
+    cache = actor.new_cache(1, 48, torch.float32)
+    checked = set()
+    for trajectory in results:
+        game = trajectory.game
+        replay = random.Random(game.seed ^ 0x5EED)
+        for record, (seat, head, legal, base, length) in zip(trajectory.decisions, game.log):
+            context = trajectory.streams[seat][base:length].astype(np.int64)
+            hidden = actor.forward_prefill(torch.from_numpy(context[None]).cuda(), cache, rows=None)
+            cards = actor.pop_context()[:, -1]
+            logits = actor.policy_logits(hidden, head, None, None, cards).cpu().numpy()
+            probs = oppo.masked_probabilities(logits, legal[None])[0]
+            np.testing.assert_allclose(record.probs, probs, rtol=0, atol=2e-5)
+            np.testing.assert_allclose(record.value, actor.player_values(hidden).cpu().numpy()[0], rtol=0, atol=2e-4)
+            assert record.action == oppo.sample_rows(record.probs[None], legal[None], np.array([replay.random()]))[0]
+            checked.add(head)
+    assert checked == {"exchange", "declare", "play"}
