@@ -452,8 +452,9 @@ def run_pointer_wave(args, device, rank: int, world_size: int, kind: str) -> dic
       d256/16L/8-2/d_ff 512, piquet field tables (32 fields, 964 rows), one decision per deal
       scored by CardScorer over its 32 cards.
     rummy: 8,192 slots, half of them decoded per wave through gathered rows (the continuous
-      collector's form), lengths U[8, 384], trunk d256/8L/8-2/d_ff 768, one decision per three
-      decoded rows scored by CandidateScorer over U[1, 64] candidates (padded to the wave's max).
+      collector's form), lengths U[8, 384], 1 in 32 decoded rows a replaced game's first token
+      at position 0, trunk d256/8L/8-2/d_ff 768, one decision per three decoded rows scored by
+      CandidateScorer over U[1, 64] candidates (padded to the wave's max).
     Each wave runs the embedder's grid over the decoded tokens first (piquet's card grid over the
     tokens' card codes, rummy's ledger grid over a 52-card ledger) and fuses its summary into the
     trunk's input; the heads read the readout token's grid cards."""
@@ -493,6 +494,10 @@ def run_pointer_wave(args, device, rank: int, world_size: int, kind: str) -> dic
     tokens[:, 0, 32:] = rng.integers(0, 12, (decoded, 32))  # card codes (the piquet card grid's input)
     rows = np.sort(rng.choice(slots, decoded, replace=False)) if decoded < slots else np.arange(slots)
     positions = (lengths[rows] - 1).astype(np.int64)
+    if kind == "rummy":
+        # Games that finished and were replaced in this wave: the slot's length resets and the
+        # new game's first token goes to position 0 (continuous.py:383-408).
+        positions[rng.random(decoded) < 1.0 / 32] = 0
     dev_tokens = torch.from_numpy(tokens).to(device)
     dev_rows = torch.from_numpy(rows.astype(np.int64)).to(device)
     dev_positions = torch.from_numpy(positions).to(device)
@@ -587,7 +592,8 @@ def run_pointer_wave(args, device, rank: int, world_size: int, kind: str) -> dic
                    " fp16 KV, card grid (2 blocks) + summary, one-hot field lookup (32 fields, 964 rows) fused into the "
                    "trunk d256/16L/8-2/d_ff 512 -> CardScorer over the readout's 32 card features -> masked sampling"),
         "rummy": (f"rummy-style continuous wave: {slots} slots, {decoded} gathered rows decoded (1 token/row), lengths "
-                  f"U[{min_len},{max_len}], fp16 KV, ledger grid (52 cards, 2 blocks) + summary, one-hot field lookup "
+                  f"U[{min_len},{max_len}] (1 in 32 a replaced game at position 0), fp16 KV, ledger grid (52 cards, "
+                  "2 blocks) + summary, one-hot field lookup "
                   f"(piquet's tables standing in for rummy's fields) fused into the trunk d256/8L/8-2/d_ff 768 -> "
                   f"CandidateScorer over U[1,64] candidates (padded to {width}) -> masked sampling"),
     }[kind]
