@@ -37,10 +37,10 @@ FIELD_VOCAB = (8, 4, 3, 2, 33, 9, 9, 4, 4, 9, 76, 9, 3, 4, 64, 5, 3, 13, 3, 5, 1
 FIELD_ROWS = sum(FIELD_VOCAB)
 
 
-def field_offsets() -> list[int]:
-    """First table row of each field (``PiquetEmbedding.offsets``)."""
+def field_offsets(vocab: tuple[int, ...] = FIELD_VOCAB) -> list[int]:
+    """First table row of each field (``PiquetEmbedding.offsets``; rummy's with its vocabulary)."""
 
-    return [sum(FIELD_VOCAB[:i]) for i in range(NUM_FIELDS)]
+    return [sum(vocab[:i]) for i in range(len(vocab))]
 
 
 def _lookup_dtype(tables: list[torch.Tensor]) -> torch.dtype:
@@ -87,10 +87,14 @@ class PiquetFieldLookup:
     dtype (the autocast dtype on CUDA, else the tables').
     """
 
-    def __init__(self, fields: torch.Tensor, ple: torch.Tensor | None = None, values: torch.Tensor | None = None):
+    def __init__(self, fields: torch.Tensor, ple: torch.Tensor | None = None, values: torch.Tensor | None = None,
+                 vocab: tuple[int, ...] = FIELD_VOCAB):
         self.parts = [fields] + [t for t in (ple, values) if t is not None]
         self.has = (ple is not None, values is not None)
-        self.offsets = field_offsets()
+        # Each field's ids live in their own rows, so no two fields of a token select the same row:
+        # the one-hot product (piquet) and the bag sum (rummy's F.embedding_bag) agree.
+        self.fields = len(vocab)
+        self.offsets = field_offsets(vocab)
         self._packed: dict[torch.dtype, torch.Tensor] = {}
 
     def table(self, dtype: torch.dtype) -> torch.Tensor:
@@ -106,7 +110,7 @@ class PiquetFieldLookup:
         if flat.dtype not in nat.INDEX_CODES:
             flat = flat.long()
         flat = flat.contiguous()
-        sums = _bags(flat, flat.shape[1], NUM_FIELDS, self.offsets, self.table(dtype), tuple(tokens.shape[:-1]))
+        sums = _bags(flat, flat.shape[1], self.fields, self.offsets, self.table(dtype), tuple(tokens.shape[:-1]))
         parts = iter(sums.split([t.shape[1] for t in self.parts], dim=-1))
         first = next(parts)
         ple = next(parts) if self.has[0] else None
@@ -180,9 +184,9 @@ def forward_ragged(trunk, lookup: PiquetFieldLookup, tokens: torch.Tensor, posit
     extra = None if summary is None else summary.reshape(-1, summary.shape[-1]).float().contiguous()
     workspace = trunk.workspace(batch, steps, workspace)
     hidden = torch.empty((batch, trunk.config.d_model), device=trunk.device)
-    offsets = (nat._i64 * NUM_FIELDS)(*lookup.offsets)
+    offsets = (nat._i64 * lookup.fields)(*lookup.offsets)
     nat.call("cg_bags_forward_ragged", trunk.dims, nat.ptr(trunk.blob), nat.ptr(flat), nat.INDEX_CODES[flat.dtype],
-             flat.shape[1], NUM_FIELDS, offsets, nat.ptr(table), table.shape[0], nat.ptr(extra), batch, steps,
+             flat.shape[1], lookup.fields, offsets, nat.ptr(table), table.shape[0], nat.ptr(extra), batch, steps,
              nat.ptr(positions.to(torch.int64).contiguous()), nat.ptr(readout_offsets.to(torch.int64).contiguous()),
              nat.ptr(None if rows is None else rows.to(torch.int64).contiguous()), int(span), nat.ptr(cache.k_pool),
              nat.ptr(cache.v_pool), nat.DTYPE_CODES[cache.dtype], cache.capacity, cache.max_len,

@@ -25,6 +25,7 @@ Fixtures:
   card_grid.npz       the piquet card grid (``CardGrid``) in fp32 and bf16 autocast
   ledger_grid.npz     rummy's ledger grid (52 cards, circular 5-tap convolution), same forms
   piquet_actor.npz    the piquet actor (lookup + card grid + trunk + heads) at a small trunk, fp32
+  rummy_actor.npz     the rummy actor (lookup + ledger grid + trunk + candidate heads), same form
 
 ``python tests/golden/make_golden.py piquet_bags`` regenerates one fixture.
 """
@@ -508,6 +509,61 @@ def make_piquet_actor() -> None:
                         **logits, **state)
 
 
+RUMMY_ACTOR_CONFIG = dict(d_model=32, n_layers=2, n_heads=4, n_kv_heads=2, d_ff=64, per_layer_dim=8)
+
+
+def make_rummy_actor() -> None:
+    """The reference ``RummyActor`` (cardgym/games/rummy/model.py:359-402) at a small trunk: the
+    full causal forward of random rummy token rows (26 field ids + a 52-card ledger), the hidden
+    state at one readout per row, both heads' candidate logits there (draw with taken counts,
+    play without; 9 candidates, the readout's ledger cards as context) and the player values;
+    fp32. Zero-initialised parameters are drawn small so that every term carries signal."""
+
+    from cardgym.games.rummy.cards import NO_CARD
+    from cardgym.games.rummy.model import RummyActor, RummyModelConfig
+    from cardgym.games.rummy.tokens import CARD_VOCAB, FIELD_VOCAB
+
+    torch.manual_seed(101)
+    model = RummyActor(RummyModelConfig(**RUMMY_ACTOR_CONFIG))
+    with torch.no_grad():
+        for param in model.parameters():
+            if not param.any():
+                param.normal_(0.0, 0.02)
+    model.eval()
+    rng = np.random.default_rng(102)
+    batch, steps, width, listed = 5, 10, 9, 13
+    fields = np.stack([rng.integers(0, vocab, (batch, steps)) for vocab in FIELD_VOCAB], axis=-1)
+    ledger = rng.integers(0, CARD_VOCAB, (batch, steps, 52))
+    tokens = torch.from_numpy(np.concatenate([fields, ledger], axis=-1).astype(np.int64))
+    readouts = rng.integers(0, steps, batch)
+    kind = rng.integers(0, 7, (batch, width))
+    cards = np.full((batch, width, listed), NO_CARD, dtype=np.int64)
+    target = np.full((batch, width, listed), NO_CARD, dtype=np.int64)
+    for r in range(batch):
+        for c in range(width):
+            n_cards = rng.integers(0, listed + 1)
+            cards[r, c, :n_cards] = rng.integers(0, 52, n_cards)
+            if rng.random() < 0.3:
+                n_target = rng.integers(1, 6)
+                target[r, c, :n_target] = rng.integers(0, 52, n_target)
+    taken = (rng.random((batch, width, 52)) < 0.1) * rng.integers(1, 3, (batch, width, 52))
+    rows = torch.arange(batch)
+    features = {"kind": torch.from_numpy(kind), "cards": torch.from_numpy(cards), "target": torch.from_numpy(target)}
+    with torch.no_grad():
+        hidden = model.forward_hidden(tokens)[rows, readouts]
+        context = model.pop_context()[rows, readouts]
+        logits_draw = model.policy_logits(hidden, "draw", {**features, "taken": torch.from_numpy(taken)}, None, context)
+        logits_play = model.policy_logits(hidden, "play", features, None, context)
+        values = model.player_values(hidden)
+    state = {f"w_{k}": v.numpy() for k, v in model.state_dict().items()}
+    np.savez_compressed(HERE / "rummy_actor.npz", tokens=tokens.numpy().astype(np.int16), readouts=readouts,
+                        hidden=hidden.numpy(), values=values.numpy(), logits_draw=logits_draw.numpy(),
+                        logits_play=logits_play.numpy(), kind=kind.astype(np.int8), cards=cards.astype(np.int8),
+                        target=target.astype(np.int8), taken=taken.astype(np.int8),
+                        field_vocab=np.array(FIELD_VOCAB), config_keys=np.array(list(RUMMY_ACTOR_CONFIG)),
+                        config_values=np.array([RUMMY_ACTOR_CONFIG[k] for k in RUMMY_ACTOR_CONFIG]), **state)
+
+
 def main() -> None:
     only = set(sys.argv[1:])
     if only:
@@ -531,6 +587,7 @@ def main() -> None:
     make_card_grid()
     make_ledger_grid()
     make_piquet_actor()
+    make_rummy_actor()
     for path in sorted(HERE.glob("*.npz")):
         print(f"{path.name}: {path.stat().st_size / 1024:.0f} KiB")
 

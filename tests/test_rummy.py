@@ -110,3 +110,52 @@ def test_ledger_grid_matches_the_reference_autocast_form():
     diff = np.abs(cards - oracle16)
     assert (diff > 1e-5).mean() < 0.02 and diff.mean() < 1e-4
     assert nat.fault_status() == 0
+
+
+def test_rummy_field_vocabulary_matches_the_reference():
+    """The restated token layout (cardgym/games/rummy/tokens.py:87-124) against the reference's own."""
+
+    from card_playing_gym_b200 import rummy
+
+    data = load_golden("rummy_actor")
+    assert rummy.FIELD_VOCAB == tuple(int(v) for v in data["field_vocab"])
+    assert len(rummy.FIELD_VOCAB) == rummy.NUM_FIELDS == rummy.CARD_START
+    assert data["tokens"].shape[-1] == rummy.CARD_START + 52
+    assert int(data["tokens"][..., rummy.CARD_START:].max()) < rummy.CARD_VOCAB
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("precision,kv,tol", [("fp32", torch.float32, 2e-2), ("bf16", torch.float16, 5e-2)])
+def test_rummy_actor_matches_the_reference_actor(precision, kv, tol):
+    """``RummyActor`` against the reference's own (cardgym/games/rummy/model.py:359-402, fp32): the
+    hidden state at each row's readout after a 10-token prefill, both heads' candidate logits
+    (draw with taken counts, play without) with the readout's ledger cards as context, the
+    player values. Tolerance as for the piquet actor: the ledger cards are always in the
+    reference's bf16-autocast rounding here."""
+
+    from card_playing_gym_b200.rummy import RummyActor, RummyModelConfig
+
+    data = load_golden("rummy_actor")
+    config = RummyModelConfig(**{str(k): int(v) for k, v in zip(data["config_keys"], data["config_values"])})
+    actor = RummyActor(config, {k[2:]: v for k, v in data.items() if k.startswith("w_")}, precision=precision)
+    tokens = torch.from_numpy(data["tokens"].astype(np.int64)).cuda()
+    batch, steps, _ = tokens.shape
+    readouts = torch.from_numpy(data["readouts"]).cuda()
+    cache = actor.new_cache(batch, steps + 1, kv)
+    hidden = actor.forward_ragged(tokens, torch.zeros(batch, dtype=torch.int64, device="cuda"), cache, readouts,
+                                  span=steps)
+    context = actor.pop_context()[torch.arange(batch, device="cuda"), readouts]
+    features = {name: torch.from_numpy(data[name].astype(np.int64)).cuda() for name in ("kind", "cards", "target")}
+
+    def scaled(got, want):
+        return float(np.abs(got - want).max() / np.abs(want).max())
+
+    assert scaled(hidden.cpu().numpy(), data["hidden"]) < tol
+    draw = actor.policy_logits(hidden, "draw", {**features, "taken": torch.from_numpy(data["taken"]).cuda()},
+                               None, context)
+    assert scaled(draw.cpu().numpy(), data["logits_draw"]) < tol
+    play = actor.policy_logits(hidden, "play", features, None, context)
+    assert scaled(play.cpu().numpy(), data["logits_play"]) < tol
+    assert scaled(actor.player_values(hidden).cpu().numpy(), data["values"]) < tol
+    with pytest.raises(ValueError):
+        actor.policy_logits(hidden, "play", None, None, context)
