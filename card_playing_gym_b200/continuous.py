@@ -290,6 +290,75 @@ class DeviceWaves:
             wave.fence.synchronize()
 
 
+def stack_features(features: list[dict[str, np.ndarray]]) -> dict[str, np.ndarray]:
+    """Per-decision candidate features padded with zeros along the candidate axis and stacked
+    (selfplay.py:570-587, ``_stack_features`` without the shape bucket)."""
+
+    count = max(next(iter(entry.values())).shape[0] for entry in features)
+    stacked = {}
+    for key, first in features[0].items():
+        array = np.zeros((len(features), count, *first.shape[1:]), dtype=first.dtype)
+        for row, entry in enumerate(features):
+            value = entry[key]
+            array[row, : value.shape[0]] = value
+        stacked[key] = array
+    return stacked
+
+
+class EagerWaves(DeviceWaves):
+    """The device half for models whose heads take per-decision candidate features (rummy): the
+    wave's launches are issued eagerly (continuous.py:333-353), each head group's features are
+    stacked and uploaded, and the head's logits go straight into masked sampling on the device.
+    """
+
+    def __init__(self, model, cache, *, values: bool) -> None:
+        self.model = model
+        self.cache = cache
+        self.values = values
+        self.device = cache.device
+
+    def launch(self, wave: PackedWave, readouts: list[tuple[int, LiveGame, float]]) -> _Wave:
+        from .sampling import masked_sample
+
+        model = self.model
+        tokens, positions, offsets, cache_rows = (
+            _pinned(a, self.device) for a in (wave.tokens, wave.positions, wave.offsets, wave.cache_rows))
+        hidden = model.forward_ragged(tokens, positions, self.cache, offsets, span=min(wave.span, self.cache.max_len),
+                                      rows=cache_rows)
+        pop = getattr(model, "pop_context", None)
+        context = pop() if pop is not None else None
+        groups: dict[str, list[tuple[int, LiveGame, float]]] = {}
+        for entry in readouts:
+            groups.setdefault(entry[1].pending.head, []).append(entry)
+        result = _Wave()
+        for head, group in groups.items():
+            entries = np.fromiter((entry for entry, _, _ in group), dtype=np.int64, count=len(group))
+            index = _pinned(entries, self.device)
+            head_hidden = hidden.index_select(0, index)
+            head_context = None
+            if context is not None:
+                head_context = context[index, _pinned(wave.offsets[entries], self.device)]
+            decisions = [state.pending for _, state, _ in group]
+            features = None
+            if decisions[0].features is not None:
+                features = {k: _pinned(v, self.device) for k, v in stack_features([d.features for d in decisions]).items()}
+            logits = model.policy_logits(head_hidden, head, features, None, head_context).float()
+            width = logits.shape[1]
+            if max(d.legal.shape[0] for d in decisions) > width:
+                raise ValueError(f"head {head!r} scored {width} actions, a decision offers more")
+            legal = np.zeros((len(group), width), dtype=np.uint8)
+            for row, decision in enumerate(decisions):
+                legal[row, : decision.legal.shape[0]] = decision.legal
+            uniforms = _pinned(np.fromiter((u for _, _, u in group), dtype=np.float64, count=len(group)), self.device)
+            probs, actions = masked_sample(logits, _pinned(legal, self.device), uniforms)
+            values = model.player_values(head_hidden).float().to("cpu", non_blocking=True) if self.values else None
+            result.readouts.append(_Readout([state for _, state, _ in group], probs.to("cpu", non_blocking=True),
+                                            actions.to("cpu", non_blocking=True), values))
+        result.fence = torch.cuda.Event()
+        result.fence.record()
+        return result
+
+
 class ContinuousCollector:
     """Keeps every lane's ``in_flight`` games running; ``collect`` returns each lane's quota
     of finished games (continuous.py:115-408). Games still running carry over, with their
@@ -313,7 +382,10 @@ class ContinuousCollector:
         # One spare position past the longest stream absorbs ragged padding.
         self.cache_length = max_length + 1
         self.stats = CollectionStats()
-        self._waves_factory = waves_factory or (lambda cache: DeviceWaves(model, cache, values=record_values))
+        # Graph-captured waves for models whose heads read only the readout (plump, piquet), as
+        # the reference's graphs_enabled decides (graphs.py:49-56); eager waves otherwise.
+        kind = DeviceWaves if getattr(model, "graphable_heads", False) else EagerWaves
+        self._waves_factory = waves_factory or (lambda cache: kind(model, cache, values=record_values))
         self.reset()
 
     def reset(self) -> None:

@@ -98,6 +98,9 @@ class PlumpActor:
     """Rollout-side plump actor over reference-named weights (actor.pt ``state_dict`` or synthetic)."""
 
     policy_heads = POLICY_HEADS
+    # The heads read only the readout state and the lookup has no host synchronisation, so a
+    # wave can be captured whole (graphs.DecodeGraphs).
+    graphable_heads = True
 
     def __init__(self, config: PlumpModelConfig, state: dict, device: torch.device | str = "cuda", precision: str = "bf16") -> None:
         self.config = config

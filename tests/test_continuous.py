@@ -106,6 +106,35 @@ class ScriptedGame:
         return self._starts
 
 
+class ScriptedRummy(ScriptedGame):
+    """Three seats, rummy tokens and rummy's candidate heads: each decision offers 1-9
+    candidates with their features (kind, cards, target; taken counts for draws)."""
+
+    players = 3
+
+    def decision(self):
+        seat = self.turn % self.players
+        head = "draw" if self.turn % 2 == 0 else "play"
+        count = self._script.randint(1, 9)
+        features = {"kind": np.array([self._script.randrange(7) for _ in range(count)], dtype=np.int64),
+                    "cards": np.full((count, 13), 52, dtype=np.int64), "target": np.full((count, 13), 52, dtype=np.int64)}
+        for c in range(count):
+            n = self._script.randint(0, 4)
+            features["cards"][c, :n] = [self._script.randrange(52) for _ in range(n)]
+        if head == "draw":
+            features["taken"] = np.array([[self._script.randrange(3) if self._script.random() < 0.1 else 0
+                                           for _ in range(52)] for _ in range(count)], dtype=np.int64)
+        legal = np.array([self._script.random() < 0.6 for _ in range(count)])
+        legal[self._script.randrange(count)] = True
+        self.log.append((seat, head, legal, self.context_base[seat], len(self.streams[seat])))
+        self.features.append(features)
+        return cont.Decision(seat=seat, head=head, legal=legal, features=features)
+
+    def __init__(self, *args, **kwargs):
+        super().__init__(*args, **kwargs)
+        self.features = []
+
+
 class ScriptedPiquet(ScriptedGame):
     """The same script with two seats, piquet tokens and piquet's heads: exchange (32 cards +
     stop), declare (2), play (32 cards)."""
@@ -340,3 +369,45 @@ def test_collector_runs_piquet_pointer_heads():
             assert record.action == oppo.sample_rows(record.probs[None], legal[None], np.array([replay.random()]))[0]
             checked.add(head)
     assert checked == {"exchange", "declare", "play"}
+
+
+@pytest.mark.gpu
+def test_collector_runs_rummy_candidate_heads():
+    """The collector over a rummy actor (heads with per-decision candidate features, so eager
+    waves as in the reference): every recorded decision against an eager prefill of its context,
+    its ledger cards and its candidates (fp32)."""
+
+    from card_playing_gym_b200.rummy import RummyActor, RummyModelConfig
+
+    data = load_golden("rummy_actor")
+    config = RummyModelConfig(**{str(k): int(v) for k, v in zip(data["config_keys"], data["config_values"])})
+    actor = RummyActor(config, {k[2:]: v for k, v in data.items() if k.startswith("w_")}, precision="fp32")
+    pool = data["tokens"].reshape(-1, data["tokens"].shape[-1]).astype(np.int64)
+
+    def deal(rng):
+        seed = rng.randrange(1 << 30)
+        return ScriptedRummy(seed, pool, restart=2 if seed % 2 else None)
+
+    lanes = [cont.Lane("rummy", 3, 16, 24, deal=deal)]
+    collector = cont.ContinuousCollector(actor, max_length=48, cohorts=2, kv_dtype="fp32", record_values=True)
+    assert isinstance(collector._waves_factory(actor.new_cache(1, 2, torch.float32)), cont.EagerWaves)
+    results = collector.collect(lanes, random.Random(13))
+    assert len(results) == 24
+    cache = actor.new_cache(1, 48, torch.float32)
+    heads = set()
+    for trajectory in results:
+        game = trajectory.game
+        replay = random.Random(game.seed ^ 0x5EED)
+        for record, (seat, head, legal, base, length), features in zip(trajectory.decisions, game.log, game.features):
+            context = trajectory.streams[seat][base:length].astype(np.int64)
+            hidden = actor.forward_prefill(torch.from_numpy(context[None]).cuda(), cache, rows=None)
+            cards = actor.pop_context()[:, -1]
+            feats = {k: torch.from_numpy(v[None]).cuda() for k, v in features.items()}
+            logits = actor.policy_logits(hidden, head, feats, None, cards).cpu().numpy()
+            probs = oppo.masked_probabilities(logits, legal[None])[0]
+            assert record.probs.shape == legal.shape
+            np.testing.assert_allclose(record.probs, probs, rtol=0, atol=2e-5)
+            np.testing.assert_allclose(record.value, actor.player_values(hidden).cpu().numpy()[0], rtol=0, atol=2e-4)
+            assert record.action == oppo.sample_rows(record.probs[None], legal[None], np.array([replay.random()]))[0]
+            heads.add(head)
+    assert heads == {"draw", "play"}
