@@ -411,3 +411,14 @@ def test_collector_runs_rummy_candidate_heads():
             assert record.action == oppo.sample_rows(record.probs[None], legal[None], np.array([replay.random()]))[0]
             heads.add(head)
     assert heads == {"draw", "play"}
+
+
+def test_stack_features_pads_the_candidate_axis_with_zeros():
+    """selfplay.py:570-587: each key stacked over decisions, zero-padded to the longest list."""
+
+    a = {"kind": np.array([3, 1]), "cards": np.full((2, 13), 52)}
+    b = {"kind": np.array([5, 6, 2]), "cards": np.arange(39).reshape(3, 13)}
+    stacked = cont.stack_features([a, b])
+    assert stacked["kind"].tolist() == [[3, 1, 0], [5, 6, 2]]
+    assert stacked["cards"].shape == (2, 3, 13) and not stacked["cards"][0, 2].any()
+    assert np.array_equal(stacked["cards"][1], b["cards"]) and stacked["cards"].dtype == b["cards"].dtype
