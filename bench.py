@@ -445,53 +445,48 @@ def run_prefill(args, device, rank: int, world_size: int, actor, cache) -> dict:
 
 
 def run_pointer_wave(args, device, rank: int, world_size: int, kind: str) -> dict:
-    """A decode wave through the one-hot field lookup, Trunk.condition, the ragged trunk and a
+    """A decode wave through the piquet or rummy actor (``piquet.PiquetActor``,
+    ``rummy.RummyActor``; synthetic weights under the reference's parameter names) and a
     pointer head with masked sampling.
 
-    piquet: 8,192 two-player deals (16,384 KV rows, all decoded), lengths U[32, 512], trunk
-      d256/16L/8-2/d_ff 512, piquet field tables (32 fields, 964 rows), one decision per deal
-      scored by CardScorer over its 32 cards.
-    rummy: 8,192 slots, half of them decoded per wave through gathered rows (the continuous
-      collector's form), lengths U[8, 384], 1 in 32 decoded rows a replaced game's first token
-      at position 0, trunk d256/8L/8-2/d_ff 768, one decision per three decoded rows scored by
-      CandidateScorer over U[1, 64] candidates (padded to the wave's max).
-    Each wave runs the embedder's grid over the decoded tokens first (piquet's card grid over the
-    tokens' card codes, rummy's ledger grid over a 52-card ledger) and fuses its summary into the
-    trunk's input; the heads read the readout token's grid cards."""
+    piquet: the 16-layer actor (d256/8-2/d_ff 512), 8,192 two-player deals (16,384 KV rows, all
+      decoded), lengths U[32, 512], one play decision per deal scored by the play CardScorer over
+      the readout token's 32 grid cards.
+    rummy: the base actor (d256/8L/8-2/d_ff 768), 8,192 slots, half of them decoded per wave
+      through gathered rows (the continuous collector's form), lengths U[8, 384], 1 in 32 decoded
+      rows a replaced game's first token at position 0, one play decision per three decoded rows
+      scored by CandidateScorer over U[1, 64] candidates (padded to the wave's max) with the
+      readout token's 52 ledger cards.
+    Each wave runs the actor's grid over the decoded tokens (piquet's card grid, rummy's ledger
+    grid), fuses its summary into the one-hot field lookup of the first trunk layer, decodes, and
+    scores the readouts with the grid cards ``pop_context`` hands back."""
 
     import torch
     import torch.distributed as dist
 
-    from card_playing_gym_b200 import _native as nat
-    from card_playing_gym_b200.config import PIQUET_SCALE, PlumpModelConfig, synthetic_plump_actor_state
-    from card_playing_gym_b200.piquet import FIELD_ROWS, FIELD_VOCAB, CardGrid, CardScorer, PiquetFieldLookup
-    from card_playing_gym_b200.piquet import forward_ragged as piquet_forward
-    from card_playing_gym_b200.rummy import NO_CARD, CandidateScorer
+    from card_playing_gym_b200 import piquet, rummy
     from card_playing_gym_b200.sampling import masked_sample
-    from card_playing_gym_b200.trunk import B200Trunk
 
     rng = np.random.default_rng(3000 + 7919 * rank + (0 if kind == "piquet" else 1))
     gen = torch.Generator(device=device).manual_seed(31 + rank)
     if kind == "piquet":
-        config, slots, decoded, min_len, max_len = PIQUET_SCALE, 16384, 16384, 32, 512
+        config = piquet.PiquetModelConfig()
+        actor = piquet.PiquetActor(config, piquet.synthetic_piquet_actor_state(config, seed=5), device=device)
+        vocab, card_codes, card_slots = piquet.FIELD_VOCAB, 12, 32
+        slots, decoded, min_len, max_len = 16384, 16384, 32, 512
     else:
-        config = PlumpModelConfig(d_model=256, n_layers=8, n_heads=8, n_kv_heads=2, d_ff=768, per_layer_dim=64)
+        config = rummy.RummyModelConfig()
+        actor = rummy.RummyActor(config, rummy.synthetic_rummy_actor_state(config, seed=5), device=device)
+        vocab, card_codes, card_slots = rummy.FIELD_VOCAB, rummy.CARD_VOCAB, 52
         slots, decoded, min_len, max_len = 8192, 4096, 8, 384
-    trunk_cfg = config.trunk()
-    trunk = B200Trunk(trunk_cfg, synthetic_plump_actor_state(config, seed=5), device=device, precision="bf16")
-    d = trunk_cfg.d_model
-    widths = (d, trunk_cfg.ple_width, trunk_cfg.value_width)
-    tables = [torch.randn(FIELD_ROWS, w, device=device, generator=gen) * 0.02 for w in widths]
-    lookup = PiquetFieldLookup(*tables)
-    cache = trunk.new_cache(slots + 1, max_len + 1, torch.float16)
+    cache = actor.new_cache(slots + 1, max_len + 1, torch.float16)
     for pool in (cache.k_pool, cache.v_pool):
         for layer in range(pool.shape[0]):
             pool[layer].normal_(generator=gen)
     lengths = rng.integers(min_len, max_len + 1, slots)
-    tokens = np.zeros((decoded, 1, 64), dtype=np.int16)
-    for field, vocab in enumerate(FIELD_VOCAB):
-        tokens[:, 0, field] = rng.integers(0, vocab, decoded)
-    tokens[:, 0, 32:] = rng.integers(0, 12, (decoded, 32))  # card codes (the piquet card grid's input)
+    fields = np.stack([rng.integers(0, v, decoded) for v in vocab], axis=-1)
+    codes = rng.integers(0, card_codes, (decoded, card_slots))
+    tokens = np.concatenate([fields, codes], axis=-1).astype(np.int16)[:, None, :]
     rows = np.sort(rng.choice(slots, decoded, replace=False)) if decoded < slots else np.arange(slots)
     positions = (lengths[rows] - 1).astype(np.int64)
     if kind == "rummy":
@@ -502,72 +497,30 @@ def run_pointer_wave(args, device, rank: int, world_size: int, kind: str) -> dic
     dev_rows = torch.from_numpy(rows.astype(np.int64)).to(device)
     dev_positions = torch.from_numpy(positions).to(device)
     offsets = torch.zeros(decoded, dtype=torch.int64, device=device)
-    score_state = lambda shapes: {n: rng.standard_normal(s).astype(np.float32) * 0.02 for n, s in shapes.items()}  # noqa: E731
     if kind == "piquet":
-        decisions, cards = decoded // 2, 32
+        decisions, width = decoded // 2, 32
         readout = torch.arange(0, decoded, 2, device=device)
-        scorer = CardScorer(score_state({
-            "query.weight": (64, d), "query.bias": (64,), "card.weight": (64, 32), "card_id.weight": (32, 64),
-            "norm.weight": (64,), "norm.bias": (64,), "hidden.weight": (64, 64), "hidden.bias": (64,),
-            "out.weight": (1, 64), "out.bias": (1,)}), device=device)
-        grid_shapes = {"code.weight": (12, 32), "rank.weight": (8, 32), "norm.weight": (32,),
-                       "summary.weight": (d, 32 * 32)}
-        for b in range(2):
-            grid_shapes.update({f"blocks.{b}.norm.weight": (32,), f"blocks.{b}.along_rank.weight": (64, 32, 3),
-                                f"blocks.{b}.along_rank.bias": (64,), f"blocks.{b}.across_suits.weight": (64, 32),
-                                f"blocks.{b}.out.weight": (32, 64), f"blocks.{b}.out.bias": (32,)})
-        grid_state = score_state(grid_shapes)
-        for name in ("norm.weight", "blocks.0.norm.weight", "blocks.1.norm.weight"):
-            grid_state[name] = np.ones_like(grid_state[name])
-        card_grid = CardGrid(grid_state, device=device)
-        legal = torch.from_numpy(rng.random((decisions, cards)) < 0.4).to(device)
+        legal = torch.from_numpy(rng.random((decisions, width)) < 0.4).to(device)
         legal[:, 0] = True
-        width = cards
-        card_features = {}
-        head = lambda hidden: scorer(hidden, card_features["cards"].index_select(0, readout))  # noqa: E731
+        features = None
     else:
         decisions = decoded // 3
         readout = torch.from_numpy(np.sort(rng.choice(decoded, decisions, replace=False))).to(device)
         counts = rng.integers(1, 65, decisions)
         width = int(counts.max())
-        scorer = CandidateScorer(score_state({
-            "query.weight": (64, d), "query.bias": (64,), "card.weight": (64, 32), "target.weight": (64, 32),
-            "taken.weight": (64, 32), "card_id.weight": (52, 64), "target_id.weight": (52, 64),
-            "taken_id.weight": (52, 64), "kind.weight": (7, 64), "size.weight": (14, 64), "norm.weight": (64,),
-            "norm.bias": (64,), "hidden.weight": (64, 64), "hidden.bias": (64,), "out.weight": (1, 64),
-            "out.bias": (1,)}), device=device)
-        ledger_shapes = {"code.weight": (570, 32), "rank.weight": (13, 32), "norm.weight": (32,),
-                         "summary.weight": (d, 52 * 32)}
-        for b in range(2):
-            ledger_shapes.update({f"blocks.{b}.norm.weight": (32,), f"blocks.{b}.along_rank.weight": (64, 32, 5),
-                                  f"blocks.{b}.along_rank.bias": (64,), f"blocks.{b}.across_suits.weight": (64, 32),
-                                  f"blocks.{b}.out.weight": (32, 64), f"blocks.{b}.out.bias": (32,)})
-        ledger_state = score_state(ledger_shapes)
-        for name in ("norm.weight", "blocks.0.norm.weight", "blocks.1.norm.weight"):
-            ledger_state[name] = np.ones_like(ledger_state[name])
-        card_grid = CardGrid(ledger_state, device=device)
-        ledger = torch.from_numpy(rng.integers(0, 570, (decoded, 1, 52)).astype(np.int16)).to(device)
-        card_features = {}
-        cand_kind = torch.from_numpy(rng.integers(0, 7, (decisions, width))).to(device)
-        cand_cards = np.full((decisions, width, 13), NO_CARD, dtype=np.int64)
+        cand_cards = np.full((decisions, width, 13), rummy.NO_CARD, dtype=np.int64)
         cand_cards[..., :3] = rng.integers(0, 52, (decisions, width, 3))
-        cand_cards[..., 1:3][rng.random((decisions, width)) < 0.7] = NO_CARD
-        cand_target = np.full((decisions, width, 13), NO_CARD, dtype=np.int64)
-        cand_cards, cand_target = torch.from_numpy(cand_cards).to(device), torch.from_numpy(cand_target).to(device)
+        cand_cards[..., 1:3][rng.random((decisions, width)) < 0.7] = rummy.NO_CARD
+        features = {"kind": torch.from_numpy(rng.integers(0, 7, (decisions, width))).to(device),
+                    "cards": torch.from_numpy(cand_cards).to(device),
+                    "target": torch.full((decisions, width, 13), rummy.NO_CARD, dtype=torch.int64, device=device)}
         legal = torch.from_numpy(np.arange(width)[None, :] < counts[:, None]).to(device)
-        head = lambda hidden: scorer(hidden, card_features["cards"].index_select(0, readout), cand_kind,  # noqa: E731
-                                     cand_cards, cand_target)
     uniforms = torch.from_numpy(rng.random(decisions)).to(device)
 
     def step():
-        # The embedder's card grid (piquet) or ledger grid (rummy): every token's card features
-        # and their summary, added to the field sums.
-        with torch.autocast("cuda", dtype=torch.bfloat16):
-            cards_all, summary = card_grid(dev_tokens[:, :, 32:] if kind == "piquet" else ledger)
-        card_features["cards"] = cards_all[:, -1]
-        hidden = piquet_forward(trunk, lookup, dev_tokens, dev_positions, cache, offsets, span=max_len + 1,
-                                rows=dev_rows, summary=summary)
-        logits = head(hidden.index_select(0, readout))
+        hidden = actor.forward_ragged(dev_tokens, dev_positions, cache, offsets, span=max_len + 1, rows=dev_rows)
+        cards = actor.pop_context()[:, 0].index_select(0, readout)  # T = 1: the readout is the only token
+        logits = actor.policy_logits(hidden.index_select(0, readout), "play", features, None, cards)
         return masked_sample(logits, legal, uniforms)
 
     for _ in range(3):
@@ -588,14 +541,15 @@ def run_pointer_wave(args, device, rank: int, world_size: int, kind: str) -> dic
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     desc = {
-        "piquet": (f"piquet decode wave: {decisions} deals ({decoded} KV rows, 1 token/row), lengths U[{min_len},{max_len}],"
-                   " fp16 KV, card grid (2 blocks) + summary, one-hot field lookup (32 fields, 964 rows) fused into the "
-                   "trunk d256/16L/8-2/d_ff 512 -> CardScorer over the readout's 32 card features -> masked sampling"),
-        "rummy": (f"rummy-style continuous wave: {slots} slots, {decoded} gathered rows decoded (1 token/row), lengths "
-                  f"U[{min_len},{max_len}] (1 in 32 a replaced game at position 0), fp16 KV, ledger grid (52 cards, "
-                  "2 blocks) + summary, one-hot field lookup "
-                  f"(piquet's tables standing in for rummy's fields) fused into the trunk d256/8L/8-2/d_ff 768 -> "
-                  f"CandidateScorer over U[1,64] candidates (padded to {width}) -> masked sampling"),
+        "piquet": (f"piquet decode wave through PiquetActor: {decisions} deals ({decoded} KV rows, 1 token/row), "
+                   f"lengths U[{min_len},{max_len}], fp16 KV, card grid (2 blocks) + summary, one-hot field lookup "
+                   "(32 fields, 964 rows) fused into the trunk d256/16L/8-2/d_ff 512 -> play CardScorer over the "
+                   "readout's 32 grid cards -> masked sampling"),
+        "rummy": (f"rummy-style continuous wave through RummyActor: {slots} slots, {decoded} gathered rows decoded "
+                  f"(1 token/row), lengths U[{min_len},{max_len}] (1 in 32 a replaced game at position 0), fp16 KV, "
+                  "ledger grid (52 cards, 2 blocks) + summary, one-hot lookup of rummy's 26 fields (931 rows) fused "
+                  f"into the trunk d256/8L/8-2/d_ff 768 -> CandidateScorer over U[1,64] candidates (padded to {width}) "
+                  "-> masked sampling"),
     }[kind]
     return {"workload": desc, "value": world_size * decisions / (ms / 1000.0), "unit": "decisions/s",
             "rows_per_s": world_size * decoded / (ms / 1000.0), "ms_per_step": ms, "steps": args.pointer_steps}

@@ -396,3 +396,72 @@ class PiquetActor:
 
         inner = torch.nn.functional.gelu(self._project("value_head.0", hidden))
         return self._project("value_head.2", inner)
+
+
+def synthetic_actor_parts(trunk: TrunkConfig, rows: int, seed: int, std: float = 0.02):
+    """(state, normal, gain) for a synthetic actor: the trunk's parameters and the field tables
+    under the reference's names, plus the seeded draw helpers for the rest. Matrices and
+    embeddings are N(0, std), norm gains 1 + N(0, std), biases N(0, std)."""
+
+    import numpy as np
+
+    from .config import PlumpModelConfig, synthetic_plump_actor_state
+
+    plump = PlumpModelConfig(d_model=trunk.d_model, n_layers=trunk.n_layers, n_heads=trunk.n_heads,
+                             n_kv_heads=trunk.n_kv_heads, d_ff=trunk.d_ff, per_layer_dim=trunk.per_layer_dim,
+                             value_embeddings=trunk.value_embeddings)
+    state = {k: v for k, v in synthetic_plump_actor_state(plump, seed=seed, std=std).items() if k.startswith("trunk.")}
+    rng = np.random.default_rng(seed + 1)
+
+    def normal(*shape: int):
+        return (std * rng.standard_normal(shape)).astype(np.float32)
+
+    def gain(n: int):
+        return (1.0 + std * rng.standard_normal(n)).astype(np.float32)
+
+    state["embedding.fields.weight"] = normal(rows, trunk.d_model)
+    if trunk.ple_width:
+        state["embedding.ple_fields.weight"] = normal(rows, trunk.ple_width)
+    if trunk.value_width:
+        state["embedding.value_fields.weight"] = normal(rows, trunk.value_width)
+    return state, normal, gain
+
+
+def synthetic_grid_state(state: dict, normal, gain, *, d: int, codes: int, ranks: int, cards: int, width: int,
+                         hidden: int, blocks: int, kernel: int, prefix: str = "embedding.grid.") -> None:
+    """A card grid's parameters (``CardGrid``, piquet/model.py:180-240) added to ``state``."""
+
+    state[prefix + "code.weight"] = normal(codes, width)
+    state[prefix + "rank.weight"] = normal(ranks, width)
+    for b in range(blocks):
+        p = f"{prefix}blocks.{b}."
+        state[p + "norm.weight"] = gain(width)
+        state[p + "along_rank.weight"] = normal(hidden, width, kernel)
+        state[p + "along_rank.bias"] = normal(hidden)
+        state[p + "across_suits.weight"] = normal(hidden, width)
+        state[p + "out.weight"] = normal(width, hidden)
+        state[p + "out.bias"] = normal(width)
+    state[prefix + "norm.weight"] = gain(width)
+    state[prefix + "summary.weight"] = normal(d, cards * width)
+
+
+def synthetic_piquet_actor_state(config: PiquetModelConfig, seed: int = 0) -> dict:
+    """Seeded float32 weights under the reference ``PiquetActor``'s parameter names and shapes
+    (the heads it rolls out with; the auxiliary head is left out)."""
+
+    trunk = config.trunk()
+    d, s, w = config.d_model, config.score_dim, config.card_width
+    state, normal, gain = synthetic_actor_parts(trunk, FIELD_ROWS, seed)
+    synthetic_grid_state(state, normal, gain, d=d, codes=12, ranks=8, cards=32, width=w, hidden=config.card_hidden,
+                         blocks=config.card_layers, kernel=config.card_kernel)
+    for scorer in ("exchange_scorer.", "play_scorer."):
+        state.update({scorer + "query.weight": normal(s, d), scorer + "query.bias": normal(s),
+                      scorer + "card.weight": normal(s, w), scorer + "card_id.weight": normal(32, s),
+                      scorer + "norm.weight": gain(s), scorer + "norm.bias": normal(s),
+                      scorer + "hidden.weight": normal(s, s), scorer + "hidden.bias": normal(s),
+                      scorer + "out.weight": normal(1, s), scorer + "out.bias": normal(1)})
+    state.update({"stop_head.weight": normal(1, d), "stop_head.bias": normal(1),
+                  "declare_head.weight": normal(2, d), "declare_head.bias": normal(2),
+                  "value_head.0.weight": normal(d, d), "value_head.0.bias": normal(d),
+                  "value_head.2.weight": normal(PLAYERS, d), "value_head.2.bias": normal(PLAYERS)})
+    return state

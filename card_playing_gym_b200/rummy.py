@@ -192,3 +192,27 @@ class RummyActor:
         w0, b0, w2, b2 = self.value
         inner = torch.nn.functional.gelu(torch.nn.functional.linear(hidden.float(), w0, b0))
         return torch.nn.functional.linear(inner, w2, b2)
+
+
+def synthetic_rummy_actor_state(config: RummyModelConfig, seed: int = 0) -> dict:
+    """Seeded float32 weights under the reference ``RummyActor``'s parameter names and shapes
+    (the heads it rolls out with; the belief heads are left out)."""
+
+    from .piquet import synthetic_actor_parts, synthetic_grid_state
+
+    trunk = config.trunk()
+    d, s, w = config.d_model, config.score_dim, config.ledger_width
+    state, normal, gain = synthetic_actor_parts(trunk, sum(FIELD_VOCAB), seed)
+    synthetic_grid_state(state, normal, gain, d=d, codes=CARD_VOCAB, ranks=13, cards=NUM_CARDS, width=w,
+                         hidden=config.ledger_hidden, blocks=config.ledger_layers, kernel=config.ledger_kernel)
+    p = "scorer."
+    state.update({p + "query.weight": normal(s, d), p + "query.bias": normal(s), p + "card.weight": normal(s, w),
+                  p + "target.weight": normal(s, w), p + "taken.weight": normal(s, w),
+                  p + "card_id.weight": normal(NUM_CARDS, s), p + "target_id.weight": normal(NUM_CARDS, s),
+                  p + "taken_id.weight": normal(NUM_CARDS, s), p + "kind.weight": normal(7, s),
+                  p + "size.weight": normal(MAX_MELD_CARDS + 1, s), p + "norm.weight": gain(s),
+                  p + "norm.bias": normal(s), p + "hidden.weight": normal(s, s), p + "hidden.bias": normal(s),
+                  p + "out.weight": normal(1, s), p + "out.bias": normal(1)})
+    state.update({"value_head.0.weight": normal(d, d), "value_head.0.bias": normal(d),
+                  "value_head.2.weight": normal(MAX_PLAYERS, d), "value_head.2.bias": normal(MAX_PLAYERS)})
+    return state

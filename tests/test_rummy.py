@@ -159,3 +159,23 @@ def test_rummy_actor_matches_the_reference_actor(precision, kv, tol):
     assert scaled(actor.player_values(hidden).cpu().numpy(), data["values"]) < tol
     with pytest.raises(ValueError):
         actor.policy_logits(hidden, "play", None, None, context)
+
+
+@pytest.mark.parametrize("name", ("piquet_actor", "rummy_actor"))
+def test_synthetic_actor_states_have_the_reference_names_and_shapes(name):
+    """The bench's synthetic piquet and rummy actor weights carry exactly the reference actors'
+    parameter names and shapes (their fixtures' state dicts), less the heads a rollout never
+    reads (piquet's auxiliary head, rummy's belief heads)."""
+
+    from card_playing_gym_b200 import piquet, rummy
+
+    data = load_golden(name)
+    module = piquet if name == "piquet_actor" else rummy
+    config_cls = piquet.PiquetModelConfig if module is piquet else rummy.RummyModelConfig
+    make = piquet.synthetic_piquet_actor_state if module is piquet else rummy.synthetic_rummy_actor_state
+    config = config_cls(**{str(k): int(v) for k, v in zip(data["config_keys"], data["config_values"])})
+    state = make(config, seed=1)
+    reference = {k[2:]: data[k].shape for k in data if k.startswith("w_")}
+    unused = {k for k in reference if k.split(".")[0] in ("auxiliary_head", "hands_head", "winner_head", "penalty_head")}
+    assert set(state) == set(reference) - unused
+    assert all(tuple(state[k].shape) == tuple(reference[k]) for k in state)
