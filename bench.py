@@ -860,8 +860,10 @@ def run_b200(args) -> int:
     if args.t2_steps > 0:
         pointer_lines["rlv6_t2"] = run_two_token_wave(args, device, rank, world_size, actor, cache, wave, span)
     if args.pointer_steps > 0:
-        pointer_lines["piquet_pointer"] = run_pointer_wave(args, device, rank, world_size, "piquet")
-        pointer_lines["rummy_style"] = run_pointer_wave(args, device, rank, world_size, "rummy")
+        with torch.cuda.nvtx.range("piquet_pointer"):  # lets a profiler select each leg's launches
+            pointer_lines["piquet_pointer"] = run_pointer_wave(args, device, rank, world_size, "piquet")
+        with torch.cuda.nvtx.range("rummy_style"):
+            pointer_lines["rummy_style"] = run_pointer_wave(args, device, rank, world_size, "rummy")
     if args.prefill_steps > 0:  # last: it overwrites the first positions of every cache row
         with torch.cuda.nvtx.range("rlv6_prefill"):  # lets a profiler select this leg's launches
             pointer_lines["rlv6_prefill"] = run_prefill(args, device, rank, world_size, actor, cache)
