@@ -305,6 +305,71 @@ def stack_features(features: list[dict[str, np.ndarray]]) -> dict[str, np.ndarra
     return stacked
 
 
+def launch_decisions(model, hidden: torch.Tensor, context: torch.Tensor | None, states: list[LiveGame],
+                     uniforms: list[float], *, values: bool) -> _Wave:
+    """Score and sample every state's pending decision on the device (selfplay.py:486-567).
+
+    ``hidden`` [N, d] (and ``context`` [N, ...] or None) are the states' readouts in order.
+    Per head group: the candidate features stacked and uploaded (heads that take them), the
+    head's logits, legal-masked softmax and inverse-CDF sampling with the states' uniforms, and
+    the probabilities, actions and (with ``values``) player values copied to pinned host memory.
+    """
+
+    from .sampling import masked_sample
+
+    device = hidden.device
+    groups: dict[str, list[int]] = {}
+    for position, state in enumerate(states):
+        groups.setdefault(state.pending.head, []).append(position)
+    result = _Wave()
+    for head, positions in groups.items():
+        index = _pinned(np.asarray(positions, dtype=np.int64), device)
+        head_hidden = hidden.index_select(0, index)
+        head_context = None if context is None else context.index_select(0, index)
+        decisions = [states[p].pending for p in positions]
+        features = None
+        if decisions[0].features is not None:
+            features = {k: _pinned(v, device) for k, v in stack_features([d.features for d in decisions]).items()}
+        logits = model.policy_logits(head_hidden, head, features, None, head_context).float()
+        width = logits.shape[1]
+        if max(d.legal.shape[0] for d in decisions) > width:
+            raise ValueError(f"head {head!r} scored {width} actions, a decision offers more")
+        legal = np.zeros((len(positions), width), dtype=np.uint8)
+        for row, decision in enumerate(decisions):
+            legal[row, : decision.legal.shape[0]] = decision.legal
+        draws = _pinned(np.asarray([uniforms[p] for p in positions], dtype=np.float64), device)
+        probs, actions = masked_sample(logits, _pinned(legal, device), draws)
+        head_values = model.player_values(head_hidden).float().to("cpu", non_blocking=True) if values else None
+        result.readouts.append(_Readout([states[p] for p in positions], probs.to("cpu", non_blocking=True),
+                                        actions.to("cpu", non_blocking=True), head_values))
+    result.fence = torch.cuda.Event()
+    result.fence.record()
+    return result
+
+
+def record_decisions(wave: _Wave, version: int) -> int:
+    """Hand each state its sampled decision as a ``DecisionRecord`` (selfplay.py:549-566), once
+    the wave's fence has passed; returns the count."""
+
+    count = 0
+    for readout in wave.readouts:
+        probs = readout.probs.numpy()
+        actions = readout.actions.numpy()
+        values = None if readout.values is None else readout.values.numpy()
+        for row, state in enumerate(readout.states):
+            decision = state.pending
+            width = decision.legal.shape[0]
+            state.decisions.append(DecisionRecord(
+                seat=decision.seat, head=decision.head,
+                position=state.offsets[decision.seat] + state.lengths[decision.seat] - 1,
+                action=int(actions[row]), probs=probs[row, :width].astype(np.float32),
+                features=decision.features, version=version,
+                value=None if values is None else values[row].copy()))
+            state.pending = None
+            count += 1
+    return count
+
+
 class EagerWaves(DeviceWaves):
     """The device half for models whose heads take per-decision candidate features (rummy): the
     wave's launches are issued eagerly (continuous.py:333-353), each head group's features are
@@ -318,8 +383,6 @@ class EagerWaves(DeviceWaves):
         self.device = cache.device
 
     def launch(self, wave: PackedWave, readouts: list[tuple[int, LiveGame, float]]) -> _Wave:
-        from .sampling import masked_sample
-
         model = self.model
         tokens, positions, offsets, cache_rows = (
             _pinned(a, self.device) for a in (wave.tokens, wave.positions, wave.offsets, wave.cache_rows))
@@ -327,36 +390,12 @@ class EagerWaves(DeviceWaves):
                                       rows=cache_rows)
         pop = getattr(model, "pop_context", None)
         context = pop() if pop is not None else None
-        groups: dict[str, list[tuple[int, LiveGame, float]]] = {}
-        for entry in readouts:
-            groups.setdefault(entry[1].pending.head, []).append(entry)
-        result = _Wave()
-        for head, group in groups.items():
-            entries = np.fromiter((entry for entry, _, _ in group), dtype=np.int64, count=len(group))
-            index = _pinned(entries, self.device)
-            head_hidden = hidden.index_select(0, index)
-            head_context = None
-            if context is not None:
-                head_context = context[index, _pinned(wave.offsets[entries], self.device)]
-            decisions = [state.pending for _, state, _ in group]
-            features = None
-            if decisions[0].features is not None:
-                features = {k: _pinned(v, self.device) for k, v in stack_features([d.features for d in decisions]).items()}
-            logits = model.policy_logits(head_hidden, head, features, None, head_context).float()
-            width = logits.shape[1]
-            if max(d.legal.shape[0] for d in decisions) > width:
-                raise ValueError(f"head {head!r} scored {width} actions, a decision offers more")
-            legal = np.zeros((len(group), width), dtype=np.uint8)
-            for row, decision in enumerate(decisions):
-                legal[row, : decision.legal.shape[0]] = decision.legal
-            uniforms = _pinned(np.fromiter((u for _, _, u in group), dtype=np.float64, count=len(group)), self.device)
-            probs, actions = masked_sample(logits, _pinned(legal, self.device), uniforms)
-            values = model.player_values(head_hidden).float().to("cpu", non_blocking=True) if self.values else None
-            result.readouts.append(_Readout([state for _, state, _ in group], probs.to("cpu", non_blocking=True),
-                                            actions.to("cpu", non_blocking=True), values))
-        result.fence = torch.cuda.Event()
-        result.fence.record()
-        return result
+        entries = np.fromiter((entry for entry, _, _ in readouts), dtype=np.int64, count=len(readouts))
+        index = _pinned(entries, self.device)
+        if context is not None:
+            context = context[index, _pinned(wave.offsets[entries], self.device)]
+        return launch_decisions(model, hidden.index_select(0, index), context, [state for _, state, _ in readouts],
+                                [u for _, _, u in readouts], values=self.values)
 
 
 class ContinuousCollector:
@@ -580,21 +619,7 @@ class ContinuousCollector:
         t0 = time.perf_counter()
         wave = self._waves[cohort]
         self._waves[cohort] = _Wave()
-        for readout in wave.readouts:
-            probs = readout.probs.numpy()
-            actions = readout.actions.numpy()
-            values = None if readout.values is None else readout.values.numpy()
-            for row, state in enumerate(readout.states):
-                decision = state.pending
-                count = decision.legal.shape[0]
-                state.decisions.append(DecisionRecord(
-                    seat=decision.seat, head=decision.head,
-                    position=state.offsets[decision.seat] + state.lengths[decision.seat] - 1,
-                    action=int(actions[row]), probs=probs[row, :count].astype(np.float32),
-                    features=decision.features, version=version,
-                    value=None if values is None else values[row].copy()))
-                state.pending = None
-                self.stats.decisions += 1
+        self.stats.decisions += record_decisions(wave, version)
         t1 = time.perf_counter()
         for slot in self._slots:
             state = slot.state

@@ -53,6 +53,7 @@ class ScriptedGame:
         self._starts = None
         self.log = []  # (seat, head, legal, context base, stream length)
         self.actions = []
+        self._prefix = self._blocks(1, 3)  # dealt with the game: decision() may come first
 
     def head(self) -> tuple[str, int]:
         return ("bid", BID) if self.turn < 4 else ("play", PLAY)
@@ -68,7 +69,7 @@ class ScriptedGame:
         return blocks
 
     def prefix_tokens(self):
-        return self._blocks(1, 3)
+        return self._prefix
 
     def decision(self):
         seat = self.turn % self.players
@@ -131,8 +132,8 @@ class ScriptedRummy(ScriptedGame):
         return cont.Decision(seat=seat, head=head, legal=legal, features=features)
 
     def __init__(self, *args, **kwargs):
-        super().__init__(*args, **kwargs)
         self.features = []
+        super().__init__(*args, **kwargs)
 
 
 class ScriptedPiquet(ScriptedGame):
