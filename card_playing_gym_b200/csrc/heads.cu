@@ -8,11 +8,12 @@
 // Sampling semantics follow the reference exactly: illegal logits -> -inf, shift by
 // the legal max, exp, illegal -> 0, divide by the sum; draw = #{k : cumsum_k < u},
 // clamped to the last legal index, an illegal draw replaced by the last legal index.
-// exp is evaluated in float64 and rounded once (a correctly rounded float32 exp);
-// the reference's numpy float32 exp carries up to ~2.4 ulp of error, so
-// probabilities agree to a few ulp and draws agree except within a few ulp of a
-// CDF step.
+// The exp is numpy's float32 exp and the sum numpy's pairwise order over the numpy row
+// (numpy_math.cuh), the division and the running cumsum are single float32 roundings and
+// the comparison is in float64, so for the same logits and uniforms the probabilities and
+// the draws are bit-identical to the reference's numpy sampler.
 #include "common.cuh"
+#include "numpy_math.cuh"
 
 namespace cg {
 
@@ -33,17 +34,12 @@ __device__ void warp_sample(const float* logits, const uint8_t* mask, int width,
   peak = warp_max(peak);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) last_legal = max(last_legal, __shfl_xor_sync(0xffffffffu, last_legal, o));
-  float total = 0.f;
-  for (int j = lane; j < width; j += 32) {
-    float e = 0.f;
-    if (mask[j]) e = static_cast<float>(exp(static_cast<double>(logits[j] - peak)));
-    probs_s[j] = e;
-    total += e;
-  }
-  total = warp_sum(total);
+  for (int j = lane; j < width; j += 32) probs_s[j] = mask[j] ? numpy_expf(__fsub_rn(logits[j], peak)) : 0.f;
+  __syncwarp();
+  const float total = numpy_row_sum(probs_s, width);  // the numpy row is the whole width
   __syncwarp();
   for (int j = lane; j < width; j += 32) {
-    const float p = probs_s[j] / total;
+    const float p = __fdiv_rn(probs_s[j], total);
     probs_s[j] = p;
     if (probs_out) probs_out[j] = p;
   }
@@ -52,7 +48,7 @@ __device__ void warp_sample(const float* logits, const uint8_t* mask, int width,
     float cdf = 0.f;
     int below = 0;
     for (int j = 0; j < width; ++j) {
-      cdf += probs_s[j];
+      cdf = __fadd_rn(cdf, probs_s[j]);
       below += static_cast<double>(cdf) < u ? 1 : 0;
     }
     int drawn = last_legal < 0 ? 0 : min(below, last_legal);
@@ -367,16 +363,15 @@ __global__ void __launch_bounds__(kDecThreads, 1) decide_kernel(cg_heads_desc de
     peak = warp_max(peak);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) last_legal = max(last_legal, __shfl_xor_sync(0xffffffffu, last_legal, o));
-    float total = 0.f;
+    for (int a = lane; a < W; a += 32) lp[a] = lm[a] ? numpy_expf(__fsub_rn(lp[a], peak)) : 0.f;
+    __syncwarp();
+    // The reference samples a head's decisions as rows of the head's own width
+    // (selfplay.py:532-545: plump's legal vectors span the whole head), so the sum runs
+    // over A entries in numpy's order; the entries past A are zero.
+    const float total = numpy_row_sum(lp, A);
+    __syncwarp();
     for (int a = lane; a < W; a += 32) {
-      float e = 0.f;
-      if (lm[a]) e = static_cast<float>(exp(static_cast<double>(lp[a] - peak)));
-      lp[a] = e;
-      total += e;
-    }
-    total = warp_sum(total);
-    for (int a = lane; a < W; a += 32) {
-      const float p = lp[a] / total;
+      const float p = __fdiv_rn(lp[a], total);
       lp[a] = p;
       if (probs_out) probs_out[di * W + a] = p;
     }
@@ -398,17 +393,17 @@ __global__ void __launch_bounds__(kDecThreads, 1) decide_kernel(cg_heads_desc de
       bool done = false;
       for (; below + 4 <= W && !done; below += 4) {  // four probabilities read ahead of the sums
         const float p0 = lp[below], p1 = lp[below + 1], p2 = lp[below + 2], p3 = lp[below + 3];
-        cdf += p0;
+        cdf = __fadd_rn(cdf, p0);
         if (!(static_cast<double>(cdf) < u)) { done = true; break; }
-        cdf += p1;
+        cdf = __fadd_rn(cdf, p1);
         if (!(static_cast<double>(cdf) < u)) { below += 1; done = true; break; }
-        cdf += p2;
+        cdf = __fadd_rn(cdf, p2);
         if (!(static_cast<double>(cdf) < u)) { below += 2; done = true; break; }
-        cdf += p3;
+        cdf = __fadd_rn(cdf, p3);
         if (!(static_cast<double>(cdf) < u)) { below += 3; done = true; break; }
       }
       for (; below < W && !done; ++below) {
-        cdf += lp[below];
+        cdf = __fadd_rn(cdf, lp[below]);
         if (!(static_cast<double>(cdf) < u)) break;
       }
       const int last_legal = last_s[i];

@@ -9,10 +9,11 @@ ranks it needs these exchanges per optimizer step, and nothing else:
   definition (mean first, then the centred second moment);
 * the entropy controller's observed per-head entropy (rl/entropy.py:51-69): per head,
   (sum w * H_norm, sum w) summed over ranks;
-* the gradients, SUM-reduced (the decision weights already divide by the global game and
-  seat counts, so per-rank gradients are partial sums of the global objective's gradient).
-  The policy and auxiliary gradient sets are reduced separately because the auxiliary
-  budget (trainer.py:897-937) scales one against the other's global norm.
+* the gradients, SUM-reduced once per optimizer step after its last backward (the decision
+  weights already divide by the global game and seat counts, so per-rank gradients are
+  partial sums of the global objective's gradient). Under the auxiliary budget
+  (trainer.py:897-937) the policy and auxiliary stashes, which both span every actor
+  parameter, are reduced separately, because one is scaled against the other's global norm.
 
 Shards are whole trajectories (GAE segments never cross ranks), contiguous in decision
 order and balanced by decision count. The collectives run on the process group given
@@ -111,86 +112,105 @@ def allreduce_head_entropy(observed: torch.Tensor, group=None) -> torch.Tensor:
 
 # -- gradients ------------------------------------------------------------------------------------
 class GradientAllreduce:
-    """SUM-allreduce of one gradient set in flat buckets, overlapped with backward.
+    """SUM-allreduce of one parameter list's gradients, once per optimizer step, in flat buckets.
 
-    Buckets are filled in reverse registration order (the order backward produces the
-    gradients of a feed-forward stack). A post-accumulate hook marks each parameter ready;
-    when every parameter of a bucket is ready the bucket is flattened and its allreduce is
-    launched asynchronously, so communication runs while backward computes earlier layers.
-    `finish()` waits for every bucket, writes the reduced values back into `.grad` and
-    re-arms for the next backward. Parameters without a gradient after backward are reduced
-    as zeros, so every rank launches the same collectives in the same order.
+    The reference trainer accumulates many backward passes into one optimizer step: one per
+    microbatch of every sequence group (trainer.py:700-731), either into ``.grad`` or, under the
+    auxiliary budget, into two stashes of ``torch.autograd.grad`` results (trainer.py:866-895).
+    The gradients are therefore reduced as they stand after the last of those passes, by an
+    explicit call: ``reduce_grads()`` for ``.grad``, ``reduce_(stash)`` for a stash (a list
+    aligned with ``params``).
+
+    A parameter that no pass reached has no gradient (``None``); what one rank's shard reached
+    another's may not have. One small MAX-allreduce of per-parameter presence flags goes first,
+    so every rank flattens the same parameters into the same buckets: a gradient present on any
+    rank is summed (ranks without one contribute zeros), one present on none stays ``None``
+    (so Adam still skips it, as on one process). Buckets (reverse parameter order, at most
+    ``bucket_bytes``) are all launched asynchronously before the first is waited on, so their
+    transfers overlap each other's flattening and unflattening. Reduced values are written back
+    into the existing gradient tensors, so other references to them see the sums.
     """
 
     def __init__(self, params: Iterable[torch.nn.Parameter], group=None, bucket_bytes: int = 32 << 20):
         self.params = [p for p in params if p.requires_grad]
         self.group = group
-        self.buckets: list[list[torch.nn.Parameter]] = []
-        current: list[torch.nn.Parameter] = []
-        size = 0
-        for p in reversed(self.params):
-            nbytes = p.numel() * p.element_size()
-            if current and size + nbytes > bucket_bytes:
-                self.buckets.append(current)
-                current, size = [], 0
-            current.append(p)
-            size += nbytes
-        if current:
-            self.buckets.append(current)
-        self._bucket_of = {id(p): i for i, bucket in enumerate(self.buckets) for p in bucket}
-        self._pending = [len(bucket) for bucket in self.buckets]
-        self._flat: list[torch.Tensor | None] = [None] * len(self.buckets)
-        self._work: list = [None] * len(self.buckets)
-        self._next = 0  # buckets launch in index order, so every rank issues the same sequence
-        self._hooks = [p.register_post_accumulate_grad_hook(self._ready) for p in self.params]
+        self.bucket_bytes = int(bucket_bytes)
 
     @property
     def world_size(self) -> int:
         return _world(self.group)[1]
 
-    def _ready(self, param: torch.nn.Parameter) -> None:
-        index = self._bucket_of[id(param)]
-        self._pending[index] -= 1
-        while self._next < len(self.buckets) and self._pending[self._next] == 0:
-            self._launch(self._next)
-            self._next += 1
-
-    def _launch(self, index: int) -> None:
-        bucket = self.buckets[index]
-        grads = [p.grad if p.grad is not None else torch.zeros_like(p) for p in bucket]
-        flat = torch.cat([g.reshape(-1) for g in grads])
-        self._flat[index] = flat
+    def _present(self, grads: Sequence[torch.Tensor | None]) -> list[bool]:
+        flags = torch.tensor([g is not None for g in grads], dtype=torch.int32,
+                             device=self.params[0].device if self.params else "cpu")
         if self.world_size > 1:
-            self._work[index] = dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
+            dist.all_reduce(flags, op=dist.ReduceOp.MAX, group=self.group)
+        return [bool(v) for v in flags.tolist()]
 
-    def finish(self) -> None:
-        """Wait for every bucket (launching any not yet launched) and write the sums back."""
+    def _buckets(self, present: list[bool]) -> list[list[int]]:
+        buckets: list[list[int]] = []
+        current: list[int] = []
+        size = 0
+        for index in reversed(range(len(self.params))):
+            if not present[index]:
+                continue
+            p = self.params[index]
+            nbytes = p.numel() * p.element_size()
+            if current and size + nbytes > self.bucket_bytes:
+                buckets.append(current)
+                current, size = [], 0
+            current.append(index)
+            size += nbytes
+        if current:
+            buckets.append(current)
+        return buckets
 
-        while self._next < len(self.buckets):
-            self._launch(self._next)
-            self._next += 1
-        for index, bucket in enumerate(self.buckets):
-            if self._work[index] is not None:
-                self._work[index].wait()
-            flat = self._flat[index]
+    def reduce_(self, grads: Sequence[torch.Tensor | None] | None) -> list[torch.Tensor | None] | None:
+        """Sum ``grads`` (aligned with ``params``; None entries allowed) over the ranks.
+
+        Returns the list of summed gradients: the same tensor objects where this rank had one,
+        new tensors where only other ranks did, None where no rank did. ``None`` in place of the
+        whole list (a stash that received nothing on this rank) is treated as all-None; it comes
+        back as None only if every rank's was empty.
+        """
+
+        empty = grads is None
+        grads = [None] * len(self.params) if grads is None else list(grads)
+        if len(grads) != len(self.params):
+            raise ValueError(f"{len(grads)} gradients for {len(self.params)} parameters")
+        present = self._present(grads)
+        if not any(present):
+            return None if empty else grads
+        if self.world_size == 1:
+            return grads
+        launched = []
+        for bucket in self._buckets(present):
+            parts = [grads[i] if grads[i] is not None else torch.zeros_like(self.params[i]) for i in bucket]
+            flat = torch.cat([part.reshape(-1) for part in parts])
+            work = dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
+            launched.append((bucket, flat, work))
+        for bucket, flat, work in launched:
+            work.wait()
             at = 0
-            for p in bucket:
-                n = p.numel()
-                value = flat[at:at + n].view_as(p)
-                if p.grad is None:
-                    p.grad = value.clone()
+            for index in bucket:
+                p = self.params[index]
+                value = flat[at:at + p.numel()].view_as(p)
+                at += p.numel()
+                if grads[index] is None:
+                    grads[index] = value.clone()
                 else:
-                    p.grad.copy_(value)
-                at += n
-        self._pending = [len(bucket) for bucket in self.buckets]
-        self._flat = [None] * len(self.buckets)
-        self._work = [None] * len(self.buckets)
-        self._next = 0
+                    grads[index].copy_(value)
+        return grads
 
-    def close(self) -> None:
-        for hook in self._hooks:
-            hook.remove()
-        self._hooks = []
+    def reduce_grads(self) -> None:
+        """Sum every parameter's ``.grad`` over the ranks, after the step's last backward."""
+
+        reduced = self.reduce_([p.grad for p in self.params])
+        if reduced is None:
+            return
+        for p, g in zip(self.params, reduced):
+            if p.grad is None and g is not None:
+                p.grad = g
 
 
 def global_grad_norm(params: Iterable[torch.nn.Parameter]) -> torch.Tensor:

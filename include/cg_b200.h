@@ -78,14 +78,17 @@ int cg_decode_attention(const void* q, int q_dtype, const void* k_cache, const v
  * contiguous; the stacked pool is [n_layers, R, KVH, L, D].
  * ------------------------------------------------------------------------------- */
 /* KVCache.write_step (kv_cache.py:84-105): k_new/v_new [B, KVH, T, D] (src_dtype) land on
- * rows[b], positions [B, T] (already clamped by the caller, as the reference does). */
+ * rows[b], positions [B, T] (already clamped by the caller, as the reference does). A row
+ * outside [0, capacity) or a position outside [0, max_len) is skipped on the device and sets
+ * the fault word (0x110, cg_fault_status), where the reference's indexing would raise. */
 int cg_kv_write_step(void* k_layer, void* v_layer, int kv_dtype, int64_t capacity, int kv_heads, int max_len,
                      int head_dim, const int64_t* rows, const int64_t* positions, int64_t batch, int steps,
                      const void* k_new, const void* v_new, int src_dtype, void* stream);
 
 /* KVCache.copy_rows (kv_cache.py:122-138): the first `length` positions of every layer of
  * sources[i] onto targets[i]; overlapping source/target sets are allowed (staged through
- * the workspace, at most cg_kv_copy_rows_workspace_bytes). */
+ * the workspace, at most cg_kv_copy_rows_workspace_bytes). A pair whose source or target
+ * lies outside [0, capacity) is skipped on the device and sets the fault word (0x111). */
 int64_t cg_kv_copy_rows_workspace_bytes(int n_layers, int kv_heads, int max_len, int head_dim, int kv_dtype,
                                         int64_t count);
 int cg_kv_copy_rows(void* k_pool, void* v_pool, int kv_dtype, int n_layers, int64_t capacity, int kv_heads,
@@ -101,8 +104,12 @@ int cg_kv_copy_rows(void* k_pool, void* v_pool, int kv_dtype, int n_layers, int6
  * size, must not exceed cg_kv_copy_rows_noalloc_max_bytes() (16 MiB); larger copies are
  * rejected with CG_ERR_ARGUMENT and should be split into several calls. The buffer is
  * shared by every call in the process on a device: calls whose copies overlap in time on
- * the GPU (on different streams) race with each other. The first call on each device
- * looks up the buffer's device address, so make that first call before any stream capture. */
+ * the GPU (on different streams) race with each other. The buffer's device address is
+ * looked up per device and CUDA context on every call made outside stream capture (so a
+ * cudaDeviceReset or another context is followed); a call inside a capture reuses the
+ * address its context recorded, so make the first call on each device, and the first after
+ * a reset, before any stream capture. Rows or targets outside [0, capacity) are skipped on
+ * the device and set the fault word (0x111, cg_fault_status). */
 int64_t cg_kv_copy_rows_noalloc_max_bytes(void);
 int cg_kv_copy_rows_noalloc(void* k_pool, void* v_pool, int kv_dtype, int n_layers, int64_t capacity, int kv_heads,
                             int max_len, int head_dim, const int64_t* sources, const int64_t* targets, int64_t count,

@@ -62,17 +62,79 @@ def _batch(seed: int = 3):
     return starts, advantages, weights, features, targets
 
 
-def _model(seed: int = 0) -> torch.nn.Module:
+class _Actor(torch.nn.Module):
+    """A trunk, two heads and a parameter no loss reaches: head_b is used only by the first decisions of
+    the batch, which all fall in rank 0's shard, so rank 1 never produces a gradient for it."""
+
+    def __init__(self) -> None:
+        super().__init__()
+        self.trunk = torch.nn.Sequential(torch.nn.Linear(6, 16), torch.nn.GELU(), torch.nn.Linear(16, 16),
+                                         torch.nn.GELU())
+        self.head_a = torch.nn.Linear(16, 1)
+        self.head_b = torch.nn.Linear(16, 1)
+        self.unused = torch.nn.Parameter(torch.zeros(3))
+
+
+HEAD_B_ROWS = 40  # decisions [0, 40) use head_b as well
+
+
+def _model(seed: int = 0) -> _Actor:
     torch.manual_seed(seed)
-    return torch.nn.Sequential(torch.nn.Linear(6, 16), torch.nn.GELU(), torch.nn.Linear(16, 16), torch.nn.GELU(),
-                               torch.nn.Linear(16, 1))
+    return _Actor()
 
 
-def _objective(model, features, targets, weights) -> torch.Tensor:
-    """A weighted-sum objective like the trainer's: weights already divide by the global count."""
+def _losses(model, features, targets, weights, first: int):
+    """(policy, auxiliary) for decisions [first, first + len) of the batch, like the trainer's two halves:
+    weighted sums whose weights already divide by the global count."""
 
-    out = model(torch.from_numpy(features)).squeeze(-1)
-    return (torch.from_numpy(weights).float() * (out - torch.from_numpy(targets)) ** 2).sum()
+    hidden = model.trunk(torch.from_numpy(features))
+    out = model.head_a(hidden).squeeze(-1)
+    index = torch.arange(first, first + len(features))
+    uses_b = index < HEAD_B_ROWS
+    if bool(uses_b.any()):  # head_b only enters the graph of microbatches that use it
+        out = out + uses_b.float() * model.head_b(hidden).squeeze(-1)
+    w = torch.from_numpy(weights).float()
+    policy = (w * (out - torch.from_numpy(targets)) ** 2).sum()
+    auxiliary = (w * hidden.square().mean(-1)).sum()
+    return policy, auxiliary
+
+
+def _objective(model, features, targets, weights, first: int = 0) -> torch.Tensor:
+    policy, auxiliary = _losses(model, features, targets, weights, first)
+    return policy + 0.5 * auxiliary
+
+
+def _stash(stash, gradients):
+    """The reference's _accumulate (trainer.py:206-223): sum autograd.grad results, keeping None."""
+
+    if stash is None:
+        return [None if g is None else g.detach().clone() for g in gradients]
+    for i, g in enumerate(gradients):
+        if g is not None:
+            stash[i] = g.detach().clone() if stash[i] is None else stash[i] + g
+    return stash
+
+
+def _step_gradients(model, features, targets, weights, first: int, micro: int = 3):
+    """One optimizer step's accumulation over `micro` microbatches: .grad from backward (the budget off), and
+    the (policy, auxiliary) stashes from autograd.grad (the budget on)."""
+
+    model.zero_grad(set_to_none=True)
+    params = list(model.parameters())
+    policy_stash = auxiliary_stash = None
+    bounds = np.linspace(0, len(features), micro + 1).astype(int)
+    for a, b in zip(bounds[:-1], bounds[1:]):
+        _objective(model, features[a:b], targets[a:b], weights[a:b], first + a).backward()
+    for a, b in zip(bounds[:-1], bounds[1:]):
+        policy, auxiliary = _losses(model, features[a:b], targets[a:b], weights[a:b], first + a)
+        auxiliary_stash = _stash(auxiliary_stash, torch.autograd.grad(auxiliary, params, retain_graph=True,
+                                                                      allow_unused=True))
+        policy_stash = _stash(policy_stash, torch.autograd.grad(policy, params, allow_unused=True))
+    return policy_stash, auxiliary_stash
+
+
+def _as_numpy(grads):
+    return [None if g is None else g.detach().numpy().copy() for g in grads]
 
 
 def _worker(rank: int, port: int, results) -> None:
@@ -93,17 +155,16 @@ def _worker(rank: int, port: int, results) -> None:
 
         model = _model()
         reducer = GradientAllreduce(model.parameters(), bucket_bytes=256)  # several buckets
-        _objective(model, features[d0:d1], targets[d0:d1], weights[d0:d1]).backward()
-        reducer.finish()
-        grads = [p.grad.clone() for p in model.parameters()]
-        norm = float(global_grad_norm(model.parameters()))
-        # A second backward through the same reducer (re-armed by finish) gives the same sums.
-        model.zero_grad(set_to_none=True)
-        _objective(model, features[d0:d1], targets[d0:d1], weights[d0:d1]).backward()
-        reducer.finish()
-        again = all(torch.equal(a, p.grad) for a, p in zip(grads, model.parameters()))
-        reducer.close()
-        results.put((rank, (g0, g1), mean, std, entropy.tolist(), [g.numpy() for g in grads], norm, again))
+        head_b_local = model.head_b.weight.grad
+        steps = []
+        for _ in range(2):  # two optimizer steps through the same reducer
+            policy, auxiliary = _step_gradients(model, features[d0:d1], targets[d0:d1], weights[d0:d1], d0)
+            head_b_local = model.head_b.weight.grad
+            reducer.reduce_grads()
+            grads = _as_numpy(p.grad for p in model.parameters())
+            norm = float(global_grad_norm(model.parameters()))
+            steps.append((grads, norm, _as_numpy(reducer.reduce_(policy)), _as_numpy(reducer.reduce_(auxiliary))))
+        results.put((rank, (g0, g1), mean, std, entropy.tolist(), steps, head_b_local is None))
     finally:
         dist.destroy_process_group()
 
@@ -168,17 +229,46 @@ def test_head_entropy_is_the_global_weighted_mean(ranks):
         assert head1 == 0.0
 
 
-def test_bucketed_gradient_sum_matches_the_whole_batch(ranks):
+def _whole_batch_step():
     _, _, weights, features, targets = _batch()
     model = _model()
-    _objective(model, features, targets, weights).backward()
-    expected = [p.grad.numpy() for p in model.parameters()]
-    expected_norm = float(global_grad_norm(model.parameters()))
+    policy, auxiliary = _step_gradients(model, features, targets, weights, 0, micro=5)
+    grads = _as_numpy(p.grad for p in model.parameters())
+    return grads, float(global_grad_norm(model.parameters())), _as_numpy(policy), _as_numpy(auxiliary)
+
+
+def _assert_same(got, want):
+    assert len(got) == len(want)
+    for g, w in zip(got, want):
+        assert (g is None) == (w is None)
+        if w is not None:
+            np.testing.assert_allclose(g, w, rtol=1e-5, atol=1e-7)
+
+
+def test_accumulated_gradients_sum_to_the_whole_batch(ranks):
+    """Several backward passes per optimizer step (3 microbatches on each rank, 5 on one process), reduced once
+    after the last: .grad, the policy and auxiliary autograd.grad stashes, and the clip norm all equal one
+    process's accumulation over the whole batch, on both optimizer steps."""
+
+    grads, norm, policy, auxiliary = _whole_batch_step()
     for rank in range(WORLD):
-        for got, want in zip(ranks[rank][4], expected):
-            np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-7)
-        assert ranks[rank][5] == pytest.approx(expected_norm, rel=1e-5)
-        assert ranks[rank][6]  # re-armed reducer reproduces the sums
-    # every rank holds identical reduced gradients
-    for a, b in zip(ranks[0][4], ranks[1][4]):
-        assert np.array_equal(a, b)
+        for step_grads, step_norm, step_policy, step_aux in ranks[rank][4]:
+            _assert_same(step_grads, grads)
+            _assert_same(step_policy, policy)
+            _assert_same(step_aux, auxiliary)
+            assert step_norm == pytest.approx(norm, rel=1e-5)
+    for a, b in zip(ranks[0][4][0][0], ranks[1][4][0][0]):
+        assert (a is None and b is None) or np.array_equal(a, b)
+
+
+def test_gradients_present_on_one_rank_only_are_summed_and_absent_ones_stay_none(ranks):
+    names = [name for name, _ in _model().named_parameters()]
+    unused = names.index("unused")
+    head_b = names.index("head_b.weight")
+    assert ranks[1][5], "rank 1's shard must never reach head_b"
+    assert not ranks[0][5]
+    for rank in range(WORLD):
+        grads, _, policy, auxiliary = ranks[rank][4][0]
+        assert grads[unused] is None and policy[unused] is None and auxiliary[unused] is None
+        assert grads[head_b] is not None and policy[head_b] is not None
+        assert auxiliary[head_b] is None  # the auxiliary loss never reaches head_b on any rank
