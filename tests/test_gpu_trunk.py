@@ -167,11 +167,8 @@ def test_decide_matches_the_oracle_heads_and_sampler(count, gather):
         # The reference samples on the host from these same logits (selfplay.py:539-548).
         mask = legal[rows, :width]
         host = oppo.masked_probabilities(logits[rows, :width], mask)
-        np.testing.assert_allclose(probs[rows, :width], host, rtol=2e-6, atol=1e-12)
-        drawn = oppo.sample_rows(host, mask, uniforms[rows])
-        differ = actions[rows] != drawn
-        near = oppo.boundary_distance(host, uniforms[rows]) < 1e-6
-        assert not (differ & ~near).any()
+        assert np.array_equal(probs[rows, :width].view(np.uint32), host.view(np.uint32))
+        assert np.array_equal(actions[rows], oppo.sample_rows(host, mask, uniforms[rows]))
         assert mask[np.arange(mask.shape[0]), actions[rows]].all()
     np.testing.assert_allclose(values.cpu().numpy(), heads.player_values(h64), atol=2e-5, rtol=1e-5)
 
