@@ -79,6 +79,8 @@ def parse_args(argv=None):
     parser.add_argument("--prefill-steps", type=int, default=10,
                         help="prefills of the rl-v6 new-game leg (every row's prefix from position 0); 0 skips it")
     parser.add_argument("--prefill-tokens", type=int, default=16, help="prefix tokens per row in the prefill leg")
+    parser.add_argument("--reference-cuda-steps", type=int, default=20,
+                        help="waves of each reference-on-this-GPU leg (eager, compiled + graphed); 0 skips them")
     return parser.parse_args(argv)
 
 
@@ -596,8 +598,105 @@ class CpuWave:
         return actions
 
 
+# ---------------------------------------------------------------------------------------------
+# the unmodified reference (baseline/_ref): its own CPU path and its own CUDA paths
+# ---------------------------------------------------------------------------------------------
+REFERENCE_PATH = REPO / "baseline" / "_ref"
+REFERENCE_MODEL_FIELDS = ("max_players", "max_hand_size", "d_model", "n_layers", "n_heads", "n_kv_heads", "d_ff",
+                          "per_layer_dim", "value_embeddings")
+
+
+def reference_import() -> str | None:
+    """Make the reference package in baseline/_ref importable; the reason it is not, or None."""
+
+    if not (REFERENCE_PATH / "cardgym" / "__init__.py").exists():
+        return "the reference package is not installed in baseline/_ref (__graft_entry__.build() places it there)"
+    if str(REFERENCE_PATH) not in sys.path:
+        sys.path.insert(0, str(REFERENCE_PATH))
+    try:
+        import cardgym.games.plump.model  # noqa: F401
+        import cardgym.rl.ppo  # noqa: F401
+    except Exception as exc:  # noqa: BLE001 - reported in the bench line
+        return f"importing the reference failed: {type(exc).__name__}: {exc}"
+    return None
+
+
+def reference_actor(config, state: dict, device):
+    """The reference's own PlumpActor (cardgym/games/plump/model.py) holding the synthetic weights."""
+
+    import torch
+    from cardgym.games.plump.model import PlumpActor as RefActor
+    from cardgym.games.plump.model import PlumpModelConfig as RefConfig
+
+    actor = RefActor(RefConfig(**{k: getattr(config, k) for k in REFERENCE_MODEL_FIELDS}))
+    missing, unexpected = actor.load_state_dict({k: torch.from_numpy(v) for k, v in state.items()}, strict=False)
+    if unexpected:
+        raise RuntimeError(f"synthetic weights the reference actor does not have: {unexpected[:4]}")
+    return actor.to(device).eval()
+
+
+class ReferenceCpuWave:
+    """One rollout wave of the reference's own CPU path on a bounded sample of games: its PlumpActor's
+    forward_ragged (fp32 PyTorch on every host core, fp32 KV pool), the heads, and its numpy
+    masked_probabilities / sample_rows (cardgym/nn/model.py:76-89, cardgym/rl/ppo.py:75-94)."""
+
+    def __init__(self, games: int, min_len: int, max_len: int, seed: int):
+        import torch
+
+        from card_playing_gym_b200.config import RL_V6, synthetic_plump_actor_state
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        self.actor = reference_actor(RL_V6, synthetic_plump_actor_state(RL_V6, seed=0), "cpu")
+        self.wave = synthetic_wave(games, min_len, max_len, seed)
+        self.games = games
+        self.cache = self.actor.new_cache(4 * games, max_len + 1, torch.float32)
+        generator = torch.Generator().manual_seed(seed + 1)
+        for layer in range(len(self.cache.k)):
+            self.cache.k[layer].normal_(generator=generator)
+            self.cache.v[layer].normal_(generator=generator)
+        w = self.wave
+        self.inputs = [torch.from_numpy(w["tokens"].astype(np.int64)), torch.from_numpy(w["positions"]),
+                       torch.from_numpy(w["offsets"])]
+        self.span = max_len + 1
+
+    def step(self) -> np.ndarray:
+        import torch
+        from cardgym.rl.ppo import masked_probabilities, sample_rows
+
+        w = self.wave
+        tokens, positions, offsets = self.inputs
+        with torch.inference_mode():
+            hidden = self.actor.forward_ragged(tokens, positions, self.cache, offsets, span=self.span)
+            readout = hidden[torch.from_numpy(w["readout_rows"])]
+            actions = np.zeros(self.games, dtype=np.int64)
+            for head, (name, width) in enumerate((("bid", 11), ("play", 52))):
+                rows = w["heads"] == head
+                logits = self.actor.policy_logits(readout[torch.from_numpy(rows)], name).float().numpy()
+                mask = w["legal"][rows, :width].astype(bool)
+                probs = masked_probabilities(logits, mask)
+                actions[rows] = sample_rows(probs, mask, w["uniforms"][rows])
+            self.actor.player_values(readout)
+        return actions
+
+
+def cpu_wave(args):
+    """The reference's own CPU wave when baseline/_ref holds it, else the numpy port (oracle/)."""
+
+    reason = reference_import()
+    if reason is None:
+        return ReferenceCpuWave(args.cpu_games, args.min_len, args.max_len, seed=99), "reference", None
+    return CpuWave(args.cpu_games, args.min_len, args.max_len, seed=99), "port", reason
+
+
+def cpu_sample_text(kind: str, games: int) -> str:
+    if kind == "reference":
+        return (f"{games} games ({4 * games} rows) per wave of the same workload through the reference's own "
+                "PlumpActor.forward_ragged + heads (fp32 PyTorch, fp32 KV) and numpy sampler, from baseline/_ref")
+    return f"{games} games ({4 * games} rows) per wave of the same workload, numpy float32 port (oracle/)"
+
+
 def cpu_baseline(args, seconds: float) -> dict:
-    wave = CpuWave(args.cpu_games, args.min_len, args.max_len, seed=99)
+    wave, kind, reason = cpu_wave(args)
     wave.step()  # warm-up
     count, start = 0, time.perf_counter()
     while True:
@@ -606,21 +705,23 @@ def cpu_baseline(args, seconds: float) -> dict:
         elapsed = time.perf_counter() - start
         if elapsed >= seconds or count >= 1000:
             break
-    return {
+    out = {
         "value": count * args.cpu_games / elapsed,
         "unit": UNIT,
         "cores": os.cpu_count(),
-        "kind": "port",
-        "sample": (f"{count} waves of {args.cpu_games} games ({4 * args.cpu_games} rows) of the same workload, "
-                   f"numpy float32 port (oracle/), {elapsed:.1f} s"),
+        "kind": kind,
+        "sample": f"{count} waves: " + cpu_sample_text(kind, args.cpu_games) + f", {elapsed:.1f} s",
     }
+    if reason:
+        out["reference_unavailable"] = reason
+    return out
 
 
 def run_reference(args) -> int:
     rank, world_size, _ = world()
     if rank != 0:
         return 0
-    wave = CpuWave(args.cpu_games, args.min_len, args.max_len, seed=99)
+    wave, kind, reason = cpu_wave(args)
     for _ in range(max(args.warmup, 1)):
         wave.step()
     start = time.perf_counter()
@@ -628,17 +729,214 @@ def run_reference(args) -> int:
         wave.step()
     elapsed = time.perf_counter() - start
     value = args.steps * args.cpu_games / elapsed
-    sample = f"{args.cpu_games} games ({4 * args.cpu_games} rows) per step, numpy float32 port of the reference path"
+    sample = cpu_sample_text(kind, args.cpu_games)
+    if reason:
+        sample += f" (the reference itself: {reason})"
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world_size,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * elapsed / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": workload_name(args), "cpu_sample_games": args.cpu_games},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": os.cpu_count(), "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": os.cpu_count(), "kind": kind, "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+def _cuda_ms(step, steps: int, device) -> float:
+    """Mean device milliseconds of `step` over `steps` calls (CUDA events on the current stream)."""
+
+    import torch
+
+    stream = torch.cuda.current_stream(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    start.record(stream)
+    for _ in range(steps):
+        step()
+    end.record(stream)
+    torch.cuda.synchronize(device)
+    return start.elapsed_time(end) / steps
+
+
+class ReferenceCudaWave:
+    """The rl-v6 bench wave (same games, lengths, tokens, fp16 KV pool of random contents) through the
+    reference's own PlumpActor on this GPU, as its batch collector runs it: bf16 autocast around
+    forward_ragged, the readouts gathered, each head's logits and the values in fp32 on their way to
+    pinned host memory (cardgym/rl/selfplay.py:406-454, 486-530). Host sampling is not timed."""
+
+    def __init__(self, args, device):
+        import torch
+
+        from card_playing_gym_b200.config import RL_V6, synthetic_plump_actor_state
+
+        self.device = device
+        self.actor = reference_actor(RL_V6, synthetic_plump_actor_state(RL_V6, seed=0), device)
+        wave = synthetic_wave(args.games, args.min_len, args.max_len, seed=1000)
+        self.games = args.games
+        self.span = args.max_len + 1
+        self.cache = self.actor.new_cache(4 * args.games + 1, self.span, torch.float16)
+        generator = torch.Generator(device=device).manual_seed(17)
+        for layer in range(len(self.cache.k)):
+            self.cache.k[layer].normal_(generator=generator)
+            self.cache.v[layer].normal_(generator=generator)
+        self.tokens = torch.from_numpy(wave["tokens"].astype(np.int64)).to(device)
+        self.positions = torch.from_numpy(wave["positions"]).to(device)
+        self.offsets = torch.from_numpy(wave["offsets"]).to(device)
+        self.readout = torch.from_numpy(wave["readout_rows"]).to(device)
+        self.groups = [(name, torch.from_numpy(np.flatnonzero(wave["heads"] == head)).to(device))
+                       for head, name in enumerate(("bid", "play"))]
+
+    def heads(self, hidden):
+        readout = hidden.index_select(0, self.readout)
+        outputs = [self.actor.policy_logits(readout.index_select(0, rows), name) for name, rows in self.groups]
+        outputs.append(self.actor.player_values(readout))
+        return [output.float() for output in outputs]
+
+    def eager_step(self):
+        import torch
+
+        with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
+            hidden = self.actor.forward_ragged(self.tokens, self.positions, self.cache, self.offsets, span=self.span)
+            return [output.to("cpu", non_blocking=True) for output in self.heads(hidden)]
+
+    def graphed_step(self):
+        """torch.compile + one CUDA graph, as the reference's DecodeGraphs builds it (cardgym/rl/graphs.py:66-151):
+        the body compiled by cardgym.nn.compile.compiled, warmed up on a side stream, captured, replayed. The plump
+        embedder's nonzero() cannot be captured (a data-dependent shape with a host sync), so the raw field lookup
+        runs once beforehand and the graph holds Trunk.condition, the 16-layer forward_ragged and the heads."""
+
+        import torch
+        from cardgym.nn.compile import compiled
+
+        with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16, cache_enabled=False):
+            lookups = [t if t is None else t.clone() for t in self.actor.embed(self.tokens)]
+
+        def outputs(x, ple, values):
+            # DecodeGraphs._outputs (graphs.py:88-102): every head on every readout, then the values.
+            with torch.autocast("cuda", dtype=torch.bfloat16, cache_enabled=False):
+                conditioned = self.actor.trunk.condition(x, ple, values)
+                hidden = self.actor.trunk.forward_ragged(*conditioned, self.cache, self.positions, self.offsets,
+                                                         self.span, None)
+                readout = hidden.index_select(0, self.readout)
+                heads = [self.actor.policy_logits(readout, name) for name, _ in self.groups]
+                return torch.cat([o.float() for o in (*heads, self.actor.player_values(readout))], dim=-1)
+
+        body = compiled(outputs, self.device)
+        stream = torch.cuda.current_stream(self.device)
+        with torch.inference_mode():
+            side = torch.cuda.Stream(self.device)
+            side.wait_stream(stream)
+            with torch.cuda.stream(side):
+                body(*lookups)
+                body(*lookups)
+            stream.wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                output = body(*lookups)
+        host = torch.empty(output.shape, dtype=output.dtype).pin_memory()
+
+        def step():
+            graph.replay()
+            host.copy_(output, non_blocking=True)
+
+        return step, graph
+
+
+def run_reference_k1(device, steps: int = 2000) -> dict:
+    """The reference's one CUDA kernel (cardgym/nn/cuda_decode.py:46-151, JIT-built by its own load_inline) against
+    this repo's decode attention at the kernel's own envelope: head_dim 32, spans <= 64, fp16, 384 rows x 3 tokens
+    (the shape its docstring times, cuda_decode.py:5-9)."""
+
+    import torch
+    from cardgym.nn import cuda_decode as k1
+
+    from card_playing_gym_b200.cuda_decode import decode_attention
+
+    generator = torch.Generator(device=device).manual_seed(3)
+    batch, heads, kv_heads, dim, tokens, span = 384, 8, 2, 32, 3, 64
+    q = torch.randn((batch, heads, tokens, dim), device=device, generator=generator).half()
+    k = torch.randn((batch, kv_heads, span, dim), device=device, generator=generator).half()
+    v = torch.randn((batch, kv_heads, span, dim), device=device, generator=generator).half()
+    rows = torch.arange(batch, device=device)
+    lengths = torch.randint(1, span - tokens + 2, (batch,), device=device, generator=generator)
+    scale = dim ** -0.5
+    theirs = k1.decode_attention(q, k, v, rows, lengths, span, scale)
+    ours = decode_attention(q, k, v, rows, lengths, span, scale)
+    difference = float((theirs.float() - ours.float()).abs().max())
+    # Each op is called `per_graph` times inside one CUDA graph, so the device time is measured and not the
+    # host's launch rate (a Python custom-op call costs more host time than either kernel takes).
+    per_graph = 100
+
+    def graphed(op):
+        stream = torch.cuda.current_stream(device)
+        side = torch.cuda.Stream(device)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                op(q, k, v, rows, lengths, span, scale)
+        stream.wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(per_graph):
+                op(q, k, v, rows, lengths, span, scale)
+        graph.replay()
+        return graph
+
+    k1_graph, ours_graph = graphed(k1.decode_attention), graphed(decode_attention)
+    replays = max(1, steps // per_graph)
+    k1_ms = _cuda_ms(k1_graph.replay, replays, device) / per_graph
+    ours_ms = _cuda_ms(ours_graph.replay, replays, device) / per_graph
+    del k1_graph, ours_graph
+    return {"shape": "384 rows x 3 tokens, 8 query / 2 KV heads of 32, spans <= 64, fp16 (L2-resident)",
+            "reference_us": 1000 * k1_ms, "b200_us": 1000 * ours_ms, "speedup": k1_ms / ours_ms,
+            "max_abs_difference": difference, "calls": replays * per_graph,
+            "timing": f"CUDA events around graph replays of {per_graph} back-to-back calls per op"}
+
+
+def run_reference_cuda(args, device) -> dict:
+    """The unmodified reference on this GPU at the rl-v6 bench config: eager, torch.compile + CUDA graph, and K1."""
+
+    reason = reference_import()
+    if reason is not None:
+        return {"unavailable": reason}
+    import torch
+
+    out: dict = {"source": "baseline/_ref (the reference package, unmodified)"}
+    steps = args.reference_cuda_steps
+    try:
+        wave = ReferenceCudaWave(args, device)
+        for _ in range(3):
+            wave.eager_step()
+        ms = _cuda_ms(wave.eager_step, steps, device)
+        out["eager"] = {"value": args.games / (ms / 1000.0), "unit": UNIT, "ms_per_step": ms, "steps": steps,
+                        "path": "SequenceModel.forward_ragged under bf16 autocast + heads, eager (how plump rolls out)"}
+    except Exception as exc:  # noqa: BLE001 - reported in the bench line
+        out["eager"] = {"unavailable": f"{type(exc).__name__}: {exc}"[:400]}
+        wave = None
+    if wave is not None:
+        started = time.perf_counter()
+        try:
+            step, graph = wave.graphed_step()
+            compile_s = time.perf_counter() - started
+            for _ in range(3):
+                step()
+            ms = _cuda_ms(step, steps, device)
+            out["compiled_graph"] = {"value": args.games / (ms / 1000.0), "unit": UNIT, "ms_per_step": ms,
+                                     "steps": steps, "compile_and_capture_s": compile_s,
+                                     "path": "cardgym.nn.compile.compiled body (Trunk.condition + forward_ragged "
+                                             "+ heads) captured in one CUDA graph; the field lookup precomputed"}
+            del graph
+        except Exception as exc:  # noqa: BLE001
+            out["compiled_graph"] = {"unavailable": f"{type(exc).__name__}: {exc}"[:400]}
+        del wave
+        torch.cuda.empty_cache()
+    try:
+        out["k1"] = run_reference_k1(device)
+    except Exception as exc:  # noqa: BLE001
+        out["k1"] = {"unavailable": f"{type(exc).__name__}: {exc}"[:400]}
+    return out
 
 
 # ---------------------------------------------------------------------------------------------
@@ -864,6 +1162,10 @@ def run_b200(args) -> int:
             pointer_lines["piquet_pointer"] = run_pointer_wave(args, device, rank, world_size, "piquet")
         with torch.cuda.nvtx.range("rummy_style"):
             pointer_lines["rummy_style"] = run_pointer_wave(args, device, rank, world_size, "rummy")
+    reference_cuda = None
+    if args.reference_cuda_steps > 0 and world_size == 1:
+        with torch.cuda.nvtx.range("reference_cuda"):
+            reference_cuda = run_reference_cuda(args, device)
     if args.prefill_steps > 0:  # last: it overwrites the first positions of every cache row
         with torch.cuda.nvtx.range("rlv6_prefill"):  # lets a profiler select this leg's launches
             pointer_lines["rlv6_prefill"] = run_prefill(args, device, rank, world_size, actor, cache)
@@ -925,6 +1227,13 @@ def run_b200(args) -> int:
         if piquet_line is not None:
             line["piquet_scale"] = piquet_line
         line.update(pointer_lines)
+        if reference_cuda is not None:
+            line["reference_cuda"] = reference_cuda
+            for key in ("eager", "compiled_graph"):
+                base = reference_cuda.get(key, {}).get("value")
+                if base:
+                    reference_cuda[key]["b200_speedup"] = value / base
+                    reference_cuda[key]["b200_e2e_speedup"] = e2e_value / base
         if world_size == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args, args.cpu_seconds)
         print(json.dumps(line), flush=True)
