@@ -20,6 +20,7 @@ import pytest
 import torch
 
 from card_playing_gym_b200 import continuous as cont
+from card_playing_gym_b200 import rollout
 from oracle import continuous as ocont
 from oracle import ppo as oppo
 from tests.conftest import load_golden
@@ -164,9 +165,9 @@ class _FakeModel:
         return _FakeCache(rows, length)
 
 
-class FakeWaves:
-    """The device half's contract, on the host: uniform probabilities over the legal actions,
-    the oracle's inverse CDF. Checks every wave's rows against the KV lengths it has seen."""
+class FakeHalf:
+    """The device half's contract, on the host: uniform probabilities over the legal actions, the oracle's
+    inverse CDF. Checks every wave's entries against the KV lengths it has seen."""
 
     def __init__(self, cache):
         self.cache = cache
@@ -184,24 +185,20 @@ class FakeWaves:
             assert position in (0, self.lengths[row]), (row, position, self.lengths[row])
             self.lengths[row] = position + int(wave.offsets[index]) + 1
             assert self.lengths[row] < self.cache.length
-        result = cont._Wave()
+        result = cont.WaveInFlight()
         groups = {}
-        for entry, state, uniform in readouts:
-            groups.setdefault(state.pending.head, []).append((entry, state, uniform))
+        for entry, trace, uniform in readouts:
+            groups.setdefault(trace.pending.head, []).append((trace, uniform))
         for head, group in groups.items():
-            width = BID if head == "bid" else PLAY
+            width = max(trace.pending.legal.shape[0] for trace, _ in group)
             mask = np.zeros((len(group), width), dtype=bool)
-            for row, (_, state, _) in enumerate(group):
-                mask[row, : state.pending.legal.shape[0]] = state.pending.legal
+            for row, (trace, _) in enumerate(group):
+                mask[row, : trace.pending.legal.shape[0]] = trace.pending.legal
             probs = oppo.masked_probabilities(np.zeros(mask.shape, np.float32), mask)
-            actions = oppo.sample_rows(probs, mask, np.array([u for _, _, u in group]))
-            result.readouts.append(cont._Readout([state for _, state, _ in group], torch.from_numpy(probs),
-                                                 torch.from_numpy(actions.astype(np.int64)), None))
+            actions = oppo.sample_rows(probs, mask, np.array([u for _, u in group]))
+            result.groups.append(rollout.SampledGroup([trace for trace, _ in group], torch.from_numpy(probs),
+                                                      torch.from_numpy(actions.astype(np.int64)), None))
         return result
-
-    @staticmethod
-    def wait(wave):
-        pass
 
 
 def test_pack_wave_matches_the_reference_packing():
@@ -233,16 +230,23 @@ def test_split_lanes_shares_quota_and_games():
         cont.split_lanes([replace(lanes[0], quota=None)], 0, 2)
 
 
-def test_restart_contexts_drops_cached_lengths():
+def test_context_restart_rewrites_the_row_from_position_zero():
+    """selfplay.py:172-190: a restarted observer's row length drops to zero, the stream tokens before the new
+    context move into its shift, and only the block's tail from the start index is decoded."""
+
     class Game:
+        num_players = 2
+
         def context_starts(self):
             return [None, 1]
 
-    state = cont.LiveGame(game=Game(), base=0, lengths=[5, 7], blocks=[[], []])
+    table = rollout.RowTable(4)
+    table.cached[2:4] = [5, 7]
+    trace = rollout.GameTrace(Game(), base=2)
     blocks = [np.zeros((2, 3)), np.arange(9).reshape(3, 3)]
-    decoded = cont.restart_contexts(state, blocks)
-    assert decoded[0] is blocks[0] and np.array_equal(decoded[1], blocks[1][1:])
-    assert state.lengths == [5, 0] and state.offsets == [0, 8]
+    rollout.queue_after_step(trace, table, blocks)
+    assert trace.queue[0][1] is blocks[0] and np.array_equal(trace.queue[1][1], blocks[1][1:])
+    assert table.cached[2:4].tolist() == [5, 0] and table.shift[2:4].tolist() == [0, 8]
 
 
 @pytest.mark.parametrize("cohorts", (1, 2))
@@ -260,7 +264,7 @@ def test_collector_host_logic(cohorts):
     fakes = []
     collector = cont.ContinuousCollector(
         _FakeModel(), device="cpu", max_length=64, cohorts=cohorts,
-        waves_factory=lambda cache: fakes.append(FakeWaves(cache)) or fakes[-1])
+        half_factory=lambda cache, values: fakes.append(FakeHalf(cache)) or fakes[-1])
     rng = random.Random(1)
     first = collector.collect(lanes, rng, version=0)
     assert len(first) == 50 and collector.in_flight > 0
@@ -391,8 +395,8 @@ def test_collector_runs_rummy_candidate_heads():
 
     lanes = [cont.Lane("rummy", 3, 16, 24, deal=deal)]
     collector = cont.ContinuousCollector(actor, max_length=48, cohorts=2, kv_dtype="fp32", record_values=True)
-    assert isinstance(collector._waves_factory(actor.new_cache(1, 2, torch.float32)), cont.EagerWaves)
     results = collector.collect(lanes, random.Random(13))
+    assert isinstance(collector.engine.half, cont.EagerHalf)
     assert len(results) == 24
     cache = actor.new_cache(1, 48, torch.float32)
     heads = set()
