@@ -136,6 +136,8 @@ _SIGNATURES: dict[str, tuple[type, list]] = {
     "cg_ppo_objective": (_i32, [_p, _p, _i64, _i32, _i64, _p, _p, _p, _f32, _f32, _p, _p, _p, _p, _i64, _p]),
     "cg_value_loss_workspace_bytes": (_i64, [_i64]),
     "cg_value_loss": (_i32, [_p, _p, _p, _p, _i64, _i32, _f32, _p, _p, _p, _i64, _p]),
+    "cg_seat_values": (_i32, [_p, _i64, _i32, _p, _p, _p, _p, _i64, _i32, _p, _p, _p]),
+    "cg_center_zero_sum": (_i32, [_p, _p, _i64, _i32, _p, _p]),
 }
 
 

@@ -24,6 +24,7 @@ from __future__ import annotations
 
 from collections.abc import Callable, Iterable, Sequence
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
@@ -62,6 +63,24 @@ def shard_games(starts: Sequence[int] | torch.Tensor, world_size: int, rank: int
         return int(torch.searchsorted(bounds[:-1], torch.tensor(target), right=False))
 
     return edge(rank), edge(rank + 1)
+
+
+def rescale_batch_weights(batch, local_games: int, global_games: int) -> None:
+    """Give a rank's batch the global decision weights, in place.
+
+    The reference's batch builder weighs every decision row and dense position by 1 / G of the
+    games it was given (cardgym/rl/batch.py:147-178). A rank built from its shard of G_r of the G
+    games scales them by G_r / G, so that the ranks' weights (and their SUM-reduced gradients) are
+    the whole batch's.
+    """
+
+    if local_games == global_games:
+        return
+    scale = np.float32(local_games / global_games)
+    for rows in batch.decisions.values():
+        rows.weight *= scale
+    for group in [*batch.actor_groups, *batch.critic_groups]:
+        group.position_weight *= scale
 
 
 # -- batch-global statistics ---------------------------------------------------------------------

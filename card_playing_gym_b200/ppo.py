@@ -231,6 +231,40 @@ def value_loss(prediction: torch.Tensor, players: torch.Tensor, targets: torch.T
     return _ValueLoss.apply(prediction, targets, players, weights, float(reward_scale))
 
 
+# -- baseline seat values -------------------------------------------------------------------------
+def seat_values(values: torch.Tensor, shift: torch.Tensor, players: torch.Tensor, seat: torch.Tensor,
+                flat: torch.Tensor | None = None, *, center: bool = False) -> tuple[torch.Tensor, torch.Tensor]:
+    """Each decision's per-seat state values and its prediction (trainer.py:556-571, 610-632).
+
+    values fp32 [M, P]; decision i reads row ``flat[i]`` (or i). Absolute seat s is column
+    ``(s - shift[i]) mod players[i]``; seats past ``players[i]`` are zero. ``center=False``: the values
+    are already zero-sum centred and the prediction is the acting seat's entry; ``center=True``: raw
+    recorded values, centred over the active seats in float64, prediction = centred column 0.
+    Returns (state f64 [N, P], prediction f64 [N]).
+    """
+
+    values = values.float().contiguous()
+    count = shift.shape[0]
+    seats = values.shape[1]
+    state = torch.empty((count, seats), dtype=torch.float64, device=values.device)
+    prediction = torch.empty(count, dtype=torch.float64, device=values.device)
+    as64 = lambda t: t.to(device=values.device, dtype=torch.int64).contiguous()  # noqa: E731
+    nat.call("cg_seat_values", nat.ptr(values), values.shape[0], seats, nat.ptr(None if flat is None else as64(flat)),
+             nat.ptr(as64(shift)), nat.ptr(as64(players)), nat.ptr(as64(seat)), count, 1 if center else 0,
+             nat.ptr(state), nat.ptr(prediction), nat.stream_handle(values.device))
+    return state, prediction
+
+
+def center_zero_sum(values: torch.Tensor, num_players: torch.Tensor) -> torch.Tensor:
+    """Projection onto the active seats' zero-sum subspace, padded seats zero (ppo.py:97-108); fp32."""
+
+    values = values.float().contiguous()
+    out = torch.empty_like(values)
+    nat.call("cg_center_zero_sum", nat.ptr(values), nat.ptr(num_players.to(torch.int64).contiguous()),
+             values.shape[0], values.shape[1], nat.ptr(out), nat.stream_handle(values.device))
+    return out
+
+
 # -- one captured step ------------------------------------------------------------------------
 class GraphedStep:
     """A fixed-shape step captured once as a CUDA graph and replayed (the update's advantage +

@@ -376,6 +376,22 @@ int cg_value_loss(const float* prediction, const float* targets, const int32_t* 
                   int64_t rows, int players_max, float reward_scale, float* grad, double* totals, void* workspace,
                   int64_t workspace_bytes, void* stream);
 
+/* The PPO baseline's seat values (PPOTrainer._baseline / _recorded_values, trainer.py:556-571,
+ * 610-632): decision i reads row flat[i] (or i when flat is NULL) of values fp32 [value_rows,
+ * seats]; absolute seat s takes column (s - shift[i]) mod players[i], seats >= players[i] zero.
+ * center = 0: values already zero-sum centred (the critic's pending values), prediction = the
+ * acting seat's (seat[i]) entry. center = 1: raw recorded values, centred over the active seats
+ * in float64 first (the reference's numpy arithmetic), prediction = the centred column 0.
+ * state_out f64 [n, seats] and prediction_out f64 [n] (either may be NULL). A row or player
+ * count out of range zeroes that decision and sets the fault word (0x400 / 0x401). */
+int cg_seat_values(const float* values, int64_t value_rows, int seats, const int64_t* flat, const int64_t* shift,
+                   const int64_t* players, const int64_t* seat, int64_t n, int center, double* state_out,
+                   double* prediction_out, void* stream);
+
+/* center_zero_sum (cardgym/rl/ppo.py:97-108): fp32 [n, seats] minus the mean over each row's
+ * first players[i] seats, padded seats zero. */
+int cg_center_zero_sum(const float* values, const int64_t* players, int64_t n, int seats, float* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -198,3 +198,29 @@ def value_loss(prediction, players, targets, weights, reward_scale: float):
     g = (w / n)[:, None] * error / reward_scale * active  # d loss / d centered
     grad = active * (g - (g * active).sum(-1, keepdims=True) / n[:, None])
     return loss, squared, grad
+
+
+def seat_values(values: np.ndarray, shift: np.ndarray, players: np.ndarray, seat: np.ndarray,
+                center: bool = False) -> tuple[np.ndarray, np.ndarray]:
+    """Per-decision seat values and the prediction, as PPOTrainer._baseline / _recorded_values compute them.
+
+    center=False (trainer.py:556-571): the stream's values [N, P] (already zero-sum centred float32), absolute
+    seat i read from column (i - shift) mod players, inactive seats zero; prediction = the acting seat's entry.
+    center=True (trainer.py:610-632): recorded raw values centred over the active seats in float64, state
+    columns (i - shift) mod players of the centred row, prediction = centred column 0.
+    Returns float64 (state [N, P], prediction [N]).
+    """
+
+    values = np.asarray(values)
+    players = np.asarray(players, np.int64)
+    count = values.shape[1]
+    seats = np.arange(count)[None, :]
+    active = seats < players[:, None]
+    columns = (seats - np.asarray(shift, np.int64)[:, None]) % players[:, None]
+    if center:
+        raw = values.astype(np.float64) * active
+        centred = (raw - raw.sum(-1, keepdims=True) / players[:, None]) * active
+        state = np.take_along_axis(centred, columns, axis=1) * active
+        return state, centred[:, 0]
+    state = (np.take_along_axis(values, columns, axis=1) * active).astype(np.float64)
+    return state, state[np.arange(len(state)), np.asarray(seat, np.int64)]

@@ -392,6 +392,44 @@ def test_value_loss_matches_the_reference_autograd():
     np.testing.assert_allclose(prediction.grad.cpu().numpy(), data["grad"], rtol=1e-4, atol=1e-9)
 
 
+@pytest.mark.parametrize("center", (False, True))
+def test_seat_values_match_the_reference_baseline(center):
+    """The baseline's seat gather (trainer.py:556-571) and the recorded values' centring (trainer.py:610-632),
+    bit-exact with the reference's numpy arithmetic; rows read through an index, 3 to 7 players of 7 seats."""
+
+    from card_playing_gym_b200.ppo import seat_values
+
+    rng = np.random.default_rng(31 + center)
+    n, seats, source_rows = 5000, 7, 6000
+    values = rng.standard_normal((source_rows, seats)).astype(np.float32)
+    flat = rng.integers(0, source_rows, n)
+    players = rng.integers(3, 8, n)
+    shift = rng.integers(0, 7, n)
+    seat = (rng.random(n) * players).astype(np.int64)
+    picked = values[flat]
+    if not center:
+        picked = oppo.center_zero_sum(picked.astype(np.float64), players).astype(np.float32)
+        values = values.copy()
+        values[flat] = picked
+    cuda = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    state, prediction = seat_values(cuda(values), cuda(shift), cuda(players), cuda(seat), cuda(flat), center=center)
+    want_state, want_prediction = oppo.seat_values(values[flat], shift, players, seat, center=center)
+    assert np.array_equal(state.cpu().numpy(), want_state)
+    assert np.array_equal(prediction.cpu().numpy(), want_prediction)
+
+
+def test_center_zero_sum_matches_the_oracle():
+    from card_playing_gym_b200.ppo import center_zero_sum
+
+    rng = np.random.default_rng(37)
+    values = rng.standard_normal((4099, 5)).astype(np.float32)
+    players = rng.integers(2, 6, 4099)
+    got = center_zero_sum(torch.from_numpy(values).cuda(), torch.from_numpy(players).cuda()).cpu().numpy()
+    want = oppo.center_zero_sum(values.astype(np.float64), players)
+    np.testing.assert_allclose(got, want, rtol=0, atol=2e-6)
+    assert (got[np.arange(5)[None, :] >= players[:, None]] == 0).all()
+
+
 def test_no_kernel_fault_was_recorded():
     from card_playing_gym_b200 import _native as nat
 
