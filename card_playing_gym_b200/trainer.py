@@ -83,9 +83,15 @@ def device_trainer(base: type) -> type:
 
             reference._reduce = reduce_over_ranks
             try:
-                return super().update(batch, iteration)
+                stats = super().update(batch, iteration)
             finally:
                 reference._reduce = local_reduce
+            # The batch sizes the update reports are counted from each rank's shard.
+            counts = [key for key in ("policy_rows", "positions") if key in stats]
+            summed = allreduce_sums(torch.tensor([stats[key] for key in counts], dtype=torch.float64,
+                                                 device=self.device), group)
+            stats.update(zip(counts, summed.tolist()))
+            return stats
 
         # -- gradients: summed over the ranks once the step's last backward is done ----------------
         def _unscale(self, parameters, *stashes):

@@ -41,12 +41,12 @@ def _reference():
     return loop, setup, trainer
 
 
-def _trainer(cls, actor, critic, components, device):
+def _trainer(cls, actor, critic, components, device, **extra):
     config = components.config
     game = config.game
     return cls(copy.deepcopy(actor), copy.deepcopy(critic), config.ppo, game.hooks(device, config.run.precision),
                device=device, precision=config.run.precision, policy_heads=game.policy_heads,
-               max_players=game.max_players)
+               max_players=game.max_players, **extra)
 
 
 def _relative(a: float, b: float) -> float:
@@ -110,3 +110,96 @@ def test_smoke_config_updates_match_the_reference():
             ours = float((states[0][name].cpu() - ref).abs().max())
             theirs = float((states[1][name].cpu() - ref).abs().max())
             assert ours <= 2.0 * theirs + 1e-6, (model, name, ours, theirs)
+
+
+def _dp_worker(rank: int, world: int, port: int, results) -> None:
+    import torch.distributed as dist
+
+    from card_playing_gym_b200.data_parallel import rescale_batch_weights, shard_games
+    from card_playing_gym_b200.trainer import device_trainer
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    import datetime
+
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        loop, setup, reference_trainer = _reference()
+        config = setup.load_config(REFERENCE / "configs" / "plump" / "smoke.toml")
+        torch.manual_seed(0)
+        np.random.seed(0)
+        random.seed(0)
+        components = setup.build_components(config, device="cpu")
+        game = config.game
+        actor, critic = copy.deepcopy(components.trainer.actor), copy.deepcopy(components.trainer.critic)
+        trajectories = components.collector.collect(game.new_games(random.Random(0), 1))
+        sequences = [game.sequences(t) for t in trajectories]
+
+        def batch_of(items):
+            return loop.build_batch(
+                [t for t, _ in items], [s for _, s in items], max_players=game.max_players,
+                actor_labels=game.actor_labels, critic_labels=game.critic_labels,
+                bucket_width=config.ppo.sequence_bucket_width,
+                critic_bucket_width=config.ppo.critic_sequence_bucket_width, max_length=game.max_length,
+                critic_max_length=game.critic_max_length, min_group_sequences=config.ppo.min_group_sequences)
+
+        pairs = list(zip(trajectories, sequences))
+        starts = np.concatenate([[0], np.cumsum([len(t.decisions) for t in trajectories])])
+        g0, g1 = shard_games(starts, world, rank)
+        shard = batch_of(pairs[g0:g1])
+        rescale_batch_weights(shard, g1 - g0, len(pairs))
+        device = torch.device("cuda", rank)
+        cls = device_trainer(reference_trainer.PPOTrainer)
+        alone = [dist.new_group([r]) for r in range(world)]  # every rank creates every group
+        out = {}
+        if rank == 0:
+            single = _trainer(cls, actor, critic, components, device, process_group=alone[0])
+            out["single"] = single.update(batch_of(pairs), 1)
+            out["single_weights"] = {k: v.cpu() for k, v in single.actor.state_dict().items()}
+        dist.barrier()
+        sharded = _trainer(cls, actor, critic, components, device, process_group=dist.group.WORLD)
+        out["sharded"] = sharded.update(shard, 1)
+        out["sharded_weights"] = {k: v.cpu() for k, v in sharded.actor.state_dict().items()}
+        results.put((rank, out))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_rank_update_matches_one_process():
+    """The same smoke-config batch: one process updating it whole against two NCCL ranks updating halves of its
+    trajectories (global decision weights, per-step gradient SUM-allreduce, global normalisation and totals)."""
+
+    import socket
+
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    results = ctx.Queue()
+    procs = [ctx.Process(target=_dp_worker, args=(r, 2, port, results)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = {}
+    try:
+        for _ in range(2):
+            rank, value = results.get(timeout=600)
+            out[rank] = value
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    single, sharded = out[0]["single"], out[0]["sharded"]
+    same = {k: v for k, v in sharded.items() if k not in NOT_COMPARED}
+    assert {k: v for k, v in out[1]["sharded"].items() if k not in NOT_COMPARED} == same  # the ranks agree
+    for key, value in single.items():
+        if key in NOT_COMPARED or not np.isfinite(value):
+            continue
+        assert _relative(sharded[key], value) < 1e-3 or abs(sharded[key] - value) < 1e-6, (key, sharded[key], value)
+    for name, want in out[0]["single_weights"].items():
+        torch.testing.assert_close(out[0]["sharded_weights"][name], want, rtol=1e-4, atol=2e-6)
+        assert torch.equal(out[0]["sharded_weights"][name], out[1]["sharded_weights"][name])
