@@ -185,15 +185,23 @@ def policy_objective(logits: torch.Tensor, old_probs: torch.Tensor, actions: tor
 
 def ppo_terms(logits: torch.Tensor, old_probs: torch.Tensor, actions: torch.Tensor, advantages: torch.Tensor, *,
               clip_ratio: float) -> PPOTerms:
-    """Masked PPO terms per row (ppo.py:28-72); computed, not differentiable (use policy_objective)."""
+    """Masked PPO terms per row (ppo.py:28-72); computed, not differentiable (use policy_objective).
+
+    The per-row terms come from the fused kernel. ``log_probs`` [N, A] (log pi over the legal actions,
+    0 elsewhere), which only the reference's gated-head entropies read, is torch's masked log_softmax,
+    as the reference computes it.
+    """
 
     rows = logits.shape[0]
     weights = torch.zeros(rows, device=logits.device)
     _, terms, _ = _run_objective(logits.detach(), old_probs, actions, advantages, weights, clip_ratio, 0.0,
                                  want_grad=False, want_terms=True)
+    legal = old_probs > 0
+    masked = logits.detach().float().masked_fill(~legal, float("-inf"))
+    log_probs = torch.where(legal, torch.log_softmax(masked, dim=-1), torch.zeros((), device=logits.device))
     return PPOTerms(
         losses=terms[:, 0], divergences=terms[:, 1], entropy=terms[:, 2], normalized_entropy=terms[:, 3],
-        entropy_eligible=terms[:, 4] > 0, log_probs=None, ratios=terms[:, 5], clipped=terms[:, 6] > 0,
+        entropy_eligible=terms[:, 4] > 0, log_probs=log_probs, ratios=terms[:, 5], clipped=terms[:, 6] > 0,
         action_log_probs=terms[:, 7],
     )
 

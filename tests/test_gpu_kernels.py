@@ -376,6 +376,7 @@ def test_ppo_objective_matches_the_reference_autograd():
         np.testing.assert_allclose(getattr(terms, key).cpu().numpy(), data[key], rtol=1e-5, atol=1e-6, err_msg=key)
     assert np.array_equal(terms.entropy_eligible.cpu().numpy(), data["entropy_eligible"])
     assert np.array_equal(terms.clipped.cpu().numpy(), data["clipped"])
+    np.testing.assert_allclose(terms.log_probs.cpu().numpy(), data["log_probs"], rtol=1e-5, atol=1e-6)
 
 
 def test_value_loss_matches_the_reference_autograd():
