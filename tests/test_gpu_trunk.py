@@ -22,9 +22,19 @@ from tests.conftest import load_golden, trunk_fixture
 pytestmark = pytest.mark.gpu
 
 TRUNKS = ("tiny_div", "tiny_cat", "rlv6")
-# fp32 mode: hidden states are LayerNorm outputs (O(1)); fp32 summation-order noise over
-# 16 layers stays well below this.
-FP32_ATOL = 5e-5
+# fp32 mode against the reference's fp32 outputs, and bf16 mode against the oracle at the kernels'
+# rounding points: max |error| / max |expected| per tensor.
+FP32_TOL = 1e-5
+BF16_TOL = 1e-3
+# The play logits of the rl-v6 fixture's bf16 waves (4 streams, prefill + 40 ragged waves) reach 1.28e-3:
+# besides fp32 summation order, the attention rounds its probabilities to the cache dtype relative to the
+# running maximum of its online softmax, where the reference (and the oracle) round the final softmax.
+# On the benchmarked 4,096-game wave the same logits stay at 7.4e-4 (test_gpu_bench_config.py).
+BF16_FIXTURE_LOGIT_TOL = 1.5e-3
+
+
+def scaled(got, expected) -> float:
+    return float(np.abs(got - expected).max() / max(np.abs(expected).max(), 1e-30))
 
 
 def make_actor(name: str, precision: str):
@@ -58,17 +68,18 @@ def run_waves(actor, data, kv_dtype):
 @pytest.mark.parametrize("name", TRUNKS)
 def test_fp32_ragged_decode_matches_the_reference(name):
     data, _, _, actor = make_actor(name, "fp32")
-    worst = 0.0
+    errors = {"hidden": 0.0, "card": 0.0, "values": 0.0}
     for wave, hidden, live in run_waves(actor, data, torch.float32):
         got = hidden.cpu().numpy()
         expected = data["prefill_hidden"] if wave < 0 else data[f"wave{wave}_hidden"]
-        worst = max(worst, float(np.abs(got[live] - expected[live]).max()))
+        errors["hidden"] = max(errors["hidden"], scaled(got[live], expected[live]))
         if wave >= 0:
             card = actor.policy_logits(hidden, "play").cpu().numpy()
-            np.testing.assert_allclose(card[live], data[f"wave{wave}_card"][live], atol=FP32_ATOL, rtol=1e-5)
+            errors["card"] = max(errors["card"], scaled(card[live], data[f"wave{wave}_card"][live]))
             values = actor.player_values(hidden).cpu().numpy()
-            np.testing.assert_allclose(values[live], data[f"wave{wave}_values"][live], atol=FP32_ATOL, rtol=1e-5)
-    assert worst < FP32_ATOL, worst
+            errors["values"] = max(errors["values"], scaled(values[live], data[f"wave{wave}_values"][live]))
+    print(f"{name} fp32 against the reference: " + ", ".join(f"{k} {v:.2e}" for k, v in errors.items()))
+    assert max(errors.values()) < FP32_TOL, errors
 
 
 @pytest.mark.parametrize("name", TRUNKS)
@@ -89,7 +100,7 @@ def test_fp32_ragged_decode_with_gathered_rows(name):
             cache, torch.from_numpy(data[f"wave{wave}_offsets"]).cuda(), rows=rows,
         )
         live = data[f"wave{wave}_counts"] > 0
-        np.testing.assert_allclose(hidden.cpu().numpy()[live], data[f"wave{wave}_hidden"][live], atol=FP32_ATOL, rtol=0)
+        assert scaled(hidden.cpu().numpy()[live], data[f"wave{wave}_hidden"][live]) < FP32_TOL
 
 
 @pytest.mark.parametrize("name", TRUNKS)
@@ -98,7 +109,7 @@ def test_bf16_ragged_decode_tracks_the_oracle_and_beats_reference_bf16_error(nam
     """bf16 GEMM operands, 16-bit KV.
 
     (1) Against the oracle evaluated at the same rounding points (bf16 GEMM operands,
-    KV/Q/probabilities in the cache dtype): max |error| / max |value| below 1e-2 on
+    KV/Q/probabilities in the cache dtype): max |error| / max |value| below 1e-3 on
     hidden states and play logits (the kernels differ from it only in fp32 summation
     order, which can flip a bf16 rounding).
     (2) Against the reference's fp32 outputs: no worse than twice the reference's own
@@ -121,11 +132,12 @@ def test_bf16_ragged_decode_tracks_the_oracle_and_beats_reference_bf16_error(nam
         expected = oracle.forward_ragged(data[f"wave{wave}_tokens"].astype(np.int64), data[f"wave{wave}_positions"],
                                          ocache, data[f"wave{wave}_offsets"])
         got = hidden.cpu().numpy()
-        scale = np.abs(expected[live]).max()
-        assert np.abs(got[live] - expected[live]).max() / scale < 1e-2
         card = actor.policy_logits(hidden, "play").cpu().numpy()
         ocard = oracle.heads.policy_logits(expected, "play")
-        assert np.abs(card[live] - ocard[live]).max() / np.abs(ocard[live]).max() < 1e-2
+        print(f"{name} bf16/{kv} wave {wave}: hidden {scaled(got[live], expected[live]):.2e}, "
+              f"play {scaled(card[live], ocard[live]):.2e}")
+        assert scaled(got[live], expected[live]) < BF16_TOL
+        assert scaled(card[live], ocard[live]) < BF16_FIXTURE_LOGIT_TOL
         reference = data[f"wave{wave}_card"][live]
         mine_err = max(mine_err, float(np.abs(card[live] - reference).max()))
         ref_err = max(ref_err, float(np.abs(data[f"wave{wave}_bf16_card"][live] - reference).max()))
@@ -205,7 +217,7 @@ def test_trunk_forward_ragged_from_conditioned_inputs(precision, kv):
     expected = oracle.trunk.forward_ragged(x[:, prefix:], ple[:, prefix:], values[:, prefix:], ocache, positions,
                                            offsets)
     error = np.abs(hidden.cpu().numpy() - expected).max() / np.abs(expected).max()
-    assert error < (FP32_ATOL if precision == "fp32" else 1e-2), error
+    assert error < (FP32_TOL if precision == "fp32" else BF16_TOL), error
 
 
 def test_wide_trunk_bf16_decode_tracks_the_oracle():
@@ -227,11 +239,11 @@ def test_wide_trunk_bf16_decode_tracks_the_oracle():
     tokens = torch.from_numpy(streams).cuda()
     got = actor.forward_prefill(tokens[:, :prefix], cache, None).cpu().numpy()
     expected = oracle.forward_prefill(streams[:, :prefix], ocache, None)
-    assert np.abs(got - expected).max() / np.abs(expected).max() < 1e-2
+    assert scaled(got, expected) < BF16_TOL
     for step in range(prefix, min(length, prefix + 3)):
         positions = np.full(batch, step, np.int64)
         offsets = np.zeros(batch, np.int64)
         got = actor.forward_ragged(tokens[:, step:step + 1], torch.from_numpy(positions).cuda(), cache,
                                    torch.from_numpy(offsets).cuda()).cpu().numpy()
         expected = oracle.forward_ragged(streams[:, step:step + 1], positions, ocache, offsets)
-        assert np.abs(got - expected).max() / np.abs(expected).max() < 1e-2, step
+        assert scaled(got, expected) < BF16_TOL, step

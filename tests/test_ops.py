@@ -91,6 +91,9 @@ def test_ops_match_the_direct_wrappers():
     want = actor.decide(hidden, heads, legal, draws)
     assert all(torch.equal(a, b) for a, b in zip(out, want))
 
+    # The trunk op on its own inputs (Trunk.condition's outputs): the fp32 trunk conditions separately; the bf16
+    # trunk folds the conditioning into its first fused layer and takes raw lookups only inside forward_ragged.
+    actor = PlumpActor(config, synthetic_plump_actor_state(config, seed=2), precision="fp32")
     tokens = torch.from_numpy(np.load("tests/golden/plump_streams.npz")["tokens"][:8, :3].astype(np.int64)).cuda()
     x, ple, values_in = actor.prepare(tokens)
     caches = [actor.new_cache(8, 8, torch.float16) for _ in range(2)]
@@ -98,7 +101,7 @@ def test_ops_match_the_direct_wrappers():
     offsets = torch.full((8,), 2, dtype=torch.int64, device="cuda")
     workspace = torch.empty(actor.trunk.step_workspace_bytes(8, 3), dtype=torch.uint8, device="cuda")
     got = OPS.trunk_forward_ragged(ops.trunk_dims_list(actor.trunk.dims), actor.trunk.blob, x, ple, values_in,
-                                   caches[0].k_pool, caches[0].v_pool, positions, offsets, None, 3, 1, workspace)
+                                   caches[0].k_pool, caches[0].v_pool, positions, offsets, None, 3, 0, workspace)
     want = actor.trunk.forward_ragged(x, ple, values_in, caches[1], positions, offsets, span=3)
     assert torch.equal(got, want)
     assert torch.equal(caches[0].k_pool, caches[1].k_pool) and torch.equal(caches[0].v_pool, caches[1].v_pool)
