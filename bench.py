@@ -225,10 +225,29 @@ def run_ppo(args, device, rank: int, world_size: int) -> dict:
     end.record(stream)
     torch.cuda.synchronize(device)
     ms = start.elapsed_time(end) / args.ppo_steps
+    kernels_ms = allreduce_ms = None
     if world_size > 1:
-        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        # The same steps split in their two parts: this rank's kernels alone, then the gradient
+        # allreduce alone (the one collective whose cost grows with the ranks).
+        dist.barrier()
+        torch.cuda.synchronize(device)
+        start.record(stream)
+        for _ in range(args.ppo_steps):
+            local_step()
+        end.record(stream)
+        torch.cuda.synchronize(device)
+        kernels_ms = start.elapsed_time(end) / args.ppo_steps
+        dist.barrier()
+        torch.cuda.synchronize(device)
+        start.record(stream)
+        for _ in range(args.ppo_steps):
+            dist.all_reduce(gradient)
+        end.record(stream)
+        torch.cuda.synchronize(device)
+        allreduce_ms = start.elapsed_time(end) / args.ppo_steps
+        t = torch.tensor([ms, kernels_ms, allreduce_ms], device=device, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        ms, kernels_ms, allreduce_ms = (float(v) for v in t.tolist())
     n, g, a, pl = d1 - d0, g1 - g0, PPO_ACTIONS, PPO_PLAYERS
     # Bytes the kernels must move on this rank: GAE, two normalisation passes + the in-place
     # normalise, the fused objective (logits, old probs, actions, advantages, weights in; dlogits
@@ -250,6 +269,9 @@ def run_ppo(args, device, rank: int, world_size: int) -> dict:
         "includes": "GAE, global two-pass mean/std and normalise on the device (no host read), fused PPO "
                     "objective fwd+grad, value loss fwd+grad, autograd backward",
         "launch": "one CUDA graph replay per step (ppo.GraphedStep)" if world_size == 1 else "eager launches",
+        "kernels_ms_per_step": kernels_ms, "gradient_allreduce_ms_per_step": allreduce_ms,
+        "gradient_allreduce_bus_gbs": (None if allreduce_ms is None else
+                                   TRUNK_PARAMS * 4 * 2 * (world_size - 1) / world_size / (allreduce_ms / 1000.0) / 1e9),
     }
 
 
