@@ -427,3 +427,47 @@ def test_stack_features_pads_the_candidate_axis_with_zeros():
     assert stacked["kind"].tolist() == [[3, 1, 0], [5, 6, 2]]
     assert stacked["cards"].shape == (2, 3, 13) and not stacked["cards"][0, 2].any()
     assert np.array_equal(stacked["cards"][1], b["cards"]) and stacked["cards"].dtype == b["cards"].dtype
+
+
+@pytest.mark.gpu
+def test_continuous_collector_probabilities_match_the_oracle():
+    """Every decision the continuous collector records for a plump actor (graphed waves, context restarts, slot
+    refills), against the CPU oracle (numpy float64): the oracle prefills the decision's context and scores
+    the head; the reference's numpy sampler turns its logits into probabilities and a draw. fp32, fp32 KV."""
+
+    import dataclasses
+
+    from card_playing_gym_b200.config import RL_V6, synthetic_plump_actor_state
+    from card_playing_gym_b200.plump import PlumpActor
+    from oracle import plump as oplump
+    from oracle.trunk import Precision
+
+    config = dataclasses.replace(RL_V6, n_layers=2)
+    state = synthetic_plump_actor_state(config, seed=6)
+    actor = PlumpActor(config, state, precision="fp32")
+    oracle = oplump.PlumpActor(state, {k: getattr(config, k) for k in (
+        "d_model", "n_layers", "n_heads", "n_kv_heads", "d_ff", "per_layer_dim", "value_embeddings", "max_players",
+        "max_hand_size")}, Precision())
+    pool = _pool()
+
+    def deal(rng):
+        seed = rng.randrange(1 << 30)
+        return ScriptedGame(seed, pool, restart=2 if seed % 2 else None)
+
+    collector = cont.ContinuousCollector(actor, max_length=48, cohorts=2, kv_dtype="fp32", record_values=True)
+    results = collector.collect([cont.Lane("plump", 4, 8, 12, deal=deal)], random.Random(41))
+    checked = 0
+    for trajectory in results:
+        game = trajectory.game
+        replay = random.Random(game.seed ^ 0x5EED)
+        for record, (seat, head, legal, base, length) in zip(trajectory.decisions, game.log):
+            context = trajectory.streams[seat][base:length].astype(np.int64)[None]
+            hidden = oracle.forward_prefill(context, oracle.new_cache(1, context.shape[1] + 1), None)
+            probs = oppo.masked_probabilities(oracle.heads.policy_logits(hidden, head).astype(np.float32), legal[None])
+            np.testing.assert_allclose(record.probs, probs[0], rtol=1e-5, atol=1e-7)
+            np.testing.assert_allclose(record.value, oracle.heads.player_values(hidden)[0], rtol=1e-5, atol=2e-6)
+            u = replay.random()
+            near = np.abs(np.cumsum(probs[0]).astype(np.float64) - u).min() < 1e-5
+            assert record.action == oppo.sample_rows(probs, legal[None], np.array([u]))[0] or near
+            checked += 1
+    assert checked > 20
