@@ -200,16 +200,43 @@ def run_ppo(args, device, rank: int, world_size: int) -> dict:
         (objective + loss).backward()
         return leaf.grad, pred.grad
 
-    # One GPU: the whole step replays as one CUDA graph. Several: the step's collectives (the
-    # normalisation's sums and the gradient allreduce) run eagerly with it.
+    # One GPU: the whole step replays as one CUDA graph. Several: the step's kernels replay as three
+    # graphs, and its collectives run between them (no collective is captured): GAE and the first
+    # pass's sums | allreduce | the second pass's sums | allreduce | normalise, objective, value
+    # loss, backward | the gradient allreduce.
     graphed = ppo.GraphedStep(local_step) if world_size == 1 else None
+    if world_size > 1:
+        first_graph = ppo.GraphedStep(lambda: (lambda a: (a, ppo.weighted_sums(a, weights64, 0.0)))(
+            ppo.segmented_gae(values, seats, starts, returns, 0.95)))
+        held: dict = {}
+
+        def second_pass():
+            advantages, first = first_graph.outputs
+            return ppo.weighted_sums_shifted(advantages, weights64, first)
+
+        def finish():
+            advantages, first = first_graph.outputs
+            ppo.normalize_from_sums_(advantages, first, held["second"].outputs)
+            leaf = logits.detach().requires_grad_()
+            objective, _ = ppo.policy_objective(leaf, old_probs, actions, advantages, weights, clip_ratio=0.2,
+                                                alpha=0.01)
+            pred = prediction.detach().requires_grad_()
+            loss, _ = ppo.value_loss(pred, players, targets, weights, 1.0)
+            (objective + loss).backward()
+            return leaf.grad, pred.grad
+
+        held["second"] = ppo.GraphedStep(second_pass)
+        finish_graph = ppo.GraphedStep(finish)
 
     def step():
         if graphed is not None:
             return graphed()
-        grads = local_step()
-        if gradient is not None:
-            dist.all_reduce(gradient)
+        _, first = first_graph()
+        dist.all_reduce(first)
+        second = held["second"]()
+        dist.all_reduce(second)
+        grads = finish_graph()
+        dist.all_reduce(gradient)
         return grads
 
     for _ in range(3):
@@ -233,7 +260,9 @@ def run_ppo(args, device, rank: int, world_size: int) -> dict:
         torch.cuda.synchronize(device)
         start.record(stream)
         for _ in range(args.ppo_steps):
-            local_step()
+            first_graph()
+            held["second"]()
+            finish_graph()
         end.record(stream)
         torch.cuda.synchronize(device)
         kernels_ms = start.elapsed_time(end) / args.ppo_steps
@@ -268,7 +297,8 @@ def run_ppo(args, device, rank: int, world_size: int) -> dict:
                         "allreduce (NCCL) per step"),
         "includes": "GAE, global two-pass mean/std and normalise on the device (no host read), fused PPO "
                     "objective fwd+grad, value loss fwd+grad, autograd backward",
-        "launch": "one CUDA graph replay per step (ppo.GraphedStep)" if world_size == 1 else "eager launches",
+        "launch": ("one CUDA graph replay per step (ppo.GraphedStep)" if world_size == 1 else
+                   "three CUDA graph replays per step with the collectives between them"),
         "kernels_ms_per_step": kernels_ms, "gradient_allreduce_ms_per_step": allreduce_ms,
         "gradient_allreduce_bus_gbs": (None if allreduce_ms is None else
                                    TRUNK_PARAMS * 4 * 2 * (world_size - 1) / world_size / (allreduce_ms / 1000.0) / 1e9),
