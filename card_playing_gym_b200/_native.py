@@ -226,9 +226,16 @@ def stream_handle(device: torch.device | None = None) -> int:
 
 
 class Workspace:
-    """A grow-only device scratch buffer per (device, purpose)."""
+    """A grow-only device scratch buffer per (device, purpose).
+
+    A buffer that a larger one replaces is kept alive, not freed: a CUDA graph captured while it
+    was current holds its address, and the next capture's ``empty_cache`` would otherwise return
+    it to the driver, so that graph's replay would touch freed memory. Growth is geometric, so
+    the retired buffers add up to less than the current one.
+    """
 
     _buffers: dict[tuple[int, str], torch.Tensor] = {}
+    _retired: list[torch.Tensor] = []
 
     @classmethod
     def get(cls, device: torch.device, nbytes: int, purpose: str = "step") -> torch.Tensor:
@@ -236,6 +243,10 @@ class Workspace:
         key = (index, purpose)
         buffer = cls._buffers.get(key)
         if buffer is None or buffer.numel() < nbytes:
-            buffer = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+            size = max(int(nbytes), 256)
+            if buffer is not None:
+                cls._retired.append(buffer)
+                size = max(size, 2 * buffer.numel())
+            buffer = torch.empty(size, dtype=torch.uint8, device=device)
             cls._buffers[key] = buffer
         return buffer

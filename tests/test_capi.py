@@ -73,3 +73,16 @@ def test_cpu_tensors_are_refused():
     k = torch.zeros(2, 2, 8, 24)
     with pytest.raises(ValueError, match="CUDA"):
         decode_attention(q, k, k, torch.zeros(2, dtype=torch.int64), torch.ones(2, dtype=torch.int64), 8, 0.2)
+
+
+def test_a_replaced_workspace_stays_alive():
+    """A captured graph keeps the address of the workspace it ran with; growing the workspace must not free it."""
+
+    device = torch.device("cpu", 0)
+    small = nat.Workspace.get(device, 1000, "test-retire")
+    address = small.data_ptr()
+    del small
+    large = nat.Workspace.get(device, 5000, "test-retire")
+    assert large.numel() >= 5000 and large.data_ptr() != address
+    assert any(t.data_ptr() == address for t in nat.Workspace._retired)
+    assert nat.Workspace.get(device, 4000, "test-retire").data_ptr() == large.data_ptr()
