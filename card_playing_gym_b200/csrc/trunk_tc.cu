@@ -110,10 +110,20 @@ __device__ __forceinline__ void load16(const float* base, int64_t tile, int widt
   }
 }
 
-__device__ __forceinline__ void store16(float* base, int64_t tile, int width, int col, int t, const float (&v)[16]) {
+// The residual row, stored with an L2 evict-last policy: the next layer's kernel reads it back after
+// the attention kernel between them has streamed the KV pool (evict-first) through L2.
+__device__ __forceinline__ void store16_keep(float* base, int64_t tile, int width, int col, int t, const float (&v)[16],
+                                             uint64_t policy) {
 #pragma unroll
   for (int q = 0; q < 4; ++q)
-    *blk(base, tile, width, col + 4 * q, t) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    asm volatile("st.global.L2::cache_hint.v4.f32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(blk(base, tile, width, col + 4 * q, t)),
+                 "f"(v[4 * q]), "f"(v[4 * q + 1]), "f"(v[4 * q + 2]), "f"(v[4 * q + 3]), "l"(policy)
+                 : "memory");
+}
+
+// Bring `bytes` (a multiple of 16, 16-byte aligned) of global memory into L2 ahead of their use.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
 // 16 consecutive floats from a 16-byte aligned parameter vector (staged in shared memory).
@@ -359,6 +369,17 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
       prm[i] = src ? src[k] : 0.f;
     }
   }
+  if (threadIdx.x == 0 && p.mode == kLayer) {
+    // Written by the wave's first kernel, long complete: this layer's PLE tile and the next
+    // QKV's value-embedding tile, read late in this kernel.
+    if (p.P)
+      prefetch_l2(blk(p.ple_blk, static_cast<int64_t>(p.layer) * p.ntiles + blockIdx.x, p.P, 0, 0),
+                  static_cast<uint32_t>(kTile * p.P * 4));
+    if (p.has_next && p.value_index >= 0)
+      prefetch_l2(reinterpret_cast<const float4*>(p.val_blk) +
+                      (static_cast<int64_t>(p.value_index) * p.ntiles + blockIdx.x) * (p.kvw / 4) * kTile,
+                  static_cast<uint32_t>(kTile * p.kvw * 4));
+  }
   pdl_wait();  // the epilogue reads and writes what earlier kernels of the stream touch
   pdl_trigger();
   EpiThread e;
@@ -488,6 +509,7 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
     }
     if (!wait_acc()) return;
     // Every GEMM that reads H has completed: H takes the next layer's value-embedding tile.
+    const uint64_t keep_x = tc::make_policy_evict_last();
     const int vbytes = kTile * p.kvw * 4;
     const bool val_smem = p.has_next && p.value_index >= 0 && vbytes <= p.hbytes;
     if (val_smem && threadIdx.x == 0) {
@@ -503,7 +525,7 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
       tc::tmem_ld16(e.lane_tmem + col, v16);
 #pragma unroll
       for (int i = 0; i < 16; ++i) x[c][i] += v16[i];
-      if (p.has_next) store16(p.x_blk, tile, d, col, t, x[c]);
+      if (p.has_next) store16_keep(p.x_blk, tile, d, col, t, x[c], keep_x);
     }
     if (p.has_next) {
       layer_norm_regs(x, lo, hi, d, e, prm + 3 * d, prm + 4 * d, abuf, red);
@@ -548,7 +570,7 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
       load16_vec(prm + col, gain);
 #pragma unroll
       for (int i = 0; i < 16; ++i) x[c][i] = x[c][i] * inv * gain[i];
-      store16(p.x_blk, tile, d, col, t, x[c]);
+      store16_keep(p.x_blk, tile, d, col, t, x[c], tc::make_policy_evict_last());
       store_operand16(abuf, col, t, x[c]);
     }
     layer_norm_regs(x, lo, hi, d, e, prm + 3 * d, prm + 4 * d, h0, red);
@@ -612,7 +634,7 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
       const int col = (lo + c) * 16;
 #pragma unroll
       for (int i = 0; i < 16; ++i) x[c][i] = p.x_in[r * d + col + i];
-      store16(p.x_blk, tile, d, col, t, x[c]);
+      store16_keep(p.x_blk, tile, d, col, t, x[c], tc::make_policy_evict_last());
     }
     for (int k = e.qd * 4; k < ple_w; k += 4 * kParts) {
       const float4 ev = *reinterpret_cast<const float4*>(p.ple_in + r * ple_w + k);
