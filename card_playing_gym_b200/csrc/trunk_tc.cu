@@ -791,18 +791,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dense_kernel(const __grid_co
           if (kPair && !(ok = tc::bar_wait_cluster(&peer_full[stage], lap & 1u, 0x40a))) break;
           tc::fence_after_sync();
           const int end = min(op.ksteps, s0 + op.ks_per_stage);
+          // One thread issues every MMA while the epilogue warps keep the SM's issue slots busy, so
+          // the loop is kept to the MMA itself: both descriptors are built once per stage and
+          // stepped by a K-slice (the 14-bit address field, in 16-byte units, never carries: shared
+          // memory addresses stay below 2^18).
+          uint64_t a_desc = tc::smem_desc(a_addr + 2 * s0 * (kTile * 16), kTile * 16, 128);
+          uint64_t b_desc = tc::smem_desc(ring_addr + stage * p.stage_bytes, 128, 256);
+          constexpr uint64_t a_step = (2 * kTile * 16) >> 4;
+          const uint64_t b_step = slice >> 4;
+          const uint32_t d_tmem = tmem + op.tmem_col;
           for (int s = s0; s < end; ++s) {
-            const uint64_t a_desc = tc::smem_desc(a_addr + 2 * s * (kTile * 16), kTile * 16, 128);
-            const uint32_t b_addr = ring_addr + stage * p.stage_bytes + (s - s0) * slice;
             const uint32_t acc = (s > 0 || op.accumulate_first) ? 1u : 0u;
             if (kPair) {
-              tc::mma_bf16_pair(tmem + op.tmem_col, a_desc, tc::smem_desc(b_addr, 128, 256), idesc, acc);
+              tc::mma_bf16_pair(d_tmem, a_desc, b_desc, idesc, acc);
             } else {
-              tc::mma_bf16(tmem + op.tmem_col, a_desc, tc::smem_desc(b_addr, 128, 256), idesc, acc);
-              if (op.n > 256)
-                tc::mma_bf16(tmem + op.tmem_col + 256, a_desc, tc::smem_desc(b_addr + 32 * 256, 128, 256),
-                             idesc_rest, acc);
+              tc::mma_bf16(d_tmem, a_desc, b_desc, idesc, acc);
+              if (op.n > 256) tc::mma_bf16(d_tmem + 256, a_desc, b_desc + ((32 * 256) >> 4), idesc_rest, acc);
             }
+            a_desc += a_step;
+            b_desc += b_step;
           }
           commit(&empty[stage]);
           if (++stage == stages) {
