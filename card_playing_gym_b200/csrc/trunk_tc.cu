@@ -173,6 +173,34 @@ __device__ __forceinline__ float gelu_bf16_operand(float x) {
   return x * (x >= 0.f ? 1.f - c : c);
 }
 
+// The same GELU on two values at once: the additions, multiplications and fused multiply-adds run
+// as packed fp32x2 operations (each lane rounded as its scalar counterpart), the reciprocal and
+// the exponential per value, so each lane's result is bit-identical to gelu_bf16_operand's.
+// Returns the pair packed as bf16 (x.x in the low half).
+__device__ __forceinline__ uint32_t gelu_bf16_pair(float2 x) {
+  const float2 z = __fmul2_rn(make_float2(fabsf(x.x), fabsf(x.y)), make_float2(0.70710678118654752f, 0.70710678118654752f));
+  const float2 den = __ffma2_rn(make_float2(0.3275911f, 0.3275911f), z, make_float2(1.f, 1.f));
+  float2 t;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t.x) : "f"(den.x));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t.y) : "f"(den.y));
+  float2 q = __ffma2_rn(t, make_float2(0.5f * 1.061405429f, 0.5f * 1.061405429f),
+                        make_float2(0.5f * -1.453152027f, 0.5f * -1.453152027f));
+  q = __ffma2_rn(q, t, make_float2(0.5f * 1.421413741f, 0.5f * 1.421413741f));
+  q = __ffma2_rn(q, t, make_float2(0.5f * -0.284496736f, 0.5f * -0.284496736f));
+  q = __ffma2_rn(q, t, make_float2(0.5f * 0.254829592f, 0.5f * 0.254829592f));
+  // (-z * z) * log2(e) = -((z * z) * log2(e)): negation is exact, so the rounding is the scalar form's
+  const float2 arg = __fmul2_rn(__fmul2_rn(z, z), make_float2(-1.4426950408889634f, -1.4426950408889634f));
+  float2 e;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.x) : "f"(arg.x));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.y) : "f"(arg.y));
+  const float2 c = __fmul2_rn(__fmul2_rn(q, t), e);
+  const float2 one_minus = __ffma2_rn(c, make_float2(-1.f, -1.f), make_float2(1.f, 1.f));  // rn(1 - c)
+  const float2 phi = make_float2(x.x >= 0.f ? one_minus.x : c.x, x.y >= 0.f ? one_minus.y : c.y);
+  const float2 g = __fmul2_rn(x, phi);
+  __nv_bfloat162 pair = __floats2bfloat162_rn(g.x, g.y);
+  return *reinterpret_cast<uint32_t*>(&pair);
+}
+
 // ---- epilogue geometry ---------------------------------------------------------------------------------
 // 12 epilogue warps; thread e belongs to warp w = e / 32. Warp w may only touch TMEM lanes
 // 32 * (w % 4) .. + 31, so row t = 32 * (w % 4) + lane, and the three warps with the same w % 4
@@ -476,10 +504,16 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           if (h == 1 && !two) break;
-          float g[16];
+          uint32_t words[8];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) g[i] = gelu_bf16_operand(v[16 * h + i] + bias[h][i]);
-          store_operand16(hb, (c + h) * 16, t, g);
+          for (int i = 0; i < 8; ++i)
+            words[i] = gelu_bf16_pair(__fadd2_rn(make_float2(v[16 * h + 2 * i], v[16 * h + 2 * i + 1]),
+                                                 make_float2(bias[h][2 * i], bias[h][2 * i + 1])));
+          const int col = (c + h) * 16;
+#pragma unroll
+          for (int q = 0; q < 2; ++q)
+            *reinterpret_cast<uint4*>(hb + (col / 8 + q) * (kTile * 16) + t * 16) =
+                make_uint4(words[4 * q], words[4 * q + 1], words[4 * q + 2], words[4 * q + 3]);
         }
       }
       publish();
