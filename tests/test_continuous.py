@@ -455,7 +455,8 @@ def test_continuous_collector_probabilities_match_the_oracle():
         return ScriptedGame(seed, pool, restart=2 if seed % 2 else None)
 
     collector = cont.ContinuousCollector(actor, max_length=48, cohorts=2, kv_dtype="fp32", record_values=True)
-    results = collector.collect([cont.Lane("plump", 4, 8, 12, deal=deal)], random.Random(41))
+    # The first 24 games to finish (short ones come first): enough decisions of both heads to check.
+    results = collector.collect([cont.Lane("plump", 4, 8, 24, deal=deal)], random.Random(41))
     checked = 0
     for trajectory in results:
         game = trajectory.game
