@@ -159,24 +159,10 @@ __device__ __forceinline__ void store_operand16(unsigned char* buf, int col, int
 // The GELU's absolute error stays below 5e-7, far inside the bf16 rounding of its output (the
 // down-projection operand); Phi(x) = 1 - 0.5 erfc(z) for x >= 0 and 0.5 erfc(z) below, so the
 // negative tail keeps its relative accuracy instead of cancelling.
-__device__ __forceinline__ float gelu_bf16_operand(float x) {
-  const float z = fabsf(x) * 0.70710678118654752f;
-  float t;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(fmaf(0.3275911f, z, 1.f)));
-  float q = fmaf(t, 0.5f * 1.061405429f, 0.5f * -1.453152027f);  // the 0.5 of 0.5 erfc folded in
-  q = fmaf(q, t, 0.5f * 1.421413741f);
-  q = fmaf(q, t, 0.5f * -0.284496736f);
-  q = fmaf(q, t, 0.5f * 0.254829592f);
-  float e;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-z * z * 1.4426950408889634f));
-  const float c = q * t * e;  // 0.5 erfc(z) = Phi(-|x|)
-  return x * (x >= 0.f ? 1.f - c : c);
-}
-
-// The same GELU on two values at once: the additions, multiplications and fused multiply-adds run
-// as packed fp32x2 operations (each lane rounded as its scalar counterpart), the reciprocal and
-// the exponential per value, so each lane's result is bit-identical to gelu_bf16_operand's.
-// Returns the pair packed as bf16 (x.x in the low half).
+// Computed on two values at once: the additions, multiplications and fused multiply-adds run as
+// Blackwell's packed fp32x2 operations (each lane rounded exactly as the scalar operation), the
+// reciprocal and the exponential per value (MUFU). Returns the pair packed as bf16 (x.x in the
+// low half), the down projection's operand.
 __device__ __forceinline__ uint32_t gelu_bf16_pair(float2 x) {
   const float2 z = __fmul2_rn(make_float2(fabsf(x.x), fabsf(x.y)), make_float2(0.70710678118654752f, 0.70710678118654752f));
   const float2 den = __ffma2_rn(make_float2(0.3275911f, 0.3275911f), z, make_float2(1.f, 1.f));
