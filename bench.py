@@ -76,6 +76,8 @@ def parse_args(argv=None):
                         help="waves of the rl-v6 T = 2 leg (two tokens appended per row); 0 skips it")
     parser.add_argument("--pointer-steps", type=int, default=20,
                         help="waves of the piquet and rummy-style pointer-head legs; 0 skips them")
+    parser.add_argument("--pointer-divisor", type=int, default=1,
+                        help="divide the pointer legs' slots and decoded rows (a small case for profilers)")
     parser.add_argument("--prefill-steps", type=int, default=10,
                         help="prefills of the rl-v6 new-game leg (every row's prefix from position 0); 0 skips it")
     parser.add_argument("--prefill-tokens", type=int, default=16, help="prefix tokens per row in the prefill leg")
@@ -533,6 +535,8 @@ def run_pointer_wave(args, device, rank: int, world_size: int, kind: str) -> dic
         actor = rummy.RummyActor(config, rummy.synthetic_rummy_actor_state(config, seed=5), device=device)
         vocab, card_codes, card_slots = rummy.FIELD_VOCAB, rummy.CARD_VOCAB, 52
         slots, decoded, min_len, max_len = 8192, 4096, 8, 384
+    divisor = max(1, args.pointer_divisor)
+    slots, decoded = max(2, slots // divisor // 2 * 2), max(2, decoded // divisor // 2 * 2)
     cache = actor.new_cache(slots + 1, max_len + 1, torch.float16)
     for pool in (cache.k_pool, cache.v_pool):
         for layer in range(pool.shape[0]):
@@ -1204,7 +1208,10 @@ def run_b200(args) -> int:
     del e2e_graph
     e2e_value = world_size * games * args.steps / (e2e_ms / 1000.0)
     e2e_eager_value = world_size * games * args.steps / (e2e_eager_ms / 1000.0)
-    ppo_line = run_ppo(args, device, rank, world_size) if args.ppo_decisions > 0 else None
+    ppo_line = None
+    if args.ppo_decisions > 0:
+        with torch.cuda.nvtx.range("ppo"):  # lets a profiler select this leg's launches
+            ppo_line = run_ppo(args, device, rank, world_size)
     piquet_line = run_piquet_scale(args, device, rank, world_size) if args.piquet_steps > 0 else None
     pointer_lines = {}
     if args.t2_steps > 0:
