@@ -1136,7 +1136,17 @@ def run_b200(args) -> int:
     dense_ms = nat.dense_timings()
     nat.attention_profiling(False)
     nat.dense_profiling(False)
+    # nvidia-smi needs a few hundred ms to start and samples every 100 ms: when the timed steps
+    # are shorter than that, every rank keeps running the same wave (untimed) until ~0.6 s of
+    # load have passed since sampling began, so the clocks and throttle reasons are read under load.
+    extra = max(0, int(600.0 / max(device_ms / args.steps, 1e-3)) - args.steps - profiled_steps)
+    for _ in range(extra):
+        step()
+    torch.cuda.synchronize(device)
+    barrier()
     clock_info = clocks.stop() if clocks else None
+    if clock_info is not None and extra:
+        clock_info["sampled_over"] = f"the timed steps and {extra} more untimed waves of the same workload"
     device_ms = max_over_ranks(device_ms)
     ms_per_step = device_ms / args.steps
     value = world_size * games * args.steps / (device_ms / 1000.0)
