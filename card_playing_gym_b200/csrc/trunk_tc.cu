@@ -443,12 +443,14 @@ __device__ void dense_epilogue(const TcParams& p, unsigned char* abuf, unsigned 
     // The residual row goes into the accumulator columns of TMEM: the out-projection and
     // every down-projection accumulate onto it, so x += out and x += down need no epilogue
     // and the row never leaves TMEM inside the layer.
+    // Every chunk's loads first, then the stores: a tensor-memory store is a compiler barrier, so
+    // interleaving them would make the chunks' global loads one round trip each.
 #pragma unroll
     for (int c = 0; c < kRC; ++c)
-      if (lo + c < hi) {
-        load16(p.x_blk, tile, d, (lo + c) * 16, t, x[c]);
-        tc::tmem_st16(e.lane_tmem + (lo + c) * 16, x[c]);
-      }
+      if (lo + c < hi) load16(p.x_blk, tile, d, (lo + c) * 16, t, x[c]);
+#pragma unroll
+    for (int c = 0; c < kRC; ++c)
+      if (lo + c < hi) tc::tmem_st16(e.lane_tmem + (lo + c) * 16, x[c]);
     tc::tmem_wait_st();
     if (!group_wait(attn_full_bar, 0, 0x404)) return;
     publish();
